@@ -1,0 +1,273 @@
+// flashattn_cuda._C — the PyTorch-facing operator layer over the C ABI in
+// include/fa_b200.h. It keeps the reference's pybind surface (csrc/bindings.cpp
+// in shrvan30/flash-attention-cuda): the same function names, argument names,
+// validation order and error messages, so existing callers and tests see the
+// same behaviour. Torch appears only here: tensors are checked, outputs are
+// allocated from the caching allocator, and raw pointers plus the current
+// stream go to the C ABI.
+
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <cmath>
+#include <mutex>
+#include <unordered_map>
+
+#include "fa_b200.h"
+
+namespace {
+
+constexpr int kHeadDim = FA_HEAD_DIM;
+
+// Message texts follow the reference's checks (csrc/flash_common.h:43-62) so
+// callers matching on them keep working.
+void check_cuda(const at::Tensor &t, const char *name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+}
+void check_half(const at::Tensor &t, const char *name) {
+  TORCH_CHECK(t.scalar_type() == at::kHalf, name, " must be fp16 (got ",
+              t.scalar_type(), ")");
+}
+void check_contiguous(const at::Tensor &t, const char *name) {
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous row-major");
+}
+// (B, H, N, 64) fp16 CUDA tensor.
+void check_bhnd(const at::Tensor &t, const char *name) {
+  check_cuda(t, name);
+  check_half(t, name);
+  check_contiguous(t, name);
+  TORCH_CHECK(t.dim() == 4, name, " must be 4-D (B, H, N, ", kHeadDim,
+              "), got ", t.dim(), "-D");
+  TORCH_CHECK(t.size(3) == kHeadDim, name, " must have head_dim == ",
+              kHeadDim, ", got ", t.size(3));
+}
+
+void check_status(int rc, const char *what) {
+  TORCH_CHECK(rc == FA_OK, what, " failed: ", fa_status_string(rc));
+}
+
+int to_int(int64_t v, const char *what) {
+  TORCH_CHECK(v >= 0 && v <= INT32_MAX, what, " out of range: ", v);
+  return static_cast<int>(v);
+}
+
+void *current_stream() {
+  return static_cast<void *>(at::cuda::getCurrentCUDAStream().stream());
+}
+
+// Decode scratch, cached per (device, stream). fa_decode leaves its arrival
+// counters at zero after every call, so a buffer is zero-filled only when it
+// is (re)allocated; keying by stream keeps concurrent streams apart. The map
+// is intentionally never destroyed (no CUDA frees during interpreter exit).
+at::Tensor decode_workspace(const at::Tensor &like, size_t bytes) {
+  static std::mutex mu;
+  static auto *cache = new std::unordered_map<uint64_t, at::Tensor>();
+  const auto stream = at::cuda::getCurrentCUDAStream();
+  const uint64_t key = (static_cast<uint64_t>(like.get_device()) << 56) ^
+                       static_cast<uint64_t>(stream.id());
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache->find(key);
+  if (it != cache->end() && static_cast<size_t>(it->second.numel()) >= bytes)
+    return it->second;
+  at::Tensor ws = at::zeros({static_cast<int64_t>(bytes)},
+                            like.options().dtype(at::kByte));
+  (*cache)[key] = ws;
+  return ws;
+}
+
+void check_decode_inputs(const at::Tensor &q, const at::Tensor &k_cache,
+                         const at::Tensor &v_cache, const at::Tensor &seq_lens,
+                         double scale) {
+  check_bhnd(q, "q");
+  check_bhnd(k_cache, "k_cache");
+  check_bhnd(v_cache, "v_cache");
+  TORCH_CHECK(q.size(2) == 1, "decode expects exactly one query row, got ",
+              q.size(2));
+  TORCH_CHECK(k_cache.sizes() == v_cache.sizes(),
+              "k_cache and v_cache must have identical shapes, got ",
+              k_cache.sizes(), " and ", v_cache.sizes());
+  TORCH_CHECK(q.size(0) == k_cache.size(0) && q.size(1) == k_cache.size(1),
+              "q and the caches must agree on batch and head count, got q=",
+              q.sizes(), " cache=", k_cache.sizes());
+  TORCH_CHECK(k_cache.size(2) > 0, "cache length must be > 0");
+  check_cuda(seq_lens, "seq_lens");
+  check_contiguous(seq_lens, "seq_lens");
+  TORCH_CHECK(seq_lens.scalar_type() == at::kInt,
+              "seq_lens must be int32 (got ", seq_lens.scalar_type(), ")");
+  TORCH_CHECK(seq_lens.dim() == 1 && seq_lens.size(0) == q.size(0),
+              "seq_lens must be 1-D of length B=", q.size(0), ", got ",
+              seq_lens.sizes());
+  TORCH_CHECK(q.device() == k_cache.device() &&
+                  q.device() == v_cache.device() &&
+                  q.device() == seq_lens.device(),
+              "q, caches and seq_lens must live on the same device");
+  TORCH_CHECK(std::isfinite(scale), "scale must be finite");
+}
+
+}  // namespace
+
+// prefill(q, k, v, causal, scale): reference csrc/bindings.cpp:10-27.
+at::Tensor prefill(const at::Tensor &q, const at::Tensor &k,
+                   const at::Tensor &v, bool causal, double scale) {
+  check_bhnd(q, "q");
+  check_bhnd(k, "k");
+  check_bhnd(v, "v");
+  TORCH_CHECK(q.sizes() == k.sizes() && q.sizes() == v.sizes(),
+              "prefill expects q, k and v to have identical shapes, got q=",
+              q.sizes(), " k=", k.sizes(), " v=", v.sizes());
+  TORCH_CHECK(q.device() == k.device() && q.device() == v.device(),
+              "q, k and v must live on the same device");
+  TORCH_CHECK(q.size(2) > 0, "sequence length must be > 0");
+  TORCH_CHECK(std::isfinite(scale), "scale must be finite");
+
+  const c10::cuda::CUDAGuard guard(q.device());
+  at::Tensor o = at::empty_like(q);
+  check_status(fa_prefill(q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                          o.data_ptr(), to_int(q.size(0), "batch"),
+                          to_int(q.size(1), "heads"),
+                          to_int(q.size(2), "sequence length"), causal ? 1 : 0,
+                          static_cast<float>(scale), current_stream()),
+               "fa_prefill");
+  return o;
+}
+
+// decode / _decode_with_split: reference csrc/bindings.cpp:36-76,127-129.
+at::Tensor decode_impl(const at::Tensor &q, const at::Tensor &k_cache,
+                       const at::Tensor &v_cache, const at::Tensor &seq_lens,
+                       double scale, int64_t split_size) {
+  check_decode_inputs(q, k_cache, v_cache, seq_lens, scale);
+  if (split_size > 0) {
+    TORCH_CHECK(split_size % 4 == 0,
+                "decode split size must be a multiple of the warp count, got ",
+                split_size);
+  }
+  const c10::cuda::CUDAGuard guard(q.device());
+  const int B = to_int(q.size(0), "batch");
+  const int H = to_int(q.size(1), "heads");
+  const int S = to_int(k_cache.size(2), "cache length");
+  const int split = split_size > 0 ? to_int(split_size, "split_size") : 0;
+  at::Tensor o = at::empty_like(q);
+  const size_t bytes =
+      fa_decode_workspace_bytes(B, H, S, split, q.get_device());
+  TORCH_CHECK(bytes > 0, "fa_decode_workspace_bytes failed");
+  at::Tensor ws = decode_workspace(q, bytes);
+  check_status(fa_decode(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                         seq_lens.data_ptr<int32_t>(), o.data_ptr(), B, H, S,
+                         static_cast<float>(scale), split, ws.data_ptr(),
+                         static_cast<size_t>(ws.numel()), current_stream()),
+               "fa_decode");
+  return o;
+}
+
+at::Tensor decode(const at::Tensor &q, const at::Tensor &k_cache,
+                  const at::Tensor &v_cache, const at::Tensor &seq_lens,
+                  double scale) {
+  return decode_impl(q, k_cache, v_cache, seq_lens, scale, 0);
+}
+
+// Per-(b, h) log-sum-exp partials {m, l, 0, 0, acc[64]} of this device's part
+// of the cache; used by the sequence-sharded multi-GPU decode.
+at::Tensor decode_partial(const at::Tensor &q, const at::Tensor &k_cache,
+                          const at::Tensor &v_cache,
+                          const at::Tensor &seq_lens, double scale) {
+  check_decode_inputs(q, k_cache, v_cache, seq_lens, scale);
+  const c10::cuda::CUDAGuard guard(q.device());
+  const int B = to_int(q.size(0), "batch");
+  const int H = to_int(q.size(1), "heads");
+  const int S = to_int(k_cache.size(2), "cache length");
+  at::Tensor part = at::empty({B, H, 68}, q.options().dtype(at::kFloat));
+  const size_t bytes = fa_decode_workspace_bytes(B, H, S, 0, q.get_device());
+  TORCH_CHECK(bytes > 0, "fa_decode_workspace_bytes failed");
+  at::Tensor ws = decode_workspace(q, bytes);
+  check_status(
+      fa_decode_partial(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                        seq_lens.data_ptr<int32_t>(), part.data_ptr<float>(), B,
+                        H, S, static_cast<float>(scale), ws.data_ptr(),
+                        static_cast<size_t>(ws.numel()), current_stream()),
+      "fa_decode_partial");
+  return part;
+}
+
+// Merges (G, B, H, 68) partials into the fp16 (B, H, 1, 64) output.
+at::Tensor merge_partials(const at::Tensor &partials) {
+  check_cuda(partials, "partials");
+  check_contiguous(partials, "partials");
+  TORCH_CHECK(partials.scalar_type() == at::kFloat,
+              "partials must be fp32 (got ", partials.scalar_type(), ")");
+  TORCH_CHECK(partials.dim() == 4 && partials.size(3) == 68,
+              "partials must be (G, B, H, 68), got ", partials.sizes());
+  const c10::cuda::CUDAGuard guard(partials.device());
+  const int G = to_int(partials.size(0), "G");
+  const int B = to_int(partials.size(1), "batch");
+  const int H = to_int(partials.size(2), "heads");
+  at::Tensor o = at::empty({B, H, 1, kHeadDim},
+                           partials.options().dtype(at::kHalf));
+  check_status(fa_merge_partials(partials.data_ptr<float>(), G, o.data_ptr(),
+                                 B, H, current_stream()),
+               "fa_merge_partials");
+  return o;
+}
+
+int64_t choose_decode_split(int64_t max_seq, int64_t batch, int64_t heads,
+                            int64_t min_blocks) {
+  return fa_choose_decode_split(static_cast<int>(max_seq),
+                                static_cast<int>(batch),
+                                static_cast<int>(heads),
+                                static_cast<int>(min_blocks));
+}
+
+// occupancy_report(): reference csrc/bindings.cpp:80-97, same row keys.
+py::list occupancy_report() {
+  fa_occupancy_entry rows[8];
+  int n = 0;
+  check_status(fa_occupancy(rows, 8, &n), "fa_occupancy");
+  py::list out;
+  for (int i = 0; i < n && i < 8; ++i) {
+    py::dict row;
+    row["kernel"] = std::string(rows[i].name);
+    row["threads_per_block"] = rows[i].threads_per_block;
+    row["registers_per_thread"] = rows[i].registers_per_thread;
+    row["shared_bytes_per_block"] = rows[i].shared_bytes_per_block;
+    row["max_active_blocks_per_sm"] = rows[i].max_active_blocks_per_sm;
+    row["theoretical_occupancy"] = rows[i].theoretical_occupancy;
+    out.append(row);
+  }
+  return out;
+}
+
+// Reads and clears the device-side error word (0: every kernel completed).
+int64_t take_device_error() {
+  unsigned int bits = 0;
+  check_status(fa_take_device_error(&bits), "fa_take_device_error");
+  return bits;
+}
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "B200 (sm_100a) FlashAttention forward for head_dim=64";
+  m.attr("head_dim") = kHeadDim;
+  m.def("prefill", &prefill,
+        "Full-sequence attention (fp16 in/out, fp32 accum)", py::arg("q"),
+        py::arg("k"), py::arg("v"), py::arg("causal"), py::arg("scale"));
+  m.def("decode", &decode, "Single-query attention against a KV cache",
+        py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
+        py::arg("seq_lens"), py::arg("scale"));
+  m.def("occupancy_report", &occupancy_report,
+        "Theoretical occupancy of each kernel at its launch configuration");
+  m.def("choose_decode_split", &choose_decode_split,
+        "Chunk size rule of the reference's split-K decode",
+        py::arg("max_seq"), py::arg("batch"), py::arg("heads"),
+        py::arg("min_blocks"));
+  m.def("_decode_with_split", &decode_impl, py::arg("q"), py::arg("k_cache"),
+        py::arg("v_cache"), py::arg("seq_lens"), py::arg("scale"),
+        py::arg("split_size"));
+  m.def("decode_partial", &decode_partial,
+        "Log-sum-exp partials of decode over this device's cache rows",
+        py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
+        py::arg("seq_lens"), py::arg("scale"));
+  m.def("merge_partials", &merge_partials,
+        "Merge (G, B, H, 68) decode partials into the fp16 output",
+        py::arg("partials"));
+  m.def("take_device_error", &take_device_error,
+        "Read and clear the device-side error word");
+}

@@ -1,0 +1,344 @@
+// C ABI (include/fa_b200.h): argument checks, TMA descriptor construction,
+// per-device one-time set-up and kernel launches. No allocation happens here;
+// callers own every buffer.
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "fa_b200.h"
+#include "fa_kernels.h"
+#include "fa_sm100.cuh"
+
+namespace fa {
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceState {
+  bool ready = false;
+  int status = FA_OK;
+  int sms = 0;
+};
+
+std::mutex g_mutex;
+DeviceState g_devices[kMaxDevices];
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t,
+                                  void *, const cuuint64_t *, const cuuint64_t *,
+                                  const cuuint32_t *, const cuuint32_t *,
+                                  CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion,
+                                  CUtensorMapFloatOOBfill);
+EncodeTiledFn g_encode = nullptr;
+
+bool aligned16(const void *p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+// One-time set-up of the current device: checks it is an sm_100 part, raises
+// the kernels' dynamic shared-memory limits and resolves the driver's tensor
+// map encoder.
+int ensure_device(int *device_out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return FA_ECUDA;
+  if (dev < 0 || dev >= kMaxDevices) return FA_EDEVICE;
+  if (device_out) *device_out = dev;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  DeviceState &st = g_devices[dev];
+  if (st.ready) return st.status;
+  st.ready = true;
+  int major = 0, minor = 0, sms = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) !=
+          cudaSuccess ||
+      cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) !=
+          cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=
+          cudaSuccess) {
+    st.status = FA_ECUDA;
+    return st.status;
+  }
+  if (major != 10 || minor != 0) {
+    st.status = FA_EDEVICE;
+    return st.status;
+  }
+  st.sms = sms;
+  if (cudaFuncSetAttribute(prefill_kernel_ptr(),
+                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           prefill_smem_bytes()) != cudaSuccess ||
+      cudaFuncSetAttribute(decode_kernel_ptr(),
+                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           decode_smem_bytes()) != cudaSuccess) {
+    st.status = FA_ECUDA;
+    return st.status;
+  }
+  if (!g_encode) {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault,
+                                &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || fn == nullptr) {
+      st.status = FA_EDEVICE;
+      return st.status;
+    }
+    g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+  }
+  st.status = FA_OK;
+  return st.status;
+}
+
+// (B*H, N, 64) fp16 view of a (B, H, N, 64) tensor, 128-row x 64-column
+// boxes written with the 128-byte swizzle; rows past N read as zero.
+int make_bhn64_map(CUtensorMap *map, const void *base, int BH, int N) {
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(FA_HEAD_DIM),
+                        static_cast<cuuint64_t>(N),
+                        static_cast<cuuint64_t>(BH)};
+  cuuint64_t strides[2] = {
+      static_cast<cuuint64_t>(FA_HEAD_DIM) * 2,
+      static_cast<cuuint64_t>(N) * FA_HEAD_DIM * 2};
+  cuuint32_t box[3] = {FA_HEAD_DIM, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                        const_cast<void *>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? FA_OK : FA_EINVAL;
+}
+
+int decode_grid(int sms, int B, int H, int S_max, int split_size) {
+  const long long cap_rows = static_cast<long long>(B) * H * S_max;
+  if (split_size > 0) {
+    const long long g = (cap_rows + split_size - 1) / split_size;
+    return static_cast<int>(g < 1 ? 1 : g);
+  }
+  const long long by_rows =
+      (cap_rows + decode_min_rows_per_cta() - 1) / decode_min_rows_per_cta();
+  long long g = static_cast<long long>(sms) * decode_ctas_per_sm();
+  if (by_rows < g) g = by_rows;
+  return static_cast<int>(g < 1 ? 1 : g);
+}
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+size_t workspace_bytes_for(int B, int H, int grid) {
+  const size_t counters = align_up(static_cast<size_t>(B) * H * 4, 256);
+  const size_t partials = (static_cast<size_t>(B) * H + grid) *
+                          kPartialFloats * sizeof(float);
+  return counters + partials;
+}
+
+bool decode_shape_ok(int B, int H, int S_max, float scale) {
+  if (B <= 0 || H <= 0 || S_max <= 0 || !isfinite(scale)) return false;
+  const long long rows = static_cast<long long>(B) * H * S_max;
+  return rows < (1ll << 40) && static_cast<long long>(B) * H < (1ll << 30);
+}
+
+int run_decode(const void *q, const void *k_cache, const void *v_cache,
+               const int32_t *seq_lens, void *o, float *partial_out, int B,
+               int H, int S_max, float scale, int split_size, void *workspace,
+               size_t workspace_bytes, void *stream) {
+  if (!decode_shape_ok(B, H, S_max, scale)) return FA_EINVAL;
+  if (split_size > 0 && split_size % 4 != 0) return FA_EINVAL;
+  if (!q || !k_cache || !v_cache || !seq_lens || (!o && !partial_out) ||
+      !workspace)
+    return FA_EINVAL;
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) ||
+      (o && !aligned16(o)) || (partial_out && !aligned16(partial_out)) ||
+      !aligned16(workspace) || (reinterpret_cast<uintptr_t>(seq_lens) & 3u))
+    return FA_EALIGN;
+  int dev = 0;
+  int rc = ensure_device(&dev);
+  if (rc != FA_OK) return rc;
+  const int grid = decode_grid(g_devices[dev].sms, B, H, S_max, split_size);
+  if (workspace_bytes < workspace_bytes_for(B, H, grid)) return FA_ENOSPACE;
+  DecodeArgs a;
+  a.q = static_cast<const __half *>(q);
+  a.k = static_cast<const __half *>(k_cache);
+  a.v = static_cast<const __half *>(v_cache);
+  a.seq_lens = seq_lens;
+  a.out = static_cast<__half *>(o);
+  a.partial_out = partial_out;
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  a.ws_counters = reinterpret_cast<uint32_t *>(ws);
+  a.ws_partials = reinterpret_cast<float *>(
+      ws + align_up(static_cast<size_t>(B) * H * 4, 256));
+  a.B = B;
+  a.H = H;
+  a.S_max = S_max;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.rows_per_cta = split_size > 0 ? split_size : 0;
+  a.grid = grid;
+  return launch_decode_kernel(a, static_cast<cudaStream_t>(stream)) ==
+                 cudaSuccess
+             ? FA_OK
+             : FA_ECUDA;
+}
+
+}  // namespace
+}  // namespace fa
+
+using namespace fa;
+
+extern "C" {
+
+int fa_prefill(const void *q, const void *k, const void *v, void *o, int B,
+               int H, int N, int causal, float scale, void *stream) {
+  if (B <= 0 || H <= 0 || N <= 0 || !isfinite(scale)) return FA_EINVAL;
+  if (static_cast<long long>(B) * H >= (1ll << 31) / 64 ||
+      static_cast<long long>(N) >= (1ll << 31))
+    return FA_EINVAL;
+  if (!q || !k || !v || !o) return FA_EINVAL;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+    return FA_EALIGN;
+  int rc = ensure_device(nullptr);
+  if (rc != FA_OK) return rc;
+  CUtensorMap tq, tk, tv;
+  if (make_bhn64_map(&tq, q, B * H, N) != FA_OK ||
+      make_bhn64_map(&tk, k, B * H, N) != FA_OK ||
+      make_bhn64_map(&tv, v, B * H, N) != FA_OK)
+    return FA_EINVAL;
+  return launch_prefill_kernel(tq, tk, tv, static_cast<__half *>(o), B, H, N,
+                               causal != 0, scale,
+                               static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? FA_OK
+             : FA_ECUDA;
+}
+
+size_t fa_decode_workspace_bytes(int B, int H, int S_max, int split_size,
+                                 int device) {
+  if (B <= 0 || H <= 0 || S_max <= 0) return 0;
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) !=
+      cudaSuccess)
+    return 0;
+  return workspace_bytes_for(B, H, decode_grid(sms, B, H, S_max, split_size));
+}
+
+int fa_decode(const void *q, const void *k_cache, const void *v_cache,
+              const int32_t *seq_lens, void *o, int B, int H, int S_max,
+              float scale, int split_size, void *workspace,
+              size_t workspace_bytes, void *stream) {
+  if (!o) return FA_EINVAL;
+  return run_decode(q, k_cache, v_cache, seq_lens, o, nullptr, B, H, S_max,
+                    scale, split_size, workspace, workspace_bytes, stream);
+}
+
+int fa_decode_partial(const void *q, const void *k_cache, const void *v_cache,
+                      const int32_t *seq_lens, float *partial_out, int B,
+                      int H, int S_max, float scale, void *workspace,
+                      size_t workspace_bytes, void *stream) {
+  if (!partial_out) return FA_EINVAL;
+  return run_decode(q, k_cache, v_cache, seq_lens, nullptr, partial_out, B, H,
+                    S_max, scale, 0, workspace, workspace_bytes, stream);
+}
+
+int fa_merge_partials(const float *partials, int G, void *o, int B, int H,
+                      void *stream) {
+  if (!partials || !o || G <= 0 || B <= 0 || H <= 0) return FA_EINVAL;
+  if (static_cast<long long>(B) * H >= (1ll << 31)) return FA_EINVAL;
+  if (!aligned16(partials) || !aligned16(o)) return FA_EALIGN;
+  int rc = ensure_device(nullptr);
+  if (rc != FA_OK) return rc;
+  return launch_merge_kernel(partials, G, static_cast<__half *>(o), B, H,
+                             static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? FA_OK
+             : FA_ECUDA;
+}
+
+int fa_choose_decode_split(int max_seq, int batch, int heads, int min_blocks) {
+  const long long per_split = static_cast<long long>(batch) * heads;
+  for (int split = 1024; split > 128; split >>= 1) {
+    const long long splits = (static_cast<long long>(max_seq) + split - 1) / split;
+    if (per_split * splits >= min_blocks) return split;
+  }
+  return 128;
+}
+
+int fa_occupancy(fa_occupancy_entry *out, int max_entries, int *count) {
+  int dev = 0;
+  int rc = ensure_device(&dev);
+  if (rc != FA_OK) return rc;
+  int max_threads = 0;
+  if (cudaDeviceGetAttribute(&max_threads,
+                             cudaDevAttrMaxThreadsPerMultiProcessor,
+                             dev) != cudaSuccess)
+    return FA_ECUDA;
+  struct K {
+    const char *name;
+    const void *fn;
+    int threads;
+    int dyn_smem;
+  } kernels[] = {
+      {"prefill_kernel", prefill_kernel_ptr(), prefill_threads(),
+       prefill_smem_bytes()},
+      {"decode_kernel", decode_kernel_ptr(), decode_threads(),
+       decode_smem_bytes()},
+      {"merge_kernel", merge_kernel_ptr(), merge_threads(), 0},
+  };
+  const int n = static_cast<int>(sizeof(kernels) / sizeof(kernels[0]));
+  if (count) *count = n;
+  for (int i = 0; i < n && i < max_entries; ++i) {
+    cudaFuncAttributes attr;
+    if (cudaFuncGetAttributes(&attr, kernels[i].fn) != cudaSuccess)
+      return FA_ECUDA;
+    int blocks = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+            &blocks, kernels[i].fn, kernels[i].threads,
+            kernels[i].dyn_smem) != cudaSuccess)
+      return FA_ECUDA;
+    fa_occupancy_entry &e = out[i];
+    memset(&e, 0, sizeof(e));
+    strncpy(e.name, kernels[i].name, sizeof(e.name) - 1);
+    e.threads_per_block = kernels[i].threads;
+    e.registers_per_thread = attr.numRegs;
+    e.shared_bytes_per_block =
+        static_cast<int>(attr.sharedSizeBytes) + kernels[i].dyn_smem;
+    e.max_active_blocks_per_sm = blocks;
+    e.theoretical_occupancy =
+        static_cast<double>(blocks) * kernels[i].threads / max_threads;
+  }
+  return FA_OK;
+}
+
+int fa_take_device_error(unsigned int *bits) {
+  if (!bits) return FA_EINVAL;
+  if (cudaDeviceSynchronize() != cudaSuccess) return FA_ECUDA;
+  unsigned int v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, g_fa_error_word, sizeof(v)) != cudaSuccess ||
+      cudaMemcpyToSymbol(g_fa_error_word, &zero, sizeof(zero)) != cudaSuccess)
+    return FA_ECUDA;
+  *bits = v;
+  return FA_OK;
+}
+
+const char *fa_status_string(int status) {
+  switch (status) {
+    case FA_OK: return "ok";
+    case FA_EINVAL: return "invalid argument";
+    case FA_EALIGN: return "pointer not 16-byte aligned";
+    case FA_ECUDA: return "CUDA runtime error";
+    case FA_ENOSPACE: return "workspace too small";
+    case FA_EDEVICE: return "device is not sm_100 or driver entry point missing";
+    default: return "unknown status";
+  }
+}
+
+int fa_num_sms(void) {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=
+      cudaSuccess)
+    return 0;
+  return sms;
+}
+
+}  // extern "C"

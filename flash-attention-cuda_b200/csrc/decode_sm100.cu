@@ -1,0 +1,491 @@
+// Decode (single query row per sequence) attention against a KV cache, B200.
+//
+// Behaviour follows the reference's split-K decode (csrc/decode.cu:50-175):
+// out[b,h] = softmax(scale * q[b,h] . K[b,h,:len_b]^T) V[b,h,:len_b] with
+// len_b = min(seq_lens[b], S_max); a sequence with no rows gets 0; partial
+// results are combined with the log-sum-exp rule, skipping empty partials.
+//
+// The schedule is different. The reference launches ceil(S_max/split) CTAs
+// per (b, h), sized by cache capacity, and merges in a second kernel. Here
+// the valid rows of all (b, h) segments are laid end to end
+// (segment g = b*H + h holds len_b rows) and a persistent grid cuts that flat
+// row range into equal pieces, so every CTA streams the same number of bytes
+// whatever the length distribution. A CTA's range can cover the tail of one
+// segment, several whole segments and the head of another. Each
+// (segment, CTA) overlap produces one (m, l, acc[64]) partial; a segment
+// covered by one CTA is finished in place, otherwise the partials go to
+// workspace slot (g + cta) — unique because the overlaps form a monotone
+// staircase — and the last CTA to arrive on the segment's counter (an
+// atomicInc that wraps back to 0, so the counters are clean for the next
+// call) merges them in a fixed order. One launch, no second pass.
+//
+// CTA = 9 warps. Warp 8 plans and streams: it walks the segment pieces and
+// issues cp.async.bulk copies of up to 128 K rows and 128 V rows (16 KiB each,
+// contiguous in the cache) into a 3-stage shared-memory ring, with a stage
+// header describing the rows. Warps 0-7 consume: each takes 16 rows of a
+// stage, 8 lanes per row (16 bytes, 8 head dims per lane), 4 rows per warp
+// instruction, 3-step shuffle dot products, block-wise online softmax in the
+// exp2 domain.
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include "fa_kernels.h"
+#include "fa_sm100.cuh"
+
+namespace fa {
+namespace decode {
+
+constexpr int kConsumerWarps = 8;
+constexpr int kProducerWarp = kConsumerWarps;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kConsumerThreads = kConsumerWarps * 32;
+constexpr int kStageRows = 128;
+constexpr int kStages = 3;
+constexpr int kRowsPerWarp = kStageRows / kConsumerWarps;  // 16
+constexpr int kMinRowsPerCta = 128;
+constexpr int kCtasPerSm = 2;
+constexpr uint32_t kStageBytes = kStageRows * kRowBytes;  // 16 KiB
+
+struct StageHeader {
+  int g;      // segment (b * H + h)
+  int n;      // rows in this stage (0 for the end marker)
+  int flags;  // kLast | kWhole | kDone
+  int c0;     // first CTA covering the segment
+  int c1;     // last CTA covering the segment
+  int pad[3];
+};
+constexpr int kLast = 1;   // last stage of this CTA's piece of the segment
+constexpr int kWhole = 2;  // the segment lies entirely inside this CTA
+constexpr int kDone = 4;   // no more stages
+
+constexpr uint32_t kKOff = 0;
+constexpr uint32_t kVOff = kStages * kStageBytes;
+constexpr uint32_t kHdrOff = 2 * kStages * kStageBytes;
+constexpr uint32_t kRedOff = kHdrOff + kStages * sizeof(StageHeader);
+constexpr uint32_t kRedBytes = kConsumerWarps * kPartialFloats * 4;
+constexpr uint32_t kBarOff = kRedOff + kRedBytes;
+constexpr uint32_t kFlagOff = kBarOff + 2 * kStages * 8;
+constexpr uint32_t kSmemBytes = kFlagOff + 16;
+
+constexpr float kNegBig = -1e30f;  // finite "no max yet", as the reference
+
+__device__ __forceinline__ int clamp_len(int len, int s_max) {
+  return len < 0 ? 0 : (len > s_max ? s_max : len);
+}
+
+__device__ __forceinline__ long long warp_sum_ll(long long v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Writes the result of a sequence with no valid rows: 0 (reference
+// decode.cu:164-172), or an empty partial (l = 0) in partial mode.
+__device__ void write_empty_sequence(const DecodeArgs &a, int b) {
+  for (int h = 0; h < a.H; ++h) {
+    const size_t g = static_cast<size_t>(b) * a.H + h;
+    if (a.partial_out) {
+      float *p = a.partial_out + g * kPartialFloats;
+      p[0] = kNegBig;
+      for (int i = 1; i < kPartialFloats; ++i) p[i] = 0.f;
+    } else {
+      uint4 *o = reinterpret_cast<uint4 *>(a.out + g * kHeadDim);
+      for (int i = 0; i < kHeadDim / 8; ++i) o[i] = make_uint4(0, 0, 0, 0);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
+    decode_kernel(const DecodeArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + kBarOff);
+  uint64_t *empty = full + kStages;
+  StageHeader *hdr = reinterpret_cast<StageHeader *>(smem + kHdrOff);
+  float *red = reinterpret_cast<float *>(smem + kRedOff);
+  volatile int *last_flag = reinterpret_cast<volatile int *>(smem + kFlagOff);
+  if (device_failed()) return;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == kProducerWarp) {
+    // ------------------------------------------------------------ planning
+    long long sum_len = 0;
+    for (int b = lane; b < a.B; b += 32) {
+      const int len = clamp_len(a.seq_lens[b], a.S_max);
+      sum_len += len;
+      if (len == 0 && (b % static_cast<int>(gridDim.x)) ==
+                          static_cast<int>(blockIdx.x)) {
+        write_empty_sequence(a, b);
+      }
+    }
+    const long long total = warp_sum_ll(sum_len) * a.H;
+    long long per = a.rows_per_cta;
+    if (per <= 0) {
+      per = (total + gridDim.x - 1) / gridDim.x;
+      if (per < kMinRowsPerCta) per = kMinRowsPerCta;
+    }
+    const long long start = static_cast<long long>(blockIdx.x) * per;
+    const long long end = start + per < total ? start + per : total;
+
+    // Locate the batch entry holding flat row `start`: warp-wide inclusive
+    // scan of H * len_b, 32 entries at a time.
+    int b_start = 0;
+    long long base_b = 0;
+    if (start < end) {
+      long long base = 0;
+      for (int chunk = 0; chunk < a.B; chunk += 32) {
+        const int b = chunk + lane;
+        const long long rows =
+            b < a.B ? static_cast<long long>(clamp_len(a.seq_lens[b], a.S_max)) *
+                          a.H
+                    : 0;
+        long long incl = rows;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const long long t = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += t;
+        }
+        const unsigned hit =
+            __ballot_sync(0xffffffffu, b < a.B && base + incl > start);
+        if (hit) {
+          const int first = __ffs(hit) - 1;
+          const long long incl_first = __shfl_sync(0xffffffffu, incl, first);
+          const long long rows_first = __shfl_sync(0xffffffffu, rows, first);
+          b_start = chunk + first;
+          base_b = base + incl_first - rows_first;
+          break;
+        }
+        base += __shfl_sync(0xffffffffu, incl, 31);
+      }
+    }
+
+    // ------------------------------------------------------------ streaming
+    if (lane == 0) {
+      const uint64_t policy = l2_policy_evict_first();
+      int it = 0;
+      bool ok = true;
+      long long cur = start;
+      int b = b_start;
+      while (ok && cur < end && b < a.B) {
+        const int len = clamp_len(a.seq_lens[b], a.S_max);
+        if (len == 0) {
+          ++b;
+          continue;
+        }
+        const long long off = cur - base_b;
+        const int h = static_cast<int>(off / len);
+        const int r = static_cast<int>(off - static_cast<long long>(h) * len);
+        const long long seg_start = base_b + static_cast<long long>(h) * len;
+        const long long seg_end = seg_start + len;
+        const long long piece_end = end < seg_end ? end : seg_end;
+        const int c0 = static_cast<int>(seg_start / per);
+        const int c1 = static_cast<int>((seg_end - 1) / per);
+        const int g = b * a.H + h;
+        const size_t row0 = static_cast<size_t>(g) * a.S_max + r;
+        for (long long r0 = cur; r0 < piece_end; r0 += kStageRows) {
+          const int n = static_cast<int>(
+              piece_end - r0 < kStageRows ? piece_end - r0 : kStageRows);
+          const int slot = it % kStages;
+          const int use = it / kStages;
+          if (use > 0 && !mbar_wait(&empty[slot], (use - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          StageHeader &hd = hdr[slot];
+          hd.g = g;
+          hd.n = n;
+          hd.flags = (r0 + n == piece_end ? kLast : 0) | (c0 == c1 ? kWhole : 0);
+          hd.c0 = c0;
+          hd.c1 = c1;
+          const size_t elem = (row0 + static_cast<size_t>(r0 - cur)) * kHeadDim;
+          const uint32_t bytes = static_cast<uint32_t>(n) * kRowBytes;
+          mbar_arrive_expect_tx(&full[slot], 2 * bytes);
+          bulk_load(smem + kKOff + slot * kStageBytes, a.k + elem, bytes,
+                    &full[slot], policy);
+          bulk_load(smem + kVOff + slot * kStageBytes, a.v + elem, bytes,
+                    &full[slot], policy);
+          ++it;
+        }
+        cur = piece_end;
+        if (cur == base_b + static_cast<long long>(a.H) * len) {
+          base_b += static_cast<long long>(a.H) * len;
+          ++b;
+        }
+      }
+      // End marker.
+      const int slot = it % kStages;
+      const int use = it / kStages;
+      if (ok && (use == 0 || mbar_wait(&empty[slot], (use - 1) & 1))) {
+        hdr[slot].n = 0;
+        hdr[slot].flags = kDone;
+        mbar_arrive(&full[slot]);
+      } else {
+        // Consumers stopped early: let our copies land before the CTA exits.
+        for (int j = (it > kStages ? it - kStages : 0); j < it; ++j)
+          mbar_wait(&full[j % kStages], (j / kStages) & 1);
+      }
+    }
+    return;
+  }
+
+  // ---------------------------------------------------------------- consumers
+  const int grp = lane >> 3;  // which of the warp's 4 rows per instruction
+  const int sub = lane & 7;   // head dims [8*sub, 8*sub + 8)
+  float qf[8];
+  int cur_g = -1;
+  float m_run = kNegBig, l_run = 0.f;
+  float acc[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+
+  for (int it = 0;; ++it) {
+    const int slot = it % kStages;
+    if (!mbar_wait(&full[slot], (it / kStages) & 1)) break;
+    const StageHeader hd = hdr[slot];
+    if (hd.flags & kDone) break;
+    if (hd.g != cur_g) {
+      cur_g = hd.g;
+      const uint4 qv = *reinterpret_cast<const uint4 *>(
+          a.q + static_cast<size_t>(cur_g) * kHeadDim + sub * 8);
+      const __half2 *qh = reinterpret_cast<const __half2 *>(&qv);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __half22float2(qh[e]);
+        qf[2 * e] = f.x * a.scale_log2;
+        qf[2 * e + 1] = f.y * a.scale_log2;
+      }
+    }
+
+    const uint32_t kb = smem_u32(smem + kKOff + slot * kStageBytes);
+    const uint32_t vb = smem_u32(smem + kVOff + slot * kStageBytes);
+    const int row_base = warp * kRowsPerWarp + grp;
+    if (warp * kRowsPerWarp < hd.n) {  // warp-uniform: shuffles below
+      float sc[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int row = row_base + 4 * i;
+        float d = 0.f;
+        if (row < hd.n) {
+          const uint4 kv = ld_shared_v4(kb + row * kRowBytes + sub * 16);
+          const __half2 *kh = reinterpret_cast<const __half2 *>(&kv);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __half22float2(kh[e]);
+            d = fmaf(qf[2 * e], f.x, d);
+            d = fmaf(qf[2 * e + 1], f.y, d);
+          }
+        }
+        sc[i] = d;
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        sc[i] += __shfl_xor_sync(0xffffffffu, sc[i], 1);
+        sc[i] += __shfl_xor_sync(0xffffffffu, sc[i], 2);
+        sc[i] += __shfl_xor_sync(0xffffffffu, sc[i], 4);
+        if (row_base + 4 * i >= hd.n) sc[i] = -INFINITY;
+      }
+      const float mx = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
+      const float m_new = fmaxf(m_run, mx);
+      const float corr = fast_exp2(m_run - m_new);
+      m_run = m_new;
+      float p[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) p[i] = fast_exp2(sc[i] - m_new);
+      l_run = fmaf(l_run, corr, (p[0] + p[1]) + (p[2] + p[3]));
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] *= corr;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int row = row_base + 4 * i;
+        if (row < hd.n) {
+          const uint4 vv = ld_shared_v4(vb + row * kRowBytes + sub * 16);
+          const __half2 *vh = reinterpret_cast<const __half2 *>(&vv);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __half22float2(vh[e]);
+            acc[2 * e] = fmaf(p[i], f.x, acc[2 * e]);
+            acc[2 * e + 1] = fmaf(p[i], f.y, acc[2 * e + 1]);
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+
+    if (!(hd.flags & kLast)) continue;
+
+    // ---- this CTA's piece of segment hd.g is complete: reduce it --------
+    // 4 row groups of the warp -> one (m, l, acc[64]) per warp.
+    float m_w = fmaxf(m_run, __shfl_xor_sync(0xffffffffu, m_run, 8));
+    m_w = fmaxf(m_w, __shfl_xor_sync(0xffffffffu, m_w, 16));
+    const float f = fast_exp2(m_run - m_w);
+    float l_w = l_run * f;
+    l_w += __shfl_xor_sync(0xffffffffu, l_w, 8);
+    l_w += __shfl_xor_sync(0xffffffffu, l_w, 16);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float v = acc[e] * f;
+      v += __shfl_xor_sync(0xffffffffu, v, 8);
+      v += __shfl_xor_sync(0xffffffffu, v, 16);
+      acc[e] = v;
+    }
+    float *my = red + warp * kPartialFloats;
+    if (lane < 8) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) my[4 + lane * 8 + e] = acc[e];
+      if (lane == 0) {
+        my[0] = m_w;
+        my[1] = l_w;
+      }
+    }
+    named_bar_sync(1, kConsumerThreads);
+
+    if (threadIdx.x < kHeadDim) {
+      const int d = threadIdx.x;
+      float M = kNegBig;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w)
+        M = fmaxf(M, red[w * kPartialFloats]);
+      float L = 0.f, A = 0.f;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        const float fw = fast_exp2(red[w * kPartialFloats] - M);
+        L = fmaf(red[w * kPartialFloats + 1], fw, L);
+        A = fmaf(red[w * kPartialFloats + 4 + d], fw, A);
+      }
+      const size_t g = static_cast<size_t>(hd.g);
+      if (hd.flags & kWhole) {
+        if (a.partial_out) {
+          float *p = a.partial_out + g * kPartialFloats;
+          p[4 + d] = A;
+          if (d == 0) {
+            p[0] = M;
+            p[1] = L;
+            p[2] = 0.f;
+            p[3] = 0.f;
+          }
+        } else {
+          a.out[g * kHeadDim + d] = __float2half_rn(L > 0.f ? A / L : 0.f);
+        }
+      } else {
+        float *ws = a.ws_partials +
+                    (g + blockIdx.x) * static_cast<size_t>(kPartialFloats);
+        ws[4 + d] = A;
+        if (d == 0) {
+          ws[0] = M;
+          ws[1] = L;
+        }
+        __threadfence();
+        named_bar_sync(2, kHeadDim);
+        if (d == 0) {
+          const unsigned n_parts = static_cast<unsigned>(hd.c1 - hd.c0);
+          const unsigned old = atomicInc(&a.ws_counters[g], n_parts);
+          *last_flag = (old == n_parts) ? 1 : 0;
+        }
+        named_bar_sync(2, kHeadDim);
+        if (*last_flag) {
+          __threadfence();
+          // Every partial of the segment is in place: merge in CTA order.
+          float M2 = kNegBig;
+          for (int c = hd.c0; c <= hd.c1; ++c) {
+            const float *pp =
+                a.ws_partials + (g + c) * static_cast<size_t>(kPartialFloats);
+            if (__ldcg(pp + 1) > 0.f) M2 = fmaxf(M2, __ldcg(pp));
+          }
+          float L2 = 0.f, A2 = 0.f;
+          for (int c = hd.c0; c <= hd.c1; ++c) {
+            const float *pp =
+                a.ws_partials + (g + c) * static_cast<size_t>(kPartialFloats);
+            const float lc = __ldcg(pp + 1);
+            if (lc <= 0.f) continue;
+            const float fc = fast_exp2(__ldcg(pp) - M2);
+            L2 = fmaf(lc, fc, L2);
+            A2 = fmaf(__ldcg(pp + 4 + d), fc, A2);
+          }
+          if (a.partial_out) {
+            float *p = a.partial_out + g * kPartialFloats;
+            p[4 + d] = A2;
+            if (d == 0) {
+              p[0] = M2;
+              p[1] = L2;
+              p[2] = 0.f;
+              p[3] = 0.f;
+            }
+          } else {
+            a.out[g * kHeadDim + d] =
+                __float2half_rn(L2 > 0.f ? A2 / L2 : 0.f);
+          }
+        }
+      }
+    }
+    m_run = kNegBig;
+    l_run = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+    named_bar_sync(1, kConsumerThreads);
+  }
+}
+
+// Log-sum-exp merge of G partial sets (G, B*H, 68) -> fp16 (B*H, 64).
+__global__ void __launch_bounds__(kHeadDim)
+    merge_kernel(const float *__restrict__ partials, int G, int BH,
+                 __half *__restrict__ out) {
+  const size_t g = blockIdx.x;
+  const int d = threadIdx.x;
+  float M = kNegBig;
+  for (int r = 0; r < G; ++r) {
+    const float *p = partials + (static_cast<size_t>(r) * BH + g) * kPartialFloats;
+    if (p[1] > 0.f) M = fmaxf(M, p[0]);
+  }
+  float L = 0.f, A = 0.f;
+  for (int r = 0; r < G; ++r) {
+    const float *p = partials + (static_cast<size_t>(r) * BH + g) * kPartialFloats;
+    if (p[1] <= 0.f) continue;
+    const float f = fast_exp2(p[0] - M);
+    L = fmaf(p[1], f, L);
+    A = fmaf(p[4 + d], f, A);
+  }
+  out[g * kHeadDim + d] = __float2half_rn(L > 0.f ? A / L : 0.f);
+}
+
+}  // namespace decode
+
+const void *decode_kernel_ptr() {
+  return reinterpret_cast<const void *>(decode::decode_kernel);
+}
+int decode_threads() { return decode::kThreads; }
+int decode_smem_bytes() { return static_cast<int>(decode::kSmemBytes); }
+int decode_ctas_per_sm() { return decode::kCtasPerSm; }
+int decode_min_rows_per_cta() { return decode::kMinRowsPerCta; }
+
+cudaError_t launch_decode_kernel(const DecodeArgs &args, cudaStream_t stream) {
+  decode::decode_kernel<<<args.grid, decode::kThreads, decode::kSmemBytes,
+                          stream>>>(args);
+  return cudaGetLastError();
+}
+
+const void *merge_kernel_ptr() {
+  return reinterpret_cast<const void *>(decode::merge_kernel);
+}
+int merge_threads() { return kHeadDim; }
+
+cudaError_t launch_merge_kernel(const float *partials, int G, __half *out,
+                                int B, int H, cudaStream_t stream) {
+  decode::merge_kernel<<<B * H, kHeadDim, 0, stream>>>(partials, G, B * H, out);
+  return cudaGetLastError();
+}
+
+}  // namespace fa

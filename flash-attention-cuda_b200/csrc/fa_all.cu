@@ -1,0 +1,6 @@
+// Single translation unit for libfa_b200.so: the kernels share the
+// device-side error word, which (without relocatable device code) must be
+// defined in the same unit that uses it.
+#include "capi.cu"
+#include "decode_sm100.cu"
+#include "prefill_sm100.cu"

@@ -1,0 +1,51 @@
+// Internal launch interface between the C ABI (capi.cu) and the kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace fa {
+
+// ---- prefill (prefill_sm100.cu) -------------------------------------------
+const void *prefill_kernel_ptr();
+int prefill_threads();
+int prefill_smem_bytes();
+cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
+                                  const CUtensorMap &tm_k,
+                                  const CUtensorMap &tm_v, __half *out, int B,
+                                  int H, int N, bool causal, float scale,
+                                  cudaStream_t stream);
+
+// ---- decode (decode_sm100.cu) ---------------------------------------------
+struct DecodeArgs {
+  const __half *q;
+  const __half *k;
+  const __half *v;
+  const int32_t *seq_lens;
+  __half *out;           // final fp16 output, or
+  float *partial_out;    // (B, H, 68) log-sum-exp partials when non-null
+  float *ws_partials;    // (B*H + grid) x 68 fp32
+  uint32_t *ws_counters; // B*H arrival counters, zero between calls
+  int B, H, S_max;
+  float scale_log2;
+  long long rows_per_cta;  // 0: balance the valid rows over the grid
+  int grid;
+};
+
+constexpr int kPartialFloats = 68;  // m, l, pad, pad, acc[64]
+
+const void *decode_kernel_ptr();
+int decode_threads();
+int decode_smem_bytes();
+int decode_ctas_per_sm();
+int decode_min_rows_per_cta();
+cudaError_t launch_decode_kernel(const DecodeArgs &args, cudaStream_t stream);
+
+const void *merge_kernel_ptr();
+int merge_threads();
+cudaError_t launch_merge_kernel(const float *partials, int G, __half *out,
+                                int B, int H, cudaStream_t stream);
+
+}  // namespace fa

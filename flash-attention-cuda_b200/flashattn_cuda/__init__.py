@@ -1,0 +1,37 @@
+"""B200 (sm_100a) FlashAttention forward for head_dim = 64.
+
+Drop-in for the reference package of the same name
+(flashattn_cuda/__init__.py in shrvan30/flash-attention-cuda): the same
+names with the same arguments, backed by hand-written sm_100a kernels in
+libfa_b200.so. There is no CPU or eager fallback: importing fails loudly if
+the compiled extension is missing.
+"""
+
+# The compiled extension links against libc10/libtorch, which are only on the
+# loader's path once torch itself has been imported.
+import torch as _torch  # noqa: F401
+
+from ._C import (  # noqa: F401
+    _decode_with_split,
+    choose_decode_split,
+    decode,
+    decode_partial,
+    head_dim,
+    merge_partials,
+    occupancy_report,
+    prefill,
+    take_device_error,
+)
+
+__all__ = [
+    "prefill",
+    "decode",
+    "head_dim",
+    "occupancy_report",
+    "choose_decode_split",
+    "decode_partial",
+    "merge_partials",
+    "take_device_error",
+]
+
+__version__ = "2.0.0+b200"

@@ -1,0 +1,146 @@
+/*
+ * fa_b200.h — C ABI of the B200 (sm_100a) head_dim-64 fp16 attention forward.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * passed as void*. No entry point allocates memory, synchronises the stream
+ * or touches a framework type; the Python package (flashattn_cuda._C) and any
+ * other host language bind these symbols directly.
+ *
+ * Tensor layout (identical to the reference's pybind contract): every
+ * q/k/v/o/cache tensor is a contiguous (B, H, rows, 64) fp16 array; row r of
+ * head (b, h) starts at element ((b * H + h) * rows + r) * 64.
+ *
+ * Return value of every int-returning call: FA_OK (0) or one FA_E* code;
+ * fa_status_string() names it. Argument errors are detected on the host
+ * before anything is launched.
+ */
+#ifndef FA_B200_H_
+#define FA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes returned by the entry points. */
+#define FA_OK 0
+#define FA_EINVAL 1     /* bad size, count or scale                      */
+#define FA_EALIGN 2     /* a pointer is not 16-byte aligned              */
+#define FA_ECUDA 3      /* a CUDA runtime call or the launch failed      */
+#define FA_ENOSPACE 4   /* caller's workspace is smaller than required   */
+#define FA_EDEVICE 5    /* device is not sm_100 / driver entry missing   */
+
+/* Bits of the device-side error word (fa_take_device_error). */
+#define FA_ERR_TIMEOUT 1u   /* a pipeline wait exceeded its time limit   */
+#define FA_ERR_SMEM_ALIGN 2u /* dynamic shared memory was not 1 KiB aligned */
+
+/* head_dim every kernel is built for (reference flash_common.h:11). */
+#define FA_HEAD_DIM 64
+
+/*
+ * Full-sequence attention forward, O = softmax(scale * Q K^T [+ causal mask]) V.
+ * q, k, v, o: (B, H, N, 64) fp16 device arrays, 16-byte aligned; o is written.
+ * causal != 0 masks key j > query i (same-length top-left causal mask).
+ * Replaces the reference's prefill()/launch_prefill
+ * (csrc/bindings.cpp:10-27, csrc/prefill.cu:347-373).
+ */
+int fa_prefill(const void *q, const void *k, const void *v, void *o, int B,
+               int H, int N, int causal, float scale, void *stream);
+
+/*
+ * Bytes of scratch memory fa_decode needs for this shape and split choice.
+ * split_size <= 0 selects the automatic, length-balanced schedule.
+ * Reference counterpart: the per-call partial_acc/partial_ml allocation in
+ * launch_decode (csrc/decode.cu:213-219), hoisted to the caller.
+ */
+size_t fa_decode_workspace_bytes(int B, int H, int S_max, int split_size,
+                                 int device);
+
+/*
+ * Single-query attention against a KV cache (the decode step).
+ * q, o: (B, H, 1, 64) fp16; k_cache, v_cache: (B, H, S_max, 64) fp16;
+ * seq_lens: (B,) int32 device array, sequence b attends cache rows
+ * [0, min(seq_lens[b], S_max)); a sequence with no rows gets an all-zero output.
+ * split_size <= 0: automatic schedule; > 0: each CTA reduces at most
+ * split_size cache rows (the reference's forced split, must be a multiple
+ * of 4 as in the reference).
+ * workspace: device scratch of at least fa_decode_workspace_bytes() bytes
+ * whose first use on a device must be zero-filled; every call leaves it
+ * ready for the next call (calls sharing one workspace must be ordered on
+ * one stream).
+ * Replaces decode()/_decode_with_split()/launch_decode
+ * (csrc/bindings.cpp:36-76,127-129, csrc/decode.cu:194-240).
+ */
+int fa_decode(const void *q, const void *k_cache, const void *v_cache,
+              const int32_t *seq_lens, void *o, int B, int H, int S_max,
+              float scale, int split_size, void *workspace,
+              size_t workspace_bytes, void *stream);
+
+/*
+ * Decode that stops before normalisation and writes, per (b, h), the
+ * log-sum-exp partial {m, l, pad, pad, acc[64]} as 68 fp32 (m in log2 units
+ * of scale*q.k; acc unnormalised). Used when the KV cache of one sequence is
+ * sharded over GPUs: each GPU reduces its chunk, the partials are exchanged,
+ * and fa_merge_partials finishes. No reference counterpart: the reference
+ * has no multi-GPU path; the partial layout is its decode.cu:215-219
+ * (m, l, acc) triple.
+ */
+int fa_decode_partial(const void *q, const void *k_cache, const void *v_cache,
+                      const int32_t *seq_lens, float *partial_out, int B,
+                      int H, int S_max, float scale, void *workspace,
+                      size_t workspace_bytes, void *stream);
+
+/*
+ * Log-sum-exp merge of G partial sets laid out (G, B, H, 68) fp32 into the
+ * fp16 output o (B, H, 1, 64). Partials with l <= 0 are skipped and a row
+ * with no keys anywhere is 0, as in the reference's merge pass
+ * (csrc/decode.cu:143-175).
+ */
+int fa_merge_partials(const float *partials, int G, void *o, int B, int H,
+                      void *stream);
+
+/*
+ * The reference's chunk-size rule: largest power of two in [128, 1024] with
+ * batch*heads*ceil(max_seq/chunk) >= min_blocks, else 128
+ * (csrc/decode.cu:183-192). Pure host function.
+ */
+int fa_choose_decode_split(int max_seq, int batch, int heads, int min_blocks);
+
+/* One row of the occupancy report (reference csrc/flash_common.h:31-38). */
+typedef struct fa_occupancy_entry {
+  char name[64];
+  int threads_per_block;
+  int registers_per_thread;
+  int shared_bytes_per_block;
+  int max_active_blocks_per_sm;
+  double theoretical_occupancy;
+} fa_occupancy_entry;
+
+/*
+ * Fills up to max_entries rows for every kernel at its launch configuration
+ * on the current device; *count receives the number of kernels.
+ * Replaces occupancy_report() (csrc/bindings.cpp:80-97).
+ */
+int fa_occupancy(fa_occupancy_entry *out, int max_entries, int *count);
+
+/*
+ * Reads and clears the device-side error word of the current device
+ * (FA_ERR_* bits, 0 when every kernel completed normally). Synchronises
+ * the device. No reference counterpart: the reference kernels have no
+ * bounded waits.
+ */
+int fa_take_device_error(unsigned int *bits);
+
+/* Name of a status code. */
+const char *fa_status_string(int status);
+
+/* Number of SMs of the current device (0 on failure). */
+int fa_num_sms(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FA_B200_H_ */
