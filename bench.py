@@ -1,0 +1,495 @@
+"""Benchmark of the B200 head_dim-64 attention forward (driver contract).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline (one JSON line on rank 0): BASELINE config 3, the Qwen2.5-0.5B-shaped
+causal prefill B=4, H=14, N=4096, d=64, fp16, sharded by (batch, head) over
+the N GPUs (fixed total work: strong scaling). A "step" is one prefill of the
+rank's share of the 56 heads. `value` is whole-job TFLOP/s (FLOPs 4*B*H*N^2*d,
+halved for causal, as the reference's run_bench.py counts them).
+
+Secondary measurements in the same line (`secondary`):
+  c2_causal / c2_full  GPT-2-small prefill B=8 H=12 N=1024 (config 2)
+  c4_decode            ragged decode B=64 H=12 cap 8192, lengths U[1,8192],
+                       batch sharded over ranks balanced by length
+  c5_decode            long decode B=1 H=14 S=131072; KV sequence-sharded over
+                       ranks, per-rank log-sum-exp partials all-gathered with
+                       NCCL and merged
+Decode GB/s counts valid K+V rows only (128 B per row each for K and V).
+
+`--impl reference` times the reference's CPU path (src/attention_cpu.py,
+restated in oracle/oracle.py) on a bounded sample of the same workload on the
+host cores; under torchrun only rank 0 runs it.
+"""
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(REPO, "flash-attention-cuda_b200")
+ORACLE_DIR = os.path.join(REPO, "oracle")
+PROFILES = os.path.join(REPO, "profiles")
+
+HEAD_DIM = 64
+SCALE = 1.0 / math.sqrt(HEAD_DIM)
+C3 = dict(B=4, H=14, N=4096, causal=True)
+C2 = dict(B=8, H=12, N=1024)
+C4 = dict(B=64, H=12, cap=8192)
+C5 = dict(B=1, H=14, S=131072)
+L2_FLUSH_BYTES = 512 << 20  # > 126 MB L2
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0,
+                  "bf16_tflops_sustained": 1400.0}
+
+
+def prefill_flops(b, h, n, causal):
+    f = 4.0 * b * h * n * n * HEAD_DIM
+    return f * 0.5 if causal else f
+
+
+def load_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return p, "measured"
+    except Exception:
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def read_profile_traffic(name):
+    """Per-launch DRAM bytes of a kernel from a committed ncu summary line
+    `traffic_bytes_per_launch: <int>` in profiles/<name>.md (None if absent)."""
+    path = os.path.join(PROFILES, name + ".md")
+    try:
+        for line in open(path):
+            if line.strip().startswith("traffic_bytes_per_launch:"):
+                return int(float(line.split(":", 1)[1].strip()))
+    except Exception:
+        pass
+    return None
+
+
+def shard_range(total, world, rank):
+    base, rem = divmod(total, world)
+    start = rank * base + min(rank, rem)
+    return start, start + base + (1 if rank < rem else 0)
+
+
+def lpt_partition(weights, world):
+    """Longest-processing-time assignment of items to `world` bins."""
+    order = sorted(range(len(weights)), key=lambda i: -weights[i])
+    loads = [0] * world
+    bins = [[] for _ in range(world)]
+    for i in order:
+        r = min(range(world), key=lambda j: loads[j])
+        bins[r].append(i)
+        loads[r] += weights[i]
+    return [sorted(b) for b in bins]
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling (NVML) during the timed regions
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting",
+        0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x10: "sync_boost",
+        0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index, interval=0.005):
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._interval = interval
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(
+                self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nvml = None
+
+    def _run(self):
+        n = self._nvml
+        while not self._stop.is_set():
+            try:
+                util = n.nvmlDeviceGetUtilizationRates(self._h).gpu
+                mhz = n.nvmlDeviceGetClockInfo(self._h, n.NVML_CLOCK_SM)
+                r = n.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.samples.append((mhz, util, r))
+            except Exception:
+                pass
+            time.sleep(self._interval)
+
+    def __enter__(self):
+        if self._nvml:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread:
+            self._thread.join()
+
+    def summary(self):
+        busy = [s for s in self.samples if s[1] > 0] or self.samples
+        reasons = set()
+        for _, _, r in busy:
+            for bit, name in self.REASONS.items():
+                if r & bit and name != "gpu_idle":
+                    reasons.add(name)
+        return {
+            "sm_mhz": statistics.median(s[0] for s in busy) if busy else None,
+            "sm_max_mhz": self.max_mhz,
+            "reasons": sorted(reasons),
+            "samples": len(busy),
+        }
+
+
+# ---------------------------------------------------------------------------
+# Timing helpers (CUDA events on the launching stream)
+# ---------------------------------------------------------------------------
+class Timer:
+    def __init__(self, torch, dist, world):
+        self.torch = torch
+        self.dist = dist
+        self.world = world
+        self.flush_buf = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8,
+                                     device="cuda")
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+
+    def max_over_ranks(self, x):
+        if self.world == 1:
+            return x
+        t = self.torch.tensor([x], dtype=self.torch.float64, device="cuda")
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def run(self, fn, steps, warmup, flush=True):
+        """Total device time of `steps` calls of fn (ms), L2 flushed before
+        each call (outside the event pair), max over ranks."""
+        torch = self.torch
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        self.barrier()
+        torch.cuda.synchronize()
+        evs = []
+        for _ in range(steps):
+            if flush:
+                self.flush_buf.zero_()
+            s = torch.cuda.Event(enable_timing=True)
+            e = torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            evs.append((s, e))
+        torch.cuda.synchronize()
+        self.barrier()
+        torch.cuda.synchronize()
+        total = sum(s.elapsed_time(e) for s, e in evs)
+        return self.max_over_ranks(total)
+
+
+# ---------------------------------------------------------------------------
+# Our arm
+# ---------------------------------------------------------------------------
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, PKG_DIR)
+    import flashattn_cuda as fa
+
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    peaks, peaks_src = load_peaks()
+    timer = Timer(torch, dist, world)
+    gen = torch.Generator(device="cuda")
+    launches = 0
+
+    def randn(*shape, seed):
+        gen.manual_seed(seed)
+        return torch.randn(*shape, generator=gen, device="cuda",
+                           dtype=torch.float16)
+
+    sampler = ClockSampler(local_rank)
+    with sampler:
+        # ---------------- headline: C3 causal prefill, heads sharded -------
+        bh = C3["B"] * C3["H"]
+        u0, u1 = shard_range(bh, world, rank)
+        units = u1 - u0
+        n = C3["N"]
+        q = randn(1, units, n, HEAD_DIM, seed=1000 + rank)
+        k = randn(1, units, n, HEAD_DIM, seed=2000 + rank)
+        v = randn(1, units, n, HEAD_DIM, seed=3000 + rank)
+        step = lambda: fa.prefill(q, k, v, True, SCALE)
+        total_ms = timer.run(step, args.steps, args.warmup)
+        launches += args.steps
+        ms = total_ms / args.steps
+        flops_total = prefill_flops(C3["B"], C3["H"], n, True)
+        value = flops_total / (ms * 1e-3) / 1e12
+        flops_rank = prefill_flops(1, units, n, True)
+        achieved = flops_rank / (ms * 1e-3) / 1e12  # this rank's kernel
+        peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+
+        # ---------------- e2e through the public API, host buffers -------
+        hq = q.cpu().pin_memory()
+        hk = k.cpu().pin_memory()
+        hv = v.cpu().pin_memory()
+        hout = torch.empty_like(hq).pin_memory()
+
+        def e2e_step():
+            dq = hq.to("cuda", non_blocking=True)
+            dk = hk.to("cuda", non_blocking=True)
+            dv = hv.to("cuda", non_blocking=True)
+            o = fa.prefill(dq, dk, dv, True, SCALE)
+            hout.copy_(o, non_blocking=True)
+
+        e2e_ms = timer.run(e2e_step, args.steps, args.warmup) / args.steps
+        launches += args.steps
+        h2d = 3 * hq.numel() * 2 * world
+        d2h = hq.numel() * 2 * world
+        del q, k, v
+
+        # ---------------- secondary: C2 prefill (replicated per rank) -----
+        secondary = {}
+        for causal in (True, False):
+            q2 = randn(C2["B"], C2["H"], C2["N"], HEAD_DIM, seed=11 + rank)
+            k2 = randn(C2["B"], C2["H"], C2["N"], HEAD_DIM, seed=12 + rank)
+            v2 = randn(C2["B"], C2["H"], C2["N"], HEAD_DIM, seed=13 + rank)
+            t = timer.run(lambda: fa.prefill(q2, k2, v2, causal, SCALE),
+                          args.steps, args.warmup) / args.steps
+            launches += args.steps
+            f = prefill_flops(C2["B"], C2["H"], C2["N"], causal)
+            secondary["c2_causal" if causal else "c2_full"] = {
+                "ms": round(t, 5), "tflops_per_gpu": round(f / (t * 1e-3) / 1e12, 2),
+                "frac_of_measured_bf16_peak": round(f / (t * 1e-3) / 1e12 / peak, 4),
+                "scaling": "replicated per GPU"}
+            del q2, k2, v2
+
+        # ---------------- secondary: C4 ragged decode ---------------------
+        g = torch.Generator().manual_seed(0)
+        all_lens = torch.randint(1, C4["cap"] + 1, (C4["B"],), generator=g,
+                                 dtype=torch.int32)
+        mine = lpt_partition(all_lens.tolist(), world)[rank]
+        lens = all_lens[mine].cuda()
+        bm = len(mine)
+        qd = randn(bm, C4["H"], 1, HEAD_DIM, seed=40 + rank)
+        kc = randn(bm, C4["H"], C4["cap"], HEAD_DIM, seed=41 + rank)
+        vc = randn(bm, C4["H"], C4["cap"], HEAD_DIM, seed=42 + rank)
+        t = timer.run(lambda: fa.decode(qd, kc, vc, lens, SCALE), args.steps,
+                      args.warmup) / args.steps
+        launches += args.steps
+        bytes_all = int(all_lens.sum()) * C4["H"] * HEAD_DIM * 2 * 2
+        bytes_rank = int(lens.sum()) * C4["H"] * HEAD_DIM * 2 * 2
+        hbm = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+        secondary["c4_decode"] = {
+            "ms": round(t, 5), "gbs_total": round(bytes_all / (t * 1e-3) / 1e9, 1),
+            "gbs_per_gpu_rank0": round(bytes_rank / (t * 1e-3) / 1e9, 1),
+            "frac_of_measured_hbm": round(bytes_rank / (t * 1e-3) / 1e9 / hbm, 4),
+            "tokens_per_s": round(C4["B"] / (t * 1e-3), 1),
+            "scaling": "strong (batch sharded, LPT by length)"}
+        del qd, kc, vc
+
+        # ---------------- secondary: C5 long decode, sequence-sharded ----
+        S = C5["S"]
+        c0, c1 = shard_range(S, world, rank)
+        qd = randn(1, C5["H"], 1, HEAD_DIM, seed=50)  # same q on every rank
+        kc = randn(1, C5["H"], c1 - c0, HEAD_DIM, seed=51 + rank)
+        vc = randn(1, C5["H"], c1 - c0, HEAD_DIM, seed=52 + rank)
+        lens_local = torch.tensor([c1 - c0], dtype=torch.int32, device="cuda")
+        gathered = torch.empty(world, 1, C5["H"], 68, device="cuda")
+
+        def c5_step():
+            if world == 1:
+                return fa.decode(qd, kc, vc, lens_local, SCALE)
+            part = fa.decode_partial(qd, kc, vc, lens_local, SCALE)
+            dist.all_gather_into_tensor(gathered, part)
+            return fa.merge_partials(gathered)
+
+        t = timer.run(c5_step, args.steps, args.warmup) / args.steps
+        launches += args.steps * (1 if world == 1 else 2)
+        b_total = S * C5["H"] * HEAD_DIM * 2 * 2
+        b_rank = (c1 - c0) * C5["H"] * HEAD_DIM * 2 * 2
+        secondary["c5_decode"] = {
+            "ms": round(t, 5), "gbs_total": round(b_total / (t * 1e-3) / 1e9, 1),
+            "frac_of_measured_hbm_per_gpu": round(
+                b_rank / (t * 1e-3) / 1e9 / hbm, 4),
+            "scaling": "strong (KV sequence sharded, NCCL all-gather of "
+                       "partials + merge)" if world > 1 else "single GPU"}
+        del qd, kc, vc
+
+    assert fa.take_device_error() == 0, "device-side error during the bench"
+    clocks = sampler.summary()
+
+    if rank != 0:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+
+    result = {
+        "metric": "causal prefill TFLOP/s (B=4,H=14,N=4096,d=64 fp16)",
+        "value": round(value, 2),
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 5),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "fp16 in, fp32 accumulate",
+        "data": "synthetic N(0,1) fp16, seeded",
+        "config": {"workload": "config3_qwen2.5-0.5b_causal_prefill",
+                   "global_batch": C3["B"], "heads": C3["H"], "seq_len": n,
+                   "head_dim": HEAD_DIM, "causal": True,
+                   "parallelism": f"batch*head sharded over {world} GPU(s)",
+                   "l2": "flushed (512 MiB write) before every timed step"},
+        "e2e": {"value": round(flops_total / (e2e_ms * 1e-3) / 1e12, 3),
+                "unit": "TFLOP/s", "ms_per_step": round(e2e_ms, 4),
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2),
+                     "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 4),
+                     "peak_source": f"{peaks_src} bf16 cuBLAS burst",
+                     "frac_of_nominal_2250": round(achieved / 2250.0, 4),
+                     "traffic": read_profile_traffic("prefill_kernel_c3")},
+        "gpu_launches": launches,
+        "clocks": clocks,
+        "secondary": secondary,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_budget)
+    print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# CPU path of the reference (numpy restatement in oracle/)
+# ---------------------------------------------------------------------------
+def cpu_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads", 1) for i in threadpool_info()
+             if i.get("user_api") == "blas"]
+        if n:
+            return max(n)
+    except Exception:
+        pass
+    return os.cpu_count() or 1
+
+
+def cpu_sample_heads(budget_s):
+    """Runs causal attention_cpu over C3 heads until `budget_s` elapses;
+    returns (heads done, seconds)."""
+    sys.path.insert(0, ORACLE_DIR)
+    import oracle
+
+    rng = np.random.default_rng(0)
+    n = C3["N"]
+    done, t_total = 0, 0.0
+    while t_total < budget_s or done == 0:
+        q, k, v = (rng.standard_normal((n, HEAD_DIM), dtype=np.float32)
+                   .astype(np.float16).astype(np.float32) for _ in range(3))
+        t0 = time.perf_counter()
+        oracle.attention_cpu(q, k, v, SCALE, causal=True)
+        t_total += time.perf_counter() - t0
+        done += 1
+    return done, t_total
+
+
+def cpu_baseline(budget_s):
+    heads, secs = cpu_sample_heads(budget_s)
+    flops = prefill_flops(1, heads, C3["N"], True)
+    return {"value": round(flops / secs / 1e12, 5), "unit": "TFLOP/s",
+            "cores": cpu_threads(), "kind": "port",
+            "sample": f"{heads} of the 56 (batch, head) causal N=4096 heads of "
+                      f"config 3 through the numpy restatement of "
+                      f"src/attention_cpu.py ({secs:.1f} s)"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    budget = max(1.0, args.cpu_budget / max(1, args.steps + args.warmup))
+    for _ in range(args.warmup):
+        cpu_sample_heads(budget)
+    heads_total, secs_total = 0, 0.0
+    for _ in range(args.steps):
+        h, s = cpu_sample_heads(budget)
+        heads_total += h
+        secs_total += s
+    flops = prefill_flops(1, heads_total, C3["N"], True)
+    value = flops / secs_total / 1e12
+    ms_per_step = prefill_flops(C3["B"], C3["H"], C3["N"], True) / (value * 1e12) * 1e3
+    result = {
+        "impl": "reference",
+        "metric": "causal prefill TFLOP/s (B=4,H=14,N=4096,d=64 fp16)",
+        "value": round(value, 5), "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 1), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None,
+        "dtype": "fp32 (numpy, inputs rounded to fp16)",
+        "data": "synthetic N(0,1), seeded",
+        "config": {"workload": "config3_qwen2.5-0.5b_causal_prefill",
+                   "global_batch": C3["B"], "heads": C3["H"],
+                   "seq_len": C3["N"], "head_dim": HEAD_DIM, "causal": True,
+                   "parallelism": "host CPU (rank 0 only)"},
+        "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s",
+                         "cores": cpu_threads(), "kind": "port",
+                         "sample": f"{heads_total} heads of config 3 over "
+                                   f"{args.steps} steps ({secs_total:.1f} s)"},
+        "e2e": {"value": round(value, 5), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(result), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-budget", type=float, default=12.0,
+                    help="seconds of CPU work for the CPU baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus if args.gpus else 1)))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if "RANK" not in os.environ:
+        world = 1
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

@@ -56,24 +56,36 @@ void *current_stream() {
   return static_cast<void *>(at::cuda::getCurrentCUDAStream().stream());
 }
 
-// Decode scratch, cached per (device, stream). fa_decode leaves its arrival
-// counters at zero after every call, so a buffer is zero-filled only when it
-// is (re)allocated; keying by stream keeps concurrent streams apart. The map
-// is intentionally never destroyed (no CUDA frees during interpreter exit).
-at::Tensor decode_workspace(const at::Tensor &like, size_t bytes) {
+// Decode scratch, cached per (device, stream): a partials buffer (no
+// initialisation needed) and an arrival-counter array that fa_decode leaves
+// at zero after every call, so it is zero-filled only when it is
+// (re)allocated. Keying by stream keeps concurrent streams apart. The map is
+// intentionally never destroyed (no CUDA frees during interpreter exit).
+struct DecodeScratch {
+  at::Tensor partials;  // uint8
+  at::Tensor counters;  // int32, zero between calls
+};
+
+DecodeScratch &decode_scratch(const at::Tensor &like, size_t partial_bytes,
+                              size_t n_counters) {
   static std::mutex mu;
-  static auto *cache = new std::unordered_map<uint64_t, at::Tensor>();
+  static auto *cache = new std::unordered_map<uint64_t, DecodeScratch>();
   const auto stream = at::cuda::getCurrentCUDAStream();
   const uint64_t key = (static_cast<uint64_t>(like.get_device()) << 56) ^
                        static_cast<uint64_t>(stream.id());
   std::lock_guard<std::mutex> lock(mu);
-  auto it = cache->find(key);
-  if (it != cache->end() && static_cast<size_t>(it->second.numel()) >= bytes)
-    return it->second;
-  at::Tensor ws = at::zeros({static_cast<int64_t>(bytes)},
-                            like.options().dtype(at::kByte));
-  (*cache)[key] = ws;
-  return ws;
+  DecodeScratch &s = (*cache)[key];
+  if (!s.partials.defined() ||
+      static_cast<size_t>(s.partials.numel()) < partial_bytes) {
+    s.partials = at::empty({static_cast<int64_t>(partial_bytes)},
+                           like.options().dtype(at::kByte));
+  }
+  if (!s.counters.defined() ||
+      static_cast<size_t>(s.counters.numel()) < n_counters) {
+    s.counters = at::zeros({static_cast<int64_t>(n_counters)},
+                           like.options().dtype(at::kInt));
+  }
+  return s;
 }
 
 void check_decode_inputs(const at::Tensor &q, const at::Tensor &k_cache,
@@ -151,12 +163,15 @@ at::Tensor decode_impl(const at::Tensor &q, const at::Tensor &k_cache,
   const size_t bytes =
       fa_decode_workspace_bytes(B, H, S, split, q.get_device());
   TORCH_CHECK(bytes > 0, "fa_decode_workspace_bytes failed");
-  at::Tensor ws = decode_workspace(q, bytes);
-  check_status(fa_decode(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
-                         seq_lens.data_ptr<int32_t>(), o.data_ptr(), B, H, S,
-                         static_cast<float>(scale), split, ws.data_ptr(),
-                         static_cast<size_t>(ws.numel()), current_stream()),
-               "fa_decode");
+  DecodeScratch &ws = decode_scratch(q, bytes, static_cast<size_t>(B) * H);
+  check_status(
+      fa_decode(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                seq_lens.data_ptr<int32_t>(), o.data_ptr(), B, H, S,
+                static_cast<float>(scale), split, ws.partials.data_ptr(),
+                static_cast<size_t>(ws.partials.numel()),
+                reinterpret_cast<uint32_t *>(ws.counters.data_ptr<int32_t>()),
+                static_cast<size_t>(ws.counters.numel()), current_stream()),
+      "fa_decode");
   return o;
 }
 
@@ -179,12 +194,15 @@ at::Tensor decode_partial(const at::Tensor &q, const at::Tensor &k_cache,
   at::Tensor part = at::empty({B, H, 68}, q.options().dtype(at::kFloat));
   const size_t bytes = fa_decode_workspace_bytes(B, H, S, 0, q.get_device());
   TORCH_CHECK(bytes > 0, "fa_decode_workspace_bytes failed");
-  at::Tensor ws = decode_workspace(q, bytes);
+  DecodeScratch &ws = decode_scratch(q, bytes, static_cast<size_t>(B) * H);
   check_status(
-      fa_decode_partial(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
-                        seq_lens.data_ptr<int32_t>(), part.data_ptr<float>(), B,
-                        H, S, static_cast<float>(scale), ws.data_ptr(),
-                        static_cast<size_t>(ws.numel()), current_stream()),
+      fa_decode_partial(
+          q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+          seq_lens.data_ptr<int32_t>(), part.data_ptr<float>(), B, H, S,
+          static_cast<float>(scale), ws.partials.data_ptr(),
+          static_cast<size_t>(ws.partials.numel()),
+          reinterpret_cast<uint32_t *>(ws.counters.data_ptr<int32_t>()),
+          static_cast<size_t>(ws.counters.numel()), current_stream()),
       "fa_decode_partial");
   return part;
 }

@@ -75,7 +75,15 @@ int ensure_device(int *device_out) {
                            prefill_smem_bytes()) != cudaSuccess ||
       cudaFuncSetAttribute(decode_kernel_ptr(),
                            cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           decode_smem_bytes()) != cudaSuccess) {
+                           decode_smem_bytes()) != cudaSuccess ||
+      // Both kernels are sized for two CTAs per SM, which needs the whole
+      // unified L1/shared array configured as shared memory.
+      cudaFuncSetAttribute(prefill_kernel_ptr(),
+                           cudaFuncAttributePreferredSharedMemoryCarveout,
+                           cudaSharedmemCarveoutMaxShared) != cudaSuccess ||
+      cudaFuncSetAttribute(decode_kernel_ptr(),
+                           cudaFuncAttributePreferredSharedMemoryCarveout,
+                           cudaSharedmemCarveoutMaxShared) != cudaSuccess) {
     st.status = FA_ECUDA;
     return st.status;
   }
@@ -130,10 +138,7 @@ int decode_grid(int sms, int B, int H, int S_max, int split_size) {
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 size_t workspace_bytes_for(int B, int H, int grid) {
-  const size_t counters = align_up(static_cast<size_t>(B) * H * 4, 256);
-  const size_t partials = (static_cast<size_t>(B) * H + grid) *
-                          kPartialFloats * sizeof(float);
-  return counters + partials;
+  return (static_cast<size_t>(B) * H + grid) * kPartialFloats * sizeof(float);
 }
 
 bool decode_shape_ok(int B, int H, int S_max, float scale) {
@@ -145,21 +150,25 @@ bool decode_shape_ok(int B, int H, int S_max, float scale) {
 int run_decode(const void *q, const void *k_cache, const void *v_cache,
                const int32_t *seq_lens, void *o, float *partial_out, int B,
                int H, int S_max, float scale, int split_size, void *workspace,
-               size_t workspace_bytes, void *stream) {
+               size_t workspace_bytes, uint32_t *counters,
+               size_t counter_count, void *stream) {
   if (!decode_shape_ok(B, H, S_max, scale)) return FA_EINVAL;
   if (split_size > 0 && split_size % 4 != 0) return FA_EINVAL;
   if (!q || !k_cache || !v_cache || !seq_lens || (!o && !partial_out) ||
-      !workspace)
+      !workspace || !counters)
     return FA_EINVAL;
   if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) ||
       (o && !aligned16(o)) || (partial_out && !aligned16(partial_out)) ||
-      !aligned16(workspace) || (reinterpret_cast<uintptr_t>(seq_lens) & 3u))
+      !aligned16(workspace) || (reinterpret_cast<uintptr_t>(seq_lens) & 3u) ||
+      (reinterpret_cast<uintptr_t>(counters) & 3u))
     return FA_EALIGN;
   int dev = 0;
   int rc = ensure_device(&dev);
   if (rc != FA_OK) return rc;
   const int grid = decode_grid(g_devices[dev].sms, B, H, S_max, split_size);
-  if (workspace_bytes < workspace_bytes_for(B, H, grid)) return FA_ENOSPACE;
+  if (workspace_bytes < workspace_bytes_for(B, H, grid) ||
+      counter_count < static_cast<size_t>(B) * H)
+    return FA_ENOSPACE;
   DecodeArgs a;
   a.q = static_cast<const __half *>(q);
   a.k = static_cast<const __half *>(k_cache);
@@ -167,10 +176,8 @@ int run_decode(const void *q, const void *k_cache, const void *v_cache,
   a.seq_lens = seq_lens;
   a.out = static_cast<__half *>(o);
   a.partial_out = partial_out;
-  uint8_t *ws = static_cast<uint8_t *>(workspace);
-  a.ws_counters = reinterpret_cast<uint32_t *>(ws);
-  a.ws_partials = reinterpret_cast<float *>(
-      ws + align_up(static_cast<size_t>(B) * H * 4, 256));
+  a.ws_counters = counters;
+  a.ws_partials = static_cast<float *>(workspace);
   a.B = B;
   a.H = H;
   a.S_max = S_max;
@@ -226,19 +233,23 @@ size_t fa_decode_workspace_bytes(int B, int H, int S_max, int split_size,
 int fa_decode(const void *q, const void *k_cache, const void *v_cache,
               const int32_t *seq_lens, void *o, int B, int H, int S_max,
               float scale, int split_size, void *workspace,
-              size_t workspace_bytes, void *stream) {
+              size_t workspace_bytes, uint32_t *counters,
+              size_t counter_count, void *stream) {
   if (!o) return FA_EINVAL;
   return run_decode(q, k_cache, v_cache, seq_lens, o, nullptr, B, H, S_max,
-                    scale, split_size, workspace, workspace_bytes, stream);
+                    scale, split_size, workspace, workspace_bytes, counters,
+                    counter_count, stream);
 }
 
 int fa_decode_partial(const void *q, const void *k_cache, const void *v_cache,
                       const int32_t *seq_lens, float *partial_out, int B,
                       int H, int S_max, float scale, void *workspace,
-                      size_t workspace_bytes, void *stream) {
+                      size_t workspace_bytes, uint32_t *counters,
+                      size_t counter_count, void *stream) {
   if (!partial_out) return FA_EINVAL;
   return run_decode(q, k_cache, v_cache, seq_lens, nullptr, partial_out, B, H,
-                    S_max, scale, 0, workspace, workspace_bytes, stream);
+                    S_max, scale, 0, workspace, workspace_bytes, counters,
+                    counter_count, stream);
 }
 
 int fa_merge_partials(const float *partials, int G, void *o, int B, int H,

@@ -50,10 +50,12 @@ int fa_prefill(const void *q, const void *k, const void *v, void *o, int B,
                int H, int N, int causal, float scale, void *stream);
 
 /*
- * Bytes of scratch memory fa_decode needs for this shape and split choice.
- * split_size <= 0 selects the automatic, length-balanced schedule.
- * Reference counterpart: the per-call partial_acc/partial_ml allocation in
- * launch_decode (csrc/decode.cu:213-219), hoisted to the caller.
+ * Bytes of scratch memory fa_decode / fa_decode_partial need for this shape
+ * and split choice (the log-sum-exp partials of segments split across CTAs).
+ * It needs no initialisation. split_size <= 0 selects the automatic,
+ * length-balanced schedule. Reference counterpart: the per-call
+ * partial_acc/partial_ml allocation in launch_decode
+ * (csrc/decode.cu:213-219), hoisted to the caller.
  */
 size_t fa_decode_workspace_bytes(int B, int H, int S_max, int split_size,
                                  int device);
@@ -66,17 +68,20 @@ size_t fa_decode_workspace_bytes(int B, int H, int S_max, int split_size,
  * split_size <= 0: automatic schedule; > 0: each CTA reduces at most
  * split_size cache rows (the reference's forced split, must be a multiple
  * of 4 as in the reference).
- * workspace: device scratch of at least fa_decode_workspace_bytes() bytes
- * whose first use on a device must be zero-filled; every call leaves it
- * ready for the next call (calls sharing one workspace must be ordered on
- * one stream).
+ * workspace: device scratch of at least fa_decode_workspace_bytes() bytes.
+ * counters: device array of at least B*H uint32 that is zero before the
+ * first call; every completed call leaves it zero again, so one array can
+ * serve any sequence of calls and shapes (calls sharing workspace or
+ * counters must be ordered on one stream; after a device error reported by
+ * fa_take_device_error, zero it again).
  * Replaces decode()/_decode_with_split()/launch_decode
  * (csrc/bindings.cpp:36-76,127-129, csrc/decode.cu:194-240).
  */
 int fa_decode(const void *q, const void *k_cache, const void *v_cache,
               const int32_t *seq_lens, void *o, int B, int H, int S_max,
               float scale, int split_size, void *workspace,
-              size_t workspace_bytes, void *stream);
+              size_t workspace_bytes, uint32_t *counters,
+              size_t counter_count, void *stream);
 
 /*
  * Decode that stops before normalisation and writes, per (b, h), the
@@ -90,7 +95,8 @@ int fa_decode(const void *q, const void *k_cache, const void *v_cache,
 int fa_decode_partial(const void *q, const void *k_cache, const void *v_cache,
                       const int32_t *seq_lens, float *partial_out, int B,
                       int H, int S_max, float scale, void *workspace,
-                      size_t workspace_bytes, void *stream);
+                      size_t workspace_bytes, uint32_t *counters,
+                      size_t counter_count, void *stream);
 
 /*
  * Log-sum-exp merge of G partial sets laid out (G, B, H, 68) fp32 into the

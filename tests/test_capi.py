@@ -33,7 +33,7 @@ def lib():
                                ctypes.c_int, ctypes.c_int, ctypes.c_float, vp]
     lib.fa_decode.argtypes = [vp, vp, vp, vp, vp, ctypes.c_int, ctypes.c_int,
                               ctypes.c_int, ctypes.c_float, ctypes.c_int, vp,
-                              ctypes.c_size_t, vp]
+                              ctypes.c_size_t, vp, ctypes.c_size_t, vp]
     lib.fa_merge_partials.argtypes = [vp, ctypes.c_int, vp, ctypes.c_int,
                                       ctypes.c_int, vp]
     return lib
@@ -112,11 +112,13 @@ def test_argument_errors_are_reported_before_any_launch(lib):
     odd = ctypes.c_void_p(4096 + 8)
     assert lib.fa_prefill(p, odd, p, p, 1, 1, 8, 0, 0.125, None) == FA_EALIGN
     # decode: split must be a multiple of 4 (reference decode.cu:209-211)
-    assert lib.fa_decode(p, p, p, p, p, 1, 1, 8, 0.125, 6, p, 1 << 20,
+    assert lib.fa_decode(p, p, p, p, p, 1, 1, 8, 0.125, 6, p, 1 << 20, p, 1,
                          None) == FA_EINVAL
-    assert lib.fa_decode(p, p, p, p, p, 1, 0, 8, 0.125, 0, p, 1 << 20,
+    assert lib.fa_decode(p, p, p, p, p, 1, 0, 8, 0.125, 0, p, 1 << 20, p, 1,
                          None) == FA_EINVAL
-    assert lib.fa_decode(p, p, p, p, None, 1, 1, 8, 0.125, 0, p, 1 << 20,
+    assert lib.fa_decode(p, p, p, p, None, 1, 1, 8, 0.125, 0, p, 1 << 20, p, 1,
+                         None) == FA_EINVAL
+    assert lib.fa_decode(p, p, p, p, p, 1, 1, 8, 0.125, 0, p, 1 << 20, None, 1,
                          None) == FA_EINVAL
     assert lib.fa_merge_partials(p, 0, p, 1, 1, None) == FA_EINVAL
 

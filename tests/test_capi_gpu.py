@@ -27,7 +27,7 @@ def lib():
                                ctypes.c_int, ctypes.c_int, ctypes.c_float, vp]
     lib.fa_decode.argtypes = [vp, vp, vp, vp, vp, ctypes.c_int, ctypes.c_int,
                               ctypes.c_int, ctypes.c_float, ctypes.c_int, vp,
-                              ctypes.c_size_t, vp]
+                              ctypes.c_size_t, vp, ctypes.c_size_t, vp]
     lib.fa_decode_workspace_bytes.argtypes = [ctypes.c_int] * 5
     lib.fa_decode_workspace_bytes.restype = ctypes.c_size_t
     lib.fa_take_device_error.argtypes = [ctypes.POINTER(ctypes.c_uint)]
@@ -60,28 +60,36 @@ def test_capi_prefill_matches_oracle(lib):
 
 
 def test_capi_decode_workspace_reuse(lib):
-    """The same zero-initialised workspace serves consecutive calls: the
-    kernel leaves its arrival counters at zero."""
+    """One zero-initialised counter array and one workspace serve consecutive
+    calls of different shapes: the kernel leaves its counters at zero."""
     torch.manual_seed(1)
-    B, H, S = 3, 4, 5000
-    q = torch.randn(B, H, 1, 64, device="cuda").half()
-    k = torch.randn(B, H, S, 64, device="cuda").half()
-    v = torch.randn(B, H, S, 64, device="cuda").half()
-    nbytes = lib.fa_decode_workspace_bytes(B, H, S, 0, 0)
-    assert nbytes > 0
-    ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
-    # too small a workspace is refused
-    assert lib.fa_decode(_ptr(q), _ptr(k), _ptr(v), _ptr(q), _ptr(q), B, H, S,
-                         SCALE, 0, _ptr(ws), nbytes - 1, _stream()) == 4
-    for lens in ([5000, 1, 2500], [17, 4999, 0], [5000, 5000, 5000]):
+    nbytes = lib.fa_decode_workspace_bytes(64, 16, 5000, 4, 0)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    ctr = torch.zeros(64 * 16, dtype=torch.int32, device="cuda")
+    cases = [(3, 4, 5000, [5000, 1, 2500], 0), (3, 4, 5000, [17, 4999, 0], 8),
+             (2, 16, 900, [900, 450], 0), (3, 4, 5000, [5000] * 3, 0),
+             (5, 2, 700, [1, 2, 3, 699, 700], 4)]
+    for B, H, S, lens, split in cases:
+        q = torch.randn(B, H, 1, 64, device="cuda").half()
+        k = torch.randn(B, H, S, 64, device="cuda").half()
+        v = torch.randn(B, H, S, 64, device="cuda").half()
+        need = lib.fa_decode_workspace_bytes(B, H, S, split, 0)
+        assert 0 < need <= nbytes
         t = torch.tensor(lens, dtype=torch.int32, device="cuda")
         o = torch.full_like(q, float("nan"))
+        # too small a workspace or counter array is refused
+        assert lib.fa_decode(_ptr(q), _ptr(k), _ptr(v), _ptr(t), _ptr(o), B, H,
+                             S, SCALE, split, _ptr(ws), need - 1, _ptr(ctr),
+                             B * H, _stream()) == 4
+        assert lib.fa_decode(_ptr(q), _ptr(k), _ptr(v), _ptr(t), _ptr(o), B, H,
+                             S, SCALE, split, _ptr(ws), need, _ptr(ctr),
+                             B * H - 1, _stream()) == 4
         rc = lib.fa_decode(_ptr(q), _ptr(k), _ptr(v), _ptr(t), _ptr(o), B, H, S,
-                           SCALE, 0, _ptr(ws), nbytes, _stream())
+                           SCALE, split, _ptr(ws), need, _ptr(ctr), ctr.numel(),
+                           _stream())
         assert rc == 0
         torch.cuda.synchronize()
         ref = oracle.decode_c(q.float().cpu().numpy(), k.float().cpu().numpy(),
                               v.float().cpu().numpy(), np.array(lens), SCALE)
         assert np.abs(o.float().cpu().numpy() - ref).max() <= 2e-3
-    counters = ws[: B * H * 4].view(torch.int32)
-    assert int(counters.abs().sum()) == 0
+        assert int(ctr.abs().sum()) == 0
