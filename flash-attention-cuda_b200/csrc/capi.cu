@@ -343,6 +343,17 @@ const char *fa_status_string(int status) {
   }
 }
 
+#ifdef FA_TRACE
+// Copies the pipeline trace stamps (profiling builds only).
+int fa_trace_read(unsigned long long *dst, size_t n) {
+  if (n > sizeof(g_fa_trace) / sizeof(g_fa_trace[0])) return FA_EINVAL;
+  cudaDeviceSynchronize();
+  return cudaMemcpyFromSymbol(dst, g_fa_trace, n * sizeof(*dst)) == cudaSuccess
+             ? FA_OK
+             : FA_ECUDA;
+}
+#endif
+
 int fa_num_sms(void) {
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;

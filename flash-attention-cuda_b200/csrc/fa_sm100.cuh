@@ -44,6 +44,20 @@ __device__ __forceinline__ bool device_failed() {
           FA_ERR_TIMEOUT) != 0;
 }
 
+// Optional cycle-stamp tracing of the pipeline (profiling builds only,
+// compiled with -DFA_TRACE): the first 4 CTAs record clock64() at fixed slots.
+#ifdef FA_TRACE
+__device__ unsigned long long g_fa_trace[4 * 4096];
+#define FA_TRACE_EVENT(slot)                                           \
+  do {                                                                 \
+    if (blockIdx.x < 4) g_fa_trace[blockIdx.x * 4096 + (slot)] = clock64(); \
+  } while (0)
+#else
+#define FA_TRACE_EVENT(slot) \
+  do {                       \
+  } while (0)
+#endif
+
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -206,6 +220,20 @@ __device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc,
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]^T, kind::f16: A (M x K, 16-bit) is read from
+// tensor memory, lane = row, two elements per 32-bit column.
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem,
+                                          uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(
+          d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrives once on `bar` when every tcgen05 operation this thread issued so far
 // has completed.
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
@@ -295,6 +323,51 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Blackwell packed fp32 pair arithmetic (one instruction for two lanes of
+// work) and the three-input max.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  return __ffma2_rn(a, b, c);
+}
+
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  return __fadd2_rn(a, b);
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for two values on the FMA/ALU pipes instead of the MUFU unit.
+// Cody-Waite style range reduction: x = j + f with j = round(x) and
+// |f| <= 1/2, where j comes from the "add 1.5 * 2^23" rounding trick (the
+// integer lands in the low mantissa bits of t). 2^f is a degree-3 polynomial
+// whose coefficients were fit for this project by iteratively reweighted
+// least squares toward the minimax relative error on [-1/2, 1/2]
+// (max relative error 7.5e-5, below half an fp16 ulp, which is all the
+// result needs: it becomes an fp16 P entry). Finally j is added to the
+// exponent field. Inputs below -125 are clamped (the result is then ~0).
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  constexpr float kC0 = 0.99992806f;
+  constexpr float kC1 = 0.69326097f;
+  constexpr float kC2 = 0.24261113f;
+  constexpr float kC3 = 0.05517166f;
+  x.x = fmaxf(x.x, -125.f);
+  x.y = fmaxf(x.y, -125.f);
+  const float2 t = fadd2(x, make_float2(kRound, kRound));
+  const float2 r = fadd2(t, make_float2(-kRound, -kRound));
+  const float2 f = ffma2(r, make_float2(-1.f, -1.f), x);
+  float2 p = ffma2(make_float2(kC3, kC3), f, make_float2(kC2, kC2));
+  p = ffma2(p, f, make_float2(kC1, kC1));
+  p = ffma2(p, f, make_float2(kC0, kC0));
+  float2 out;
+  out.x = __uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23));
+  out.y = __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23));
+  return out;
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t *>(&h);
@@ -314,6 +387,28 @@ __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "r"(addr));
   return v;
+}
+
+// Per-warpgroup register reallocation (all four warps of a warpgroup must
+// execute the same one).
+template <int kRegs>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+template <int kRegs>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+
+// True in exactly one lane of a fully active warp.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "elect.sync _|P, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
 }
 
 // Named barrier over a subset of the CTA's warps.

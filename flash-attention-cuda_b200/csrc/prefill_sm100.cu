@@ -5,28 +5,30 @@
 // O = softmax(scale * Q K^T, causal mask k <= q) V per (batch, head), with
 // fully-masked causal key tiles skipped. The implementation is a different
 // machine: QK^T and PV run on the 5th-generation tensor cores (tcgen05.mma,
-// fp32 accumulators in tensor memory), Q/K/V tiles arrive by TMA into a
-// two-stage mbarrier ring, and the online softmax runs in registers of four
-// dedicated warps that read S straight out of tensor memory.
+// fp32 accumulators in tensor memory), Q/K/V tiles arrive by TMA into an
+// mbarrier ring, and the online softmax runs in registers of dedicated warps
+// that read S straight out of tensor memory and write P back into it.
 //
-// CTA = 6 warps, one 128-row query tile of one (batch, head):
-//   warps 0-3  softmax: thread t owns query row t (= TMEM lane t). Reads S,
-//              applies mask / running max / exp2 / row sum, writes P (fp16)
-//              into shared memory, rescales O in TMEM when the max moved.
-//   warp 4     TMA producer: Q once, then K_j, V_j per 128-key tile.
-//   warp 5     MMA issuer (one thread): S_j = Q K_j^T, O += P_j V_j.
-// Two CTAs share an SM (112 KiB shared memory and 256 TMEM columns each), so
-// one CTA's softmax overlaps the other's tensor-core work; inside a CTA, S_{j+1}
-// is computed while the softmax warps exponentiate S_j.
+// A kernel that allocates tensor memory runs one CTA per SM, so overlap is
+// built inside the CTA: it owns two 128-row query tiles of one (batch, head)
+// (rows [256*i, 256*i + 256)) and ping-pongs them. While one softmax
+// warpgroup exponentiates its S tile, the tensor core computes the other
+// tile's S or PV. Both tiles share every K/V tile loaded.
 //
-// Shared memory (1 KiB aligned, every tile in the 128-byte-swizzled layout
-// the TMA writes and the MMA descriptors describe):
-//   Q  [128 rows x 128 B]            16 KiB
-//   K  2 stages x [128 keys x 128 B] 32 KiB
-//   V  2 stages x [128 keys x 128 B] 32 KiB
-//   P  2 halves x [128 rows x 64 keys x 2 B] 32 KiB  (keys 0-63, 64-127)
+// CTA = 10 warps (320 threads):
+//   warps 0-3  softmax of query tile 0 (thread = row = TMEM lane)
+//   warps 4-7  softmax of query tile 1
+//   warp 8     TMA producer: Q tiles once, then K_j, V_j per 128-key tile
+//   warp 9     MMA issuer (one thread); owns the TMEM allocation
+//
+// Shared memory (1 KiB aligned, 128-byte-swizzled tiles as written by TMA):
+//   Q0, Q1  [128 rows x 128 B]            32 KiB
+//   K       3 stages x [128 keys x 128 B] 48 KiB
+//   V       3 stages x [128 keys x 128 B] 48 KiB
 //   mbarriers, TMEM base address, abort flag
-// Tensor memory: S at columns [0,128), O at columns [128,192).
+// Tensor memory (512 columns x 128 lanes, fp32 words):
+//   S0 [0,128)  S1 [128,256)  O0 [256,320)  O1 [320,384)
+//   P0 [384,448)  P1 [448,512)   (P = fp16 pairs, the A operand of PV)
 
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -34,44 +36,49 @@
 #include <math.h>
 #include <stdint.h>
 
-#include "fa_sm100.cuh"
 #include "fa_kernels.h"
+#include "fa_sm100.cuh"
 
 namespace fa {
 namespace prefill {
 
-constexpr int kBlockM = 128;  // query rows per CTA
+constexpr int kBlockM = 128;  // query rows per tile
 constexpr int kBlockN = 128;  // keys per KV tile
-constexpr int kStages = 2;
-constexpr int kThreads = 192;
-constexpr int kSoftmaxThreads = 128;
-constexpr int kProducerWarp = 4;
-constexpr int kMmaWarp = 5;
+constexpr int kTilesPerCta = 2;
+constexpr int kStages = 3;
+constexpr int kSoftmaxThreads = 128;  // per query tile
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kThreads = 384;  // 3 warpgroups; warps 10-11 only donate registers
+constexpr int kCtrlRegs = 24;
+constexpr int kSoftmaxRegs = 240;
+static_assert(128 * kCtrlRegs + 256 * kSoftmaxRegs <= kThreads * 168,
+              "register split exceeds the launch allocation");
 constexpr uint32_t kTileBytes = kBlockN * kRowBytes;  // 16 KiB
 
 constexpr uint32_t kQOff = 0;
-constexpr uint32_t kKOff = kQOff + kTileBytes;
+constexpr uint32_t kKOff = kQOff + kTilesPerCta * kTileBytes;
 constexpr uint32_t kVOff = kKOff + kStages * kTileBytes;
-constexpr uint32_t kPOff = kVOff + kStages * kTileBytes;
-constexpr uint32_t kBarOff = kPOff + 2 * kTileBytes;
+constexpr uint32_t kBarOff = kVOff + kStages * kTileBytes;
 // barrier slots
 constexpr int kBarQFull = 0;
-constexpr int kBarKFull = 1;                     // + stage
-constexpr int kBarVFull = kBarKFull + kStages;   // + stage
-constexpr int kBarKVEmpty = kBarVFull + kStages; // + stage
-constexpr int kBarSFull = kBarKVEmpty + kStages;
-constexpr int kBarSFree = kBarSFull + 1;
-constexpr int kBarPFull = kBarSFree + 1;
-constexpr int kBarODone = kBarPFull + 1;
-constexpr int kBarDrain = kBarODone + 1;
+constexpr int kBarKFull = kBarQFull + 1;          // + stage
+constexpr int kBarVFull = kBarKFull + kStages;    // + stage
+constexpr int kBarKVEmpty = kBarVFull + kStages;  // + stage
+constexpr int kBarSFull = kBarKVEmpty + kStages;  // + tile
+constexpr int kBarSFree = kBarSFull + kTilesPerCta;
+constexpr int kBarPFull = kBarSFree + kTilesPerCta;
+constexpr int kBarODone = kBarPFull + kTilesPerCta;
+constexpr int kBarDrain = kBarODone + kTilesPerCta;
 constexpr int kNumBars = kBarDrain + 1;
 constexpr uint32_t kTmemSlotOff = kBarOff + kNumBars * 8;
 constexpr uint32_t kAbortOff = kTmemSlotOff + 4;
 constexpr uint32_t kSmemBytes = kAbortOff + 4 + 8;
 
-constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kTmemS = 0;
-constexpr uint32_t kTmemO = 128;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemS = 0;    // + 128 * tile
+constexpr uint32_t kTmemO = 256;  // + 64 * tile
+constexpr uint32_t kTmemP = 384;  // + 64 * tile
 
 constexpr uint32_t kIdescS = idesc_f16_f32(kBlockM, kBlockN, false);
 constexpr uint32_t kIdescPV = idesc_f16_f32(kBlockM, kHeadDim, true);
@@ -82,7 +89,48 @@ constexpr uint32_t kIdescPV = idesc_f16_f32(kBlockM, kHeadDim, true);
 // both use the same reference point.
 constexpr float kRescaleThreshold = 8.0f;
 
-__global__ void __launch_bounds__(kThreads, 2)
+// Of every 4 column pairs, this many take their exponentials from the MUFU
+// unit and the rest from exp2_poly2 on the FMA pipe.
+constexpr int kMufuPairsOf4 = 2;
+
+// S = Q K^T for one 128x128 tile: 4 MMAs of K=16 (32 bytes further along
+// the swizzled 128-byte rows each).
+__device__ __forceinline__ void issue_s_tile(uint32_t d, uint64_t q_desc,
+                                             uint64_t k_desc) {
+#pragma unroll
+  for (int kk = 0; kk < kHeadDim / 16; ++kk)
+    mma_f16_ss(d, q_desc + 2 * kk, k_desc + 2 * kk, kIdescS, kk > 0 ? 1u : 0u);
+}
+
+// O (+)= P V for one tile: 8 MMAs of K=16 keys. P is read from tensor memory
+// (8 columns = 16 fp16 per step); V steps by 16 rows = 2048 bytes.
+__device__ __forceinline__ void issue_pv_tile(uint32_t d, uint32_t p_tmem,
+                                              uint64_t v_desc, bool accumulate) {
+#pragma unroll
+  for (int kk = 0; kk < kBlockN / 16; ++kk)
+    mma_f16_ts(d, p_tmem + 8 * kk, v_desc + 128 * kk, kIdescPV,
+               (accumulate || kk > 0) ? 1u : 0u);
+}
+
+struct TileInfo {
+  int qt;    // query tile index along the sequence
+  int n_kv;  // key tiles this query tile attends (0: tile past the end)
+};
+
+__device__ __forceinline__ TileInfo tile_info(int pair, int t, int N,
+                                              int causal) {
+  TileInfo ti;
+  ti.qt = 2 * pair + t;
+  const int n_qt = (N + kBlockM - 1) / kBlockM;
+  if (ti.qt >= n_qt) {
+    ti.n_kv = 0;
+  } else {
+    ti.n_kv = causal ? ti.qt + 1 : (N + kBlockN - 1) / kBlockN;
+  }
+  return ti;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
                    const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v,
@@ -98,12 +146,15 @@ __global__ void __launch_bounds__(kThreads, 2)
     return;
   }
 
-  // Heaviest causal tiles first: blockIdx.x walks query tiles from the last
-  // (most keys) to the first, heads fastest.
+  // Heaviest causal pairs first: blockIdx.x walks query-tile pairs from the
+  // last (most keys) to the first, heads fastest.
   const int n_qt = (N + kBlockM - 1) / kBlockM;
-  const int qt = n_qt - 1 - static_cast<int>(blockIdx.x / BH);
+  const int n_pairs = (n_qt + 1) / 2;
+  const int pair = n_pairs - 1 - static_cast<int>(blockIdx.x / BH);
   const int bh = static_cast<int>(blockIdx.x % BH);
-  const int n_kv = causal ? (qt + 1) : (N + kBlockN - 1) / kBlockN;
+  const TileInfo t0 = tile_info(pair, 0, N, causal);
+  const TileInfo t1 = tile_info(pair, 1, N, causal);
+  const int n_kv = t0.n_kv > t1.n_kv ? t0.n_kv : t1.n_kv;
 
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kBarOff);
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kTmemSlotOff);
@@ -117,10 +168,12 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(&bars[kBarVFull + s], 1);
       mbar_init(&bars[kBarKVEmpty + s], 1);
     }
-    mbar_init(&bars[kBarSFull], 1);
-    mbar_init(&bars[kBarSFree], kSoftmaxThreads);
-    mbar_init(&bars[kBarPFull], kSoftmaxThreads);
-    mbar_init(&bars[kBarODone], 1);
+    for (int t = 0; t < kTilesPerCta; ++t) {
+      mbar_init(&bars[kBarSFull + t], 1);
+      mbar_init(&bars[kBarSFree + t], kSoftmaxThreads);
+      mbar_init(&bars[kBarPFull + t], kSoftmaxThreads);
+      mbar_init(&bars[kBarODone + t], 1);
+    }
     mbar_init(&bars[kBarDrain], 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -133,26 +186,36 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-
   const uint32_t sbase = smem_u32(smem);
 
+  // Register split: the control warpgroup (producer, MMA, two idle warps)
+  // gives registers to the two softmax warpgroups, which hold a full S row.
+  // 128 * kCtrlRegs + 256 * kSoftmaxRegs <= kThreads * 168 (launch budget).
+  // Each role's code sits inside the branch that sized its registers, so
+  // the compiler allocates each region for its own budget.
+  if (warp >= 8) {
+    setmaxnreg_dec<kCtrlRegs>();
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------------ TMA
     if (lane == 0) {
       prefetch_tensormap(&tm_q);
       prefetch_tensormap(&tm_k);
       prefetch_tensormap(&tm_v);
-      mbar_arrive_expect_tx(&bars[kBarQFull], kTileBytes);
-      tma_load_3d(smem + kQOff, &tm_q, &bars[kBarQFull], 0, qt * kBlockM, bh);
+      const bool two = t1.n_kv > 0;
+      mbar_arrive_expect_tx(&bars[kBarQFull], (two ? 2 : 1) * kTileBytes);
+      tma_load_3d(smem + kQOff, &tm_q, &bars[kBarQFull], 0, t0.qt * kBlockM,
+                  bh);
+      if (two)
+        tma_load_3d(smem + kQOff + kTileBytes, &tm_q, &bars[kBarQFull], 0,
+                    t1.qt * kBlockM, bh);
       int issued = 0;
       for (int j = 0; j < n_kv; ++j) {
         if (*abort_flag) break;
-        const int s = j & 1;
-        if (j >= kStages) {
-          if (!mbar_wait(&bars[kBarKVEmpty + s], ((j >> 1) - 1) & 1)) {
-            *abort_flag = 1;
-            break;
-          }
+        const int s = j % kStages;
+        const int use = j / kStages;
+        if (use > 0 && !mbar_wait(&bars[kBarKVEmpty + s], (use - 1) & 1)) {
+          *abort_flag = 1;
+          break;
         }
         mbar_arrive_expect_tx(&bars[kBarKFull + s], kTileBytes);
         tma_load_3d(smem + kKOff + s * kTileBytes, &tm_k, &bars[kBarKFull + s],
@@ -162,93 +225,119 @@ __global__ void __launch_bounds__(kThreads, 2)
                     0, j * kBlockN, bh);
         issued = j + 1;
       }
-      // Make sure no copy of ours is still landing in shared memory when the
-      // CTA exits (only matters when another role gave up early).
+      // No copy of ours may still be landing when the CTA exits (matters
+      // only when another role gave up early).
       if (*abort_flag) {
         mbar_wait(&bars[kBarQFull], 0);
         for (int j = (issued > kStages ? issued - kStages : 0); j < issued;
              ++j) {
-          mbar_wait(&bars[kBarKFull + (j & 1)], (j >> 1) & 1);
-          mbar_wait(&bars[kBarVFull + (j & 1)], (j >> 1) & 1);
+          mbar_wait(&bars[kBarKFull + j % kStages], (j / kStages) & 1);
+          mbar_wait(&bars[kBarVFull + j % kStages], (j / kStages) & 1);
         }
       }
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------ MMA
-    if (lane == 0) {
-      const uint32_t q_addr = sbase + kQOff;
-      const uint32_t p_addr = sbase + kPOff;
-      const uint32_t tS = tmem_base + kTmemS;
-      const uint32_t tO = tmem_base + kTmemO;
-      auto issue_s = [&](int j) {
-        const uint32_t k_addr = sbase + kKOff + (j & 1) * kTileBytes;
-#pragma unroll
-        for (int kk = 0; kk < kHeadDim / 16; ++kk) {
-          mma_f16_ss(tS, sw128_desc(q_addr + 32 * kk),
-                     sw128_desc(k_addr + 32 * kk), kIdescS, kk > 0);
+    // The whole warp runs the control flow, so every operand below is
+    // warp-uniform; one elected lane issues the tcgen05 instructions.
+    // Descriptors are formed once and advanced by adding byte offsets >> 4.
+    const bool leader = elect_one();
+    const uint32_t tmem = __shfl_sync(0xffffffffu, tmem_base, 0);
+    const int n0 = t0.n_kv;
+    const int n1 = t1.n_kv;
+    const uint64_t desc0 = sw128_desc(sbase);
+    bool ok = mbar_wait(&bars[kBarQFull], 0) &&
+              mbar_wait(&bars[kBarKFull + 0], 0);
+    if (ok) {
+      tc_fence_after();
+      if (leader) {
+        if (n0 > 0) {
+          issue_s_tile(tmem + kTmemS, desc0 + (kQOff >> 4), desc0 + (kKOff >> 4));
+          mma_commit(&bars[kBarSFull + 0]);
         }
-      };
-      bool ok = mbar_wait(&bars[kBarQFull], 0) &&
-                mbar_wait(&bars[kBarKFull + 0], 0);
-      if (ok) {
-        tc_fence_after();
-        issue_s(0);
-        mma_commit(&bars[kBarSFull]);
+        if (n1 > 0) {
+          issue_s_tile(tmem + kTmemS + 128, desc0 + ((kQOff + kTileBytes) >> 4),
+                       desc0 + (kKOff >> 4));
+          mma_commit(&bars[kBarSFull + 1]);
+        }
       }
-      for (int j = 0; ok && j < n_kv; ++j) {
-        if (*abort_flag) {
-          ok = false;
-          break;
-        }
-        if (j + 1 < n_kv) {
-          const int s1 = (j + 1) & 1;
-          if (!mbar_wait(&bars[kBarKFull + s1], ((j + 1) >> 1) & 1) ||
-              !mbar_wait(&bars[kBarSFree], j & 1)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          issue_s(j + 1);
-          mma_commit(&bars[kBarSFull]);
-        }
-        const int s = j & 1;
-        if (!mbar_wait(&bars[kBarPFull], j & 1) ||
-            !mbar_wait(&bars[kBarVFull + s], (j >> 1) & 1)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t v_addr = sbase + kVOff + s * kTileBytes;
-#pragma unroll
-        for (int kk = 0; kk < kBlockN / 16; ++kk) {
-          const uint32_t a = p_addr + (kk >> 2) * kTileBytes + 32 * (kk & 3);
-          mma_f16_ss(tO, sw128_desc(a), sw128_desc(v_addr + 2048 * kk),
-                     kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
-        }
-        mma_commit(&bars[kBarODone]);
-        mma_commit(&bars[kBarKVEmpty + s]);
-      }
-      if (!ok) *abort_flag = 1;
-      // Every MMA issued above has retired once this commit lands; TMEM is
-      // not released before that.
-      mma_commit(&bars[kBarDrain]);
-      mbar_wait(&bars[kBarDrain], 0);
+      __syncwarp();
     }
+    for (int j = 0; ok && j < n_kv; ++j) {
+      if (*abort_flag) {
+        ok = false;
+        break;
+      }
+      const int s = j % kStages;
+      const int s1 = (j + 1) % kStages;
+#pragma unroll
+      for (int t = 0; t < kTilesPerCta; ++t) {
+        const int nt = t ? n1 : n0;
+        if (!ok || j >= nt) continue;
+        if (j + 1 < nt) {
+          if (!mbar_wait(&bars[kBarKFull + s1], ((j + 1) / kStages) & 1) ||
+              !mbar_wait(&bars[kBarSFree + t], j & 1)) {
+            ok = false;
+            continue;
+          }
+          FA_TRACE_EVENT(2048 + j * 16 + t * 8 + 3);
+          tc_fence_after();
+          if (leader) {
+            issue_s_tile(tmem + kTmemS + 128 * t,
+                         desc0 + ((kQOff + t * kTileBytes) >> 4),
+                         desc0 + ((kKOff + s1 * kTileBytes) >> 4));
+            mma_commit(&bars[kBarSFull + t]);
+          }
+          __syncwarp();
+          FA_TRACE_EVENT(2048 + j * 16 + t * 8 + 1);
+        }
+        if (!mbar_wait(&bars[kBarPFull + t], j & 1) ||
+            !mbar_wait(&bars[kBarVFull + s], (j / kStages) & 1)) {
+          ok = false;
+          continue;
+        }
+        FA_TRACE_EVENT(2048 + j * 16 + t * 8 + 4);
+        tc_fence_after();
+        if (leader) {
+          issue_pv_tile(tmem + kTmemO + 64 * t, tmem + kTmemP + 64 * t,
+                        desc0 + ((kVOff + s * kTileBytes) >> 4), j > 0);
+          mma_commit(&bars[kBarODone + t]);
+        }
+        __syncwarp();
+        FA_TRACE_EVENT(2048 + j * 16 + t * 8 + 2);
+      }
+      if (!ok) break;
+      if (leader) mma_commit(&bars[kBarKVEmpty + s]);
+      __syncwarp();
+    }
+    if (!ok && leader) *abort_flag = 1;
+    // Every MMA issued above has retired once this commit lands; TMEM is
+    // not released before that.
+    if (leader) mma_commit(&bars[kBarDrain]);
     __syncwarp();
+    mbar_wait(&bars[kBarDrain], 0);
+  }
   } else {
+    setmaxnreg_inc<kSoftmaxRegs>();
     // -------------------------------------------------------------- softmax
-    const int row = threadIdx.x;  // 0..127 == TMEM lane
-    const uint32_t lane_addr = static_cast<uint32_t>(warp * 32) << 16;
-    const uint32_t tS = tmem_base + lane_addr + kTmemS;
-    const uint32_t tO = tmem_base + lane_addr + kTmemO;
-    const uint32_t p_row = sbase + kPOff + row * kRowBytes;
-    const int swz = row & 7;
+    const int t = warp >> 2;            // query tile of this warpgroup
+    const int row = threadIdx.x & 127;  // row in the tile == TMEM lane
+    const TileInfo ti = t == 0 ? t0 : t1;
+    const uint32_t lane_addr = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem_base + lane_addr + kTmemS + 128 * t;
+    const uint32_t tO = tmem_base + lane_addr + kTmemO + 64 * t;
+    const uint32_t tP = tmem_base + lane_addr + kTmemP + 64 * t;
+    uint64_t *s_full = &bars[kBarSFull + t];
+    uint64_t *s_free = &bars[kBarSFree + t];
+    uint64_t *p_full = &bars[kBarPFull + t];
+    uint64_t *o_done = &bars[kBarODone + t];
     float m_use = -INFINITY;  // running max, in log2 units of scale * q.k
     float l_sum = 0.f;
     bool ok = true;
 
-    for (int j = 0; j < n_kv; ++j) {
-      if (*abort_flag || !mbar_wait(&bars[kBarSFull], j & 1)) {
+    for (int j = 0; j < ti.n_kv; ++j) {
+      if (row == 0) FA_TRACE_EVENT(t * 1024 + j * 8 + 0);
+      if (*abort_flag || !mbar_wait(s_full, j & 1)) {
         ok = false;
         break;
       }
@@ -260,7 +349,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       tmem_ld32(tS + 96, sr[3]);
       tmem_wait_ld();
       tc_fence_before();
-      mbar_arrive(&bars[kBarSFree]);
+      mbar_arrive(s_free);
+      if (row == 0) FA_TRACE_EVENT(t * 1024 + j * 8 + 1);
 
       float s[128];
 #pragma unroll
@@ -276,16 +366,28 @@ __global__ void __launch_bounds__(kThreads, 2)
         sl = 1.f;
       }
       const int kbase = j * kBlockN;
-      const bool diag = causal && (j == qt);
+      const bool diag = causal && (j == ti.qt);
       if (diag || kbase + kBlockN > N) {
         int lim = N - kbase;
         if (diag) lim = min(lim, row + 1);
 #pragma unroll
         for (int c = 0; c < 128; ++c) s[c] = (c < lim) ? s[c] : -INFINITY;
       }
-      float mx = s[0];
+      // Row max: three-input max over 8 independent chains (one 127-long
+      // dependent chain would leave the two softmax warps of an SM
+      // sub-partition stalled on max latency).
+      float mxp[8];
 #pragma unroll
-      for (int c = 1; c < 128; ++c) mx = fmaxf(mx, s[c]);
+      for (int i = 0; i < 8; ++i) mxp[i] = s[i];
+#pragma unroll
+      for (int c = 8; c < 128; c += 16) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          mxp[i] = fmax3(mxp[i], s[c + i], s[c + 8 + i]);
+      }
+      const float mx = fmax3(fmax3(mxp[0], mxp[1], mxp[2]),
+                             fmax3(mxp[3], mxp[4], mxp[5]),
+                             fmaxf(mxp[6], mxp[7]));
       const float m_tile = mx * sl;
       float corr = 1.f;
       const bool rescale = m_tile > m_use + kRescaleThreshold;
@@ -296,22 +398,36 @@ __global__ void __launch_bounds__(kThreads, 2)
       l_sum *= corr;
       const float neg_m = -m_use;
 
-      uint32_t pk[64];
-      float rs0 = 0.f, rs1 = 0.f;
+      // P = 2^(s*sl - m). The exponent argument is one packed FMA per two
+      // columns; the exponentials alternate between the MUFU unit and a
+      // polynomial on the FMA pipe (exp2_poly2) so neither pipe bounds the
+      // step alone. The row sum uses four packed accumulators.
+      const float2 sl2 = make_float2(sl, sl);
+      const float2 nm2 = make_float2(neg_m, neg_m);
+      float2 rs[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) rs[i] = make_float2(0.f, 0.f);
+      uint32_t pk[2][32];  // P row as fp16 pairs, TMEM columns [0,32), [32,64)
 #pragma unroll
       for (int c = 0; c < 128; c += 2) {
-        const float p0 = fast_exp2(fmaf(s[c], sl, neg_m));
-        const float p1 = fast_exp2(fmaf(s[c + 1], sl, neg_m));
-        rs0 += p0;
-        rs1 += p1;
-        pk[c >> 1] = pack_half2(p0, p1);
+        const float2 x = ffma2(make_float2(s[c], s[c + 1]), sl2, nm2);
+        float2 p;
+        if (((c >> 1) & 3) >= kMufuPairsOf4) {
+          p = exp2_poly2(x);
+        } else {
+          p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+        }
+        rs[(c >> 1) & 3] = fadd2(rs[(c >> 1) & 3], p);
+        pk[c >> 6][(c >> 1) & 31] = pack_half2(p.x, p.y);
       }
-      l_sum += rs0 + rs1;
+      const float2 rsum = fadd2(fadd2(rs[0], rs[1]), fadd2(rs[2], rs[3]));
+      l_sum += rsum.x + rsum.y;
 
       if (j > 0) {
-        // PV_{j-1} must have retired: it still reads the P buffer and it
-        // writes the O columns a rescale would touch.
-        if (!mbar_wait(&bars[kBarODone], (j - 1) & 1)) {
+        // PV_{j-1} must have retired: it reads the P columns about to be
+        // overwritten and writes the O columns a rescale would touch.
+        if (row == 0) FA_TRACE_EVENT(t * 1024 + j * 8 + 2);
+        if (!mbar_wait(o_done, (j - 1) & 1)) {
           ok = false;
           break;
         }
@@ -327,49 +443,46 @@ __global__ void __launch_bounds__(kThreads, 2)
               o[c] = __float_as_uint(__uint_as_float(o[c]) * corr);
             tmem_st32(tO + 32 * h, o);
           }
-          tmem_wait_st();
         }
       }
-#pragma unroll
-      for (int cc = 0; cc < 16; ++cc) {
-        const uint32_t addr = p_row + (cc >> 3) * kTileBytes +
-                              (static_cast<uint32_t>((cc & 7) ^ swz) << 4);
-        st_shared_v4(addr, pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2],
-                     pk[4 * cc + 3]);
-      }
-      fence_proxy_async_smem();
+      tmem_st32(tP, pk[0]);
+      tmem_st32(tP + 32, pk[1]);
+      tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&bars[kBarPFull]);
+      mbar_arrive(p_full);
+      if (row == 0) FA_TRACE_EVENT(t * 1024 + j * 8 + 4);
     }
 
-    if (ok && mbar_wait(&bars[kBarODone], (n_kv - 1) & 1)) {
-      tc_fence_after();
-      uint32_t o[2][32];
-      tmem_ld32(tO, o[0]);
-      tmem_ld32(tO + 32, o[1]);
-      tmem_wait_ld();
-      const int q_row = qt * kBlockM + row;
-      if (q_row < N) {
-        const float inv_l = (l_sum > 0.f) ? 1.f / l_sum : 0.f;
-        uint4 *dst = reinterpret_cast<uint4 *>(
-            out + (static_cast<size_t>(bh) * N + q_row) * kHeadDim);
+    if (ti.n_kv > 0) {
+      if (ok && mbar_wait(o_done, (ti.n_kv - 1) & 1)) {
+        tc_fence_after();
+        uint32_t o[2][32];
+        tmem_ld32(tO, o[0]);
+        tmem_ld32(tO + 32, o[1]);
+        tmem_wait_ld();
+        const int q_row = ti.qt * kBlockM + row;
+        if (q_row < N) {
+          const float inv_l = (l_sum > 0.f) ? 1.f / l_sum : 0.f;
+          uint4 *dst = reinterpret_cast<uint4 *>(
+              out + (static_cast<size_t>(bh) * N + q_row) * kHeadDim);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint4 v;
-          const uint32_t *src = &o[c >> 2][(c & 3) * 8];
-          v.x = pack_half2(__uint_as_float(src[0]) * inv_l,
-                           __uint_as_float(src[1]) * inv_l);
-          v.y = pack_half2(__uint_as_float(src[2]) * inv_l,
-                           __uint_as_float(src[3]) * inv_l);
-          v.z = pack_half2(__uint_as_float(src[4]) * inv_l,
-                           __uint_as_float(src[5]) * inv_l);
-          v.w = pack_half2(__uint_as_float(src[6]) * inv_l,
-                           __uint_as_float(src[7]) * inv_l);
-          dst[c] = v;
+          for (int c = 0; c < 8; ++c) {
+            uint4 v;
+            const uint32_t *src = &o[c >> 2][(c & 3) * 8];
+            v.x = pack_half2(__uint_as_float(src[0]) * inv_l,
+                             __uint_as_float(src[1]) * inv_l);
+            v.y = pack_half2(__uint_as_float(src[2]) * inv_l,
+                             __uint_as_float(src[3]) * inv_l);
+            v.z = pack_half2(__uint_as_float(src[4]) * inv_l,
+                             __uint_as_float(src[5]) * inv_l);
+            v.w = pack_half2(__uint_as_float(src[6]) * inv_l,
+                             __uint_as_float(src[7]) * inv_l);
+            dst[c] = v;
+          }
         }
+      } else {
+        *abort_flag = 1;
       }
-    } else {
-      *abort_flag = 1;
     }
   }
 
@@ -398,7 +511,9 @@ cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
                 "causal tile skipping assumes square tiles");
   const int BH = B * H;
   const int n_qt = (N + prefill::kBlockM - 1) / prefill::kBlockM;
-  const unsigned grid = static_cast<unsigned>(n_qt) * static_cast<unsigned>(BH);
+  const int n_pairs = (n_qt + 1) / 2;
+  const unsigned grid =
+      static_cast<unsigned>(n_pairs) * static_cast<unsigned>(BH);
   const float scale_log2 = scale * 1.4426950408889634f;
   prefill::prefill_kernel<<<grid, prefill::kThreads, prefill::kSmemBytes,
                             stream>>>(tm_q, tm_k, tm_v, out, N, BH,

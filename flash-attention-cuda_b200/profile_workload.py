@@ -1,0 +1,65 @@
+"""Fixed workloads for profiling one kernel under ncu.
+
+    python flash-attention-cuda_b200/profile_workload.py --case prefill_c3
+    ncu --set full --clock-control none -k regex:prefill_kernel -s 2 -c 1 \
+        python flash-attention-cuda_b200/profile_workload.py --case prefill_c3
+
+Each case runs `--iters` launches of one kernel on seeded synthetic inputs
+(the BASELINE configurations); the first launches are warm-up, so skip them
+with ncu's -s. Inputs stay well under a few GB of device memory.
+"""
+
+import argparse
+import math
+import os
+import sys
+
+import torch
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+import flashattn_cuda as fa  # noqa: E402
+
+SCALE = 1.0 / math.sqrt(64)
+
+CASES = {
+    # name: (kind, shape, causal)
+    "prefill_c3": ("prefill", (4, 14, 4096), True),
+    "prefill_c2_causal": ("prefill", (8, 12, 1024), True),
+    "prefill_c2_full": ("prefill", (8, 12, 1024), False),
+    "prefill_small": ("prefill", (1, 8, 2048), True),
+    "decode_c4": ("decode", (64, 12, 8192), None),
+    "decode_c5": ("decode", (1, 14, 131072), None),
+}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--case", choices=sorted(CASES), required=True)
+    ap.add_argument("--iters", type=int, default=3)
+    args = ap.parse_args()
+    kind, (b, h, n), causal = CASES[args.case]
+    g = torch.Generator(device="cuda").manual_seed(0)
+    if kind == "prefill":
+        q, k, v = (torch.randn(b, h, n, 64, generator=g, device="cuda",
+                               dtype=torch.float16) for _ in range(3))
+        fn = lambda: fa.prefill(q, k, v, causal, SCALE)
+    else:
+        q = torch.randn(b, h, 1, 64, generator=g, device="cuda", dtype=torch.float16)
+        k, v = (torch.randn(b, h, n, 64, generator=g, device="cuda",
+                            dtype=torch.float16) for _ in range(2))
+        cpu_gen = torch.Generator().manual_seed(0)
+        if b > 1:
+            lens = torch.randint(1, n + 1, (b,), generator=cpu_gen, dtype=torch.int32)
+        else:
+            lens = torch.full((b,), n, dtype=torch.int32)
+        lens = lens.cuda()
+        fn = lambda: fa.decode(q, k, v, lens, SCALE)
+    for _ in range(args.iters):
+        fn()
+    torch.cuda.synchronize()
+    assert fa.take_device_error() == 0
+    print(f"{args.case}: {args.iters} launches ok")
+
+
+if __name__ == "__main__":
+    main()
