@@ -4,3 +4,4 @@
 #include "capi.cu"
 #include "decode_sm100.cu"
 #include "prefill_sm100.cu"
+#include "noalloc.cu"

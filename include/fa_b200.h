@@ -99,6 +99,31 @@ int fa_decode_partial(const void *q, const void *k_cache, const void *v_cache,
                       size_t counter_count, void *stream);
 
 /*
+ * Largest batch * heads that fa_decode_noalloc accepts; its scratch array is
+ * sized for this many (batch, head) pairs.
+ */
+#define FA_NOALLOC_MAX_BH 8192
+
+/*
+ * fa_decode without caller-provided scratch, for callers that cannot
+ * allocate GPU memory (a memory pool fixed at start-up, a plugin that only
+ * receives its input and output pointers). Same arguments, layout and
+ * results as fa_decode with the automatic schedule; no reference
+ * counterpart (the reference allocates its scratch on every call).
+ * The scratch lives in a fixed device array inside the library (about
+ * 2.5 MB on every GPU that loads it, held until the process exits), so
+ * nothing is allocated. Limits: B * H <= FA_NOALLOC_MAX_BH, else
+ * FA_ENOSPACE before anything is launched. The first call on a device looks
+ * up the array's device address (make it before any stream capture). All
+ * calls share the array: calls that can overlap on the GPU (different
+ * streams, or other devices' threads racing on one device) corrupt each
+ * other's results; order them on one stream.
+ */
+int fa_decode_noalloc(const void *q, const void *k_cache, const void *v_cache,
+                      const int32_t *seq_lens, void *o, int B, int H,
+                      int S_max, float scale, void *stream);
+
+/*
  * Log-sum-exp merge of G partial sets laid out (G, B, H, 68) fp32 into the
  * fp16 output o (B, H, 1, 64). Partials with l <= 0 are skipped and a row
  * with no keys anywhere is 0, as in the reference's merge pass
