@@ -308,6 +308,7 @@ def run_ours(args, rank, world, local_rank):
             "gbs_per_gpu_rank0": round(bytes_rank / (t * 1e-3) / 1e9, 1),
             "frac_of_measured_hbm": round(bytes_rank / (t * 1e-3) / 1e9 / hbm, 4),
             "tokens_per_s": round(C4["B"] / (t * 1e-3), 1),
+            "traffic_bytes_per_launch_ncu": read_profile_traffic("decode_kernel_c4"),
             "scaling": "strong (batch sharded, LPT by length)"}
         del qd, kc, vc
 
@@ -338,6 +339,11 @@ def run_ours(args, rank, world, local_rank):
             "scaling": "strong (KV sequence sharded, NCCL all-gather of "
                        "partials + merge)" if world > 1 else "single GPU"}
         del qd, kc, vc
+
+        # ------- the reference's own CUDA kernels on this B200 (baseline) ----
+        if world == 1 and not args.no_ref_cuda:
+            secondary["reference_cuda_kernels"] = ref_cuda_measure(
+                timer, randn, args.steps, args.warmup)
 
     assert fa.take_device_error() == 0, "device-side error during the bench"
     clocks = sampler.summary()
@@ -385,6 +391,47 @@ def run_ours(args, rank, world, local_rank):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def ref_cuda_measure(timer, randn, steps, warmup):
+    """Times the reference's own CUDA kernels (built for sm_100 from its
+    sources into oracle/_ref by oracle/build_ref.py) on the same configs."""
+    import torch
+
+    sys.path.insert(0, ORACLE_DIR)
+    try:
+        import build_ref
+        ref = build_ref.load()
+    except Exception as ex:  # not built on this machine
+        return {"unavailable": f"oracle/_ref not built: {type(ex).__name__}"}
+    out = {}
+    n = C3["N"]
+    q, k, v = (randn(C3["B"], C3["H"], n, HEAD_DIM, seed=70 + i) for i in range(3))
+    t = timer.run(lambda: ref.prefill(q, k, v, True, SCALE), steps, warmup) / steps
+    out["c3_prefill"] = {"ms": round(t, 4), "tflops": round(
+        prefill_flops(C3["B"], C3["H"], n, True) / (t * 1e-3) / 1e12, 2)}
+    del q, k, v
+    g = torch.Generator().manual_seed(0)
+    lens = torch.randint(1, C4["cap"] + 1, (C4["B"],), generator=g,
+                         dtype=torch.int32).cuda()
+    qd = randn(C4["B"], C4["H"], 1, HEAD_DIM, seed=73)
+    kc = randn(C4["B"], C4["H"], C4["cap"], HEAD_DIM, seed=74)
+    vc = randn(C4["B"], C4["H"], C4["cap"], HEAD_DIM, seed=75)
+    t = timer.run(lambda: ref.decode(qd, kc, vc, lens, SCALE), steps, warmup) / steps
+    b = int(lens.sum()) * C4["H"] * HEAD_DIM * 2 * 2
+    out["c4_decode"] = {"ms": round(t, 4), "gbs": round(b / (t * 1e-3) / 1e9, 1)}
+    del qd, kc, vc
+    S = C5["S"]
+    qd = randn(1, C5["H"], 1, HEAD_DIM, seed=76)
+    kc = randn(1, C5["H"], S, HEAD_DIM, seed=77)
+    vc = randn(1, C5["H"], S, HEAD_DIM, seed=78)
+    lens = torch.tensor([S], dtype=torch.int32, device="cuda")
+    t = timer.run(lambda: ref.decode(qd, kc, vc, lens, SCALE), steps, warmup) / steps
+    b = S * C5["H"] * HEAD_DIM * 2 * 2
+    out["c5_decode"] = {"ms": round(t, 4), "gbs": round(b / (t * 1e-3) / 1e9, 1)}
+    out["note"] = ("reference csrc/prefill.cu + csrc/decode.cu compiled for "
+                   "sm_100 from its own sources, same inputs and timing")
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -477,6 +524,8 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=12.0,
                     help="seconds of CPU work for the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ref-cuda", action="store_true",
+                    help="skip timing the reference's own CUDA kernels")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
