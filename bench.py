@@ -78,21 +78,15 @@ def read_profile_traffic(name):
 
 
 def shard_range(total, world, rank):
-    base, rem = divmod(total, world)
-    start = rank * base + min(rank, rem)
-    return start, start + base + (1 if rank < rem else 0)
+    sys.path.insert(0, PKG_DIR)
+    from flashattn_cuda.dist import shard_units
+    return shard_units(total, world, rank)
 
 
 def lpt_partition(weights, world):
-    """Longest-processing-time assignment of items to `world` bins."""
-    order = sorted(range(len(weights)), key=lambda i: -weights[i])
-    loads = [0] * world
-    bins = [[] for _ in range(world)]
-    for i in order:
-        r = min(range(world), key=lambda j: loads[j])
-        bins[r].append(i)
-        loads[r] += weights[i]
-    return [sorted(b) for b in bins]
+    sys.path.insert(0, PKG_DIR)
+    from flashattn_cuda.dist import lpt_partition as lpt
+    return lpt(weights, world)
 
 
 # ---------------------------------------------------------------------------
@@ -319,14 +313,11 @@ def run_ours(args, rank, world, local_rank):
         kc = randn(1, C5["H"], c1 - c0, HEAD_DIM, seed=51 + rank)
         vc = randn(1, C5["H"], c1 - c0, HEAD_DIM, seed=52 + rank)
         lens_local = torch.tensor([c1 - c0], dtype=torch.int32, device="cuda")
-        gathered = torch.empty(world, 1, C5["H"], 68, device="cuda")
+
+        from flashattn_cuda.dist import sharded_decode
 
         def c5_step():
-            if world == 1:
-                return fa.decode(qd, kc, vc, lens_local, SCALE)
-            part = fa.decode_partial(qd, kc, vc, lens_local, SCALE)
-            dist.all_gather_into_tensor(gathered, part)
-            return fa.merge_partials(gathered)
+            return sharded_decode(qd, kc, vc, lens_local, SCALE)
 
         t = timer.run(c5_step, args.steps, args.warmup) / args.steps
         launches += args.steps * (1 if world == 1 else 2)
