@@ -41,11 +41,14 @@ namespace decode {
 
 constexpr int kConsumerWarps = 8;
 constexpr int kProducerWarp = kConsumerWarps;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kMergerWarp = kConsumerWarps + 1;
+constexpr int kThreads = (kConsumerWarps + 2) * 32;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kStageRows = 128;
 constexpr int kStages = 3;
 constexpr int kRowsPerWarp = kStageRows / kConsumerWarps;  // 16
+constexpr int kRowIters = kRowsPerWarp / 4;  // a warp covers 4 rows at once
+static_assert(kRowsPerWarp % 4 == 0, "rows per warp must be a multiple of 4");
 constexpr int kMinRowsPerCta = 128;
 constexpr int kCtasPerSm = 2;
 constexpr uint32_t kStageBytes = kStageRows * kRowBytes;  // 16 KiB
@@ -66,10 +69,14 @@ constexpr uint32_t kKOff = 0;
 constexpr uint32_t kVOff = kStages * kStageBytes;
 constexpr uint32_t kHdrOff = 2 * kStages * kStageBytes;
 constexpr uint32_t kRedOff = kHdrOff + kStages * sizeof(StageHeader);
-constexpr uint32_t kRedBytes = kConsumerWarps * kPartialFloats * 4;
+// Hand-off buffers from the consumer warps to the merger warp, double
+// buffered: per buffer one (m, l, acc) per consumer warp plus a header.
+constexpr int kRedBufs = 2;
+constexpr uint32_t kRedBufBytes = kConsumerWarps * kPartialFloats * 4 + 32;
+constexpr uint32_t kRedBytes = kRedBufs * kRedBufBytes;
 constexpr uint32_t kBarOff = kRedOff + kRedBytes;
-constexpr uint32_t kFlagOff = kBarOff + 2 * kStages * 8;
-constexpr uint32_t kSmemBytes = kFlagOff + 16;
+// full[kStages], empty[kStages], red_full[kRedBufs], red_empty[kRedBufs]
+constexpr uint32_t kSmemBytes = kBarOff + (2 * kStages + 2 * kRedBufs) * 8;
 
 constexpr float kNegBig = -1e30f;  // finite "no max yet", as the reference
 
@@ -99,6 +106,107 @@ __device__ void write_empty_sequence(const DecodeArgs &a, int b) {
   }
 }
 
+// Writes a finished (m, l, acc) for segment g: the fp16 output, or the
+// partial in partial mode. Lane l holds dims l and l + 32.
+__device__ __forceinline__ void finish_segment(const DecodeArgs &a, size_t g,
+                                               float M, float L, float A0,
+                                               float A1, int lane) {
+  if (a.partial_out) {
+    float *p = a.partial_out + g * kPartialFloats;
+    p[4 + lane] = A0;
+    p[4 + 32 + lane] = A1;
+    if (lane == 0) {
+      p[0] = M;
+      p[1] = L;
+      p[2] = 0.f;
+      p[3] = 0.f;
+    }
+  } else {
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    a.out[g * kHeadDim + lane] = __float2half_rn(A0 * inv);
+    a.out[g * kHeadDim + 32 + lane] = __float2half_rn(A1 * inv);
+  }
+}
+
+// Merger warp: combines the consumer warps' partials of each finished piece,
+// writes whole segments directly, and for segments split across CTAs
+// publishes this CTA's partial; the last CTA to arrive on the segment's
+// counter merges all of them (partials are read in parallel, merged in CTA
+// order, so the result is deterministic).
+__device__ void merger(const DecodeArgs &a, uint8_t *red_base,
+                       uint64_t *red_full, uint64_t *red_empty) {
+  const int lane = threadIdx.x & 31;
+  for (int piece = 0;; ++piece) {
+    const int buf = piece & 1;
+    if (!mbar_wait(&red_full[buf], (piece >> 1) & 1)) return;
+    const float *red = reinterpret_cast<const float *>(red_base + buf * kRedBufBytes);
+    const int *hdr_in = reinterpret_cast<const int *>(red + kConsumerWarps * kPartialFloats);
+    const int flags = hdr_in[1];
+    if (flags & kDone) return;
+    const size_t g = static_cast<size_t>(hdr_in[0]);
+    const int c0 = hdr_in[2];
+    const int c1 = hdr_in[3];
+    float M = kNegBig;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, red[w * kPartialFloats]);
+    float L = 0.f, A0 = 0.f, A1 = 0.f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) {
+      const float fw = fast_exp2(red[w * kPartialFloats] - M);
+      L = fmaf(red[w * kPartialFloats + 1], fw, L);
+      A0 = fmaf(red[w * kPartialFloats + 4 + lane], fw, A0);
+      A1 = fmaf(red[w * kPartialFloats + 4 + 32 + lane], fw, A1);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&red_empty[buf]);  // buffer consumed
+
+    if (flags & kWhole) {
+      finish_segment(a, g, M, L, A0, A1, lane);
+      continue;
+    }
+    float *ws = a.ws_partials + (g + blockIdx.x) * static_cast<size_t>(kPartialFloats);
+    ws[4 + lane] = A0;
+    ws[4 + 32 + lane] = A1;
+    if (lane == 0) {
+      ws[0] = M;
+      ws[1] = L;
+    }
+    __threadfence();
+    __syncwarp();
+    unsigned last = 0;
+    if (lane == 0) {
+      const unsigned n_parts = static_cast<unsigned>(c1 - c0);
+      last = atomicInc(&a.ws_counters[g], n_parts) == n_parts;
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) continue;
+    __threadfence();
+    // every partial of the segment is in place: merge them
+    float M2 = kNegBig;
+    for (int c = c0 + lane; c <= c1; c += 32) {
+      const float *pp = a.ws_partials + (g + c) * static_cast<size_t>(kPartialFloats);
+      if (__ldcg(pp + 1) > 0.f) M2 = fmaxf(M2, __ldcg(pp));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+      M2 = fmaxf(M2, __shfl_xor_sync(0xffffffffu, M2, o));
+    float L2 = 0.f, B0 = 0.f, B1 = 0.f;
+#pragma unroll 4
+    for (int c = c0; c <= c1; ++c) {
+      const float *pp = a.ws_partials + (g + c) * static_cast<size_t>(kPartialFloats);
+      const float lc = __ldcg(pp + 1);
+      const float mc = __ldcg(pp);
+      const float x0 = __ldcg(pp + 4 + lane);
+      const float x1 = __ldcg(pp + 4 + 32 + lane);
+      const float fc = lc > 0.f ? fast_exp2(mc - M2) : 0.f;
+      L2 = fmaf(lc, fc, L2);
+      B0 = fmaf(x0, fc, B0);
+      B1 = fmaf(x1, fc, B1);
+    }
+    finish_segment(a, g, M2, L2, B0, B1, lane);
+  }
+}
+
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     decode_kernel(const DecodeArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -107,14 +215,18 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + kBarOff);
   uint64_t *empty = full + kStages;
   StageHeader *hdr = reinterpret_cast<StageHeader *>(smem + kHdrOff);
-  float *red = reinterpret_cast<float *>(smem + kRedOff);
-  volatile int *last_flag = reinterpret_cast<volatile int *>(smem + kFlagOff);
+  uint64_t *red_full = empty + kStages;
+  uint64_t *red_empty = red_full + kRedBufs;
   if (device_failed()) return;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumerWarps);
+    }
+    for (int r = 0; r < kRedBufs; ++r) {
+      mbar_init(&red_full[r], kConsumerWarps);
+      mbar_init(&red_empty[r], 1);
     }
     fence_barrier_init();
   }
@@ -241,12 +353,18 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     return;
   }
 
+  if (warp == kMergerWarp) {
+    merger(a, smem + kRedOff, red_full, red_empty);
+    return;
+  }
+
   // ---------------------------------------------------------------- consumers
   const int grp = lane >> 3;  // which of the warp's 4 rows per instruction
   const int sub = lane & 7;   // head dims [8*sub, 8*sub + 8)
   float qf[8];
   int cur_g = -1;
   float m_run = kNegBig, l_run = 0.f;
+  int piece = 0;  // pieces handed to the merger warp so far
   float acc[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) acc[e] = 0.f;
@@ -255,7 +373,21 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     const int slot = it % kStages;
     if (!mbar_wait(&full[slot], (it / kStages) & 1)) break;
     const StageHeader hd = hdr[slot];
-    if (hd.flags & kDone) break;
+    if (hd.flags & kDone) {
+      // tell the merger warp there is nothing more (same hand-off protocol)
+      const int buf = piece & 1;
+      if (piece >= kRedBufs &&
+          !mbar_wait(&red_empty[buf], ((piece >> 1) - 1) & 1))
+        break;
+      if (warp == 0 && lane == 0) {
+        int *hdr_out = reinterpret_cast<int *>(smem + kRedOff + buf * kRedBufBytes +
+                                               kConsumerWarps * kPartialFloats * 4);
+        hdr_out[1] = kDone;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&red_full[buf]);
+      break;
+    }
     if (hd.g != cur_g) {
       cur_g = hd.g;
       const uint4 qv = *reinterpret_cast<const uint4 *>(
@@ -273,9 +405,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     const uint32_t vb = smem_u32(smem + kVOff + slot * kStageBytes);
     const int row_base = warp * kRowsPerWarp + grp;
     if (warp * kRowsPerWarp < hd.n) {  // warp-uniform: shuffles below
-      float sc[4];
+      float sc[kRowIters];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < kRowIters; ++i) {
         const int row = row_base + 4 * i;
         float d = 0.f;
         if (row < hd.n) {
@@ -291,24 +423,30 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         sc[i] = d;
       }
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < kRowIters; ++i) {
         sc[i] += __shfl_xor_sync(0xffffffffu, sc[i], 1);
         sc[i] += __shfl_xor_sync(0xffffffffu, sc[i], 2);
         sc[i] += __shfl_xor_sync(0xffffffffu, sc[i], 4);
         if (row_base + 4 * i >= hd.n) sc[i] = -INFINITY;
       }
-      const float mx = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
+      float mx = sc[0];
+#pragma unroll
+      for (int i = 1; i < kRowIters; ++i) mx = fmaxf(mx, sc[i]);
       const float m_new = fmaxf(m_run, mx);
       const float corr = fast_exp2(m_run - m_new);
       m_run = m_new;
-      float p[4];
+      float p[kRowIters];
+      float psum = 0.f;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) p[i] = fast_exp2(sc[i] - m_new);
-      l_run = fmaf(l_run, corr, (p[0] + p[1]) + (p[2] + p[3]));
+      for (int i = 0; i < kRowIters; ++i) {
+        p[i] = fast_exp2(sc[i] - m_new);
+        psum += p[i];
+      }
+      l_run = fmaf(l_run, corr, psum);
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc[e] *= corr;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < kRowIters; ++i) {
         const int row = row_base + 4 * i;
         if (row < hd.n) {
           const uint4 vv = ld_shared_v4(vb + row * kRowBytes + sub * 16);
@@ -327,8 +465,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 
     if (!(hd.flags & kLast)) continue;
 
-    // ---- this CTA's piece of segment hd.g is complete: reduce it --------
-    // 4 row groups of the warp -> one (m, l, acc[64]) per warp.
+    // ---- this CTA's piece of segment hd.g is complete: reduce the warp's 4
+    // row groups to one (m, l, acc[64]) and hand it to the merger warp, which
+    // combines the 8 warps and finishes the segment while the consumers go
+    // on streaming the next piece.
     float m_w = fmaxf(m_run, __shfl_xor_sync(0xffffffffu, m_run, 8));
     m_w = fmaxf(m_w, __shfl_xor_sync(0xffffffffu, m_w, 16));
     const float f = fast_exp2(m_run - m_w);
@@ -342,6 +482,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       v += __shfl_xor_sync(0xffffffffu, v, 16);
       acc[e] = v;
     }
+    const int buf = piece & 1;
+    if (piece >= kRedBufs &&
+        !mbar_wait(&red_empty[buf], ((piece >> 1) - 1) & 1))
+      break;
+    float *red = reinterpret_cast<float *>(smem + kRedOff + buf * kRedBufBytes);
     float *my = red + warp * kPartialFloats;
     if (lane < 8) {
 #pragma unroll
@@ -351,91 +496,20 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         my[1] = l_w;
       }
     }
-    named_bar_sync(1, kConsumerThreads);
-
-    if (threadIdx.x < kHeadDim) {
-      const int d = threadIdx.x;
-      float M = kNegBig;
-#pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w)
-        M = fmaxf(M, red[w * kPartialFloats]);
-      float L = 0.f, A = 0.f;
-#pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) {
-        const float fw = fast_exp2(red[w * kPartialFloats] - M);
-        L = fmaf(red[w * kPartialFloats + 1], fw, L);
-        A = fmaf(red[w * kPartialFloats + 4 + d], fw, A);
-      }
-      const size_t g = static_cast<size_t>(hd.g);
-      if (hd.flags & kWhole) {
-        if (a.partial_out) {
-          float *p = a.partial_out + g * kPartialFloats;
-          p[4 + d] = A;
-          if (d == 0) {
-            p[0] = M;
-            p[1] = L;
-            p[2] = 0.f;
-            p[3] = 0.f;
-          }
-        } else {
-          a.out[g * kHeadDim + d] = __float2half_rn(L > 0.f ? A / L : 0.f);
-        }
-      } else {
-        float *ws = a.ws_partials +
-                    (g + blockIdx.x) * static_cast<size_t>(kPartialFloats);
-        ws[4 + d] = A;
-        if (d == 0) {
-          ws[0] = M;
-          ws[1] = L;
-        }
-        __threadfence();
-        named_bar_sync(2, kHeadDim);
-        if (d == 0) {
-          const unsigned n_parts = static_cast<unsigned>(hd.c1 - hd.c0);
-          const unsigned old = atomicInc(&a.ws_counters[g], n_parts);
-          *last_flag = (old == n_parts) ? 1 : 0;
-        }
-        named_bar_sync(2, kHeadDim);
-        if (*last_flag) {
-          __threadfence();
-          // Every partial of the segment is in place: merge in CTA order.
-          float M2 = kNegBig;
-          for (int c = hd.c0; c <= hd.c1; ++c) {
-            const float *pp =
-                a.ws_partials + (g + c) * static_cast<size_t>(kPartialFloats);
-            if (__ldcg(pp + 1) > 0.f) M2 = fmaxf(M2, __ldcg(pp));
-          }
-          float L2 = 0.f, A2 = 0.f;
-          for (int c = hd.c0; c <= hd.c1; ++c) {
-            const float *pp =
-                a.ws_partials + (g + c) * static_cast<size_t>(kPartialFloats);
-            const float lc = __ldcg(pp + 1);
-            if (lc <= 0.f) continue;
-            const float fc = fast_exp2(__ldcg(pp) - M2);
-            L2 = fmaf(lc, fc, L2);
-            A2 = fmaf(__ldcg(pp + 4 + d), fc, A2);
-          }
-          if (a.partial_out) {
-            float *p = a.partial_out + g * kPartialFloats;
-            p[4 + d] = A2;
-            if (d == 0) {
-              p[0] = M2;
-              p[1] = L2;
-              p[2] = 0.f;
-              p[3] = 0.f;
-            }
-          } else {
-            a.out[g * kHeadDim + d] =
-                __float2half_rn(L2 > 0.f ? A2 / L2 : 0.f);
-          }
-        }
-      }
+    if (warp == 0 && lane == 0) {
+      int *hdr_out = reinterpret_cast<int *>(red + kConsumerWarps * kPartialFloats);
+      hdr_out[0] = hd.g;
+      hdr_out[1] = hd.flags;
+      hdr_out[2] = hd.c0;
+      hdr_out[3] = hd.c1;
     }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&red_full[buf]);
+    ++piece;
     m_run = kNegBig;
     l_run = 0.f;
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-    named_bar_sync(1, kConsumerThreads);
   }
 }
 

@@ -380,11 +380,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int i = 0; i < 8; ++i) mxp[i] = s[i];
 #pragma unroll
-      for (int c = 8; c < 128; c += 16) {
+      for (int c = 8; c + 16 <= 128; c += 16) {  // columns 8..119
 #pragma unroll
         for (int i = 0; i < 8; ++i)
           mxp[i] = fmax3(mxp[i], s[c + i], s[c + 8 + i]);
       }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mxp[i] = fmaxf(mxp[i], s[120 + i]);
       const float mx = fmax3(fmax3(mxp[0], mxp[1], mxp[2]),
                              fmax3(mxp[3], mxp[4], mxp[5]),
                              fmaxf(mxp[6], mxp[7]));

@@ -372,3 +372,20 @@ def test_occupancy_report_rows():
     by = {r["kernel"]: r for r in rows}
     # tensor-memory kernels run one CTA per SM
     assert by["prefill_kernel"]["max_active_blocks_per_sm"] == 1
+
+
+def test_prefill_causal_single_key_rows_are_exact():
+    """Causal row 0 attends to key 0 only, so its output is v[0] exactly
+    whatever the logits (regression: a row-max that read past the 128
+    columns of the S tile made P != 1 there)."""
+    torch.manual_seed(2256)
+    q = rand(2, 12, 256, HEAD_DIM)
+    k = rand(2, 12, 256, HEAD_DIM)
+    v = (torch.randn(2, 12, 256, HEAD_DIM, device="cuda") * 3).half()
+    out = flashattn_cuda.prefill(q, k, v, True, SCALE)
+    assert torch.equal(out[:, :, 0], v[:, :, 0])
+    # every query tile's first row attends to a full prefix; the last row of
+    # a non-causal single-key sequence too
+    one = flashattn_cuda.prefill(q[:, :, :1].contiguous(), k[:, :, :1].contiguous(),
+                                 v[:, :, :1].contiguous(), False, SCALE)
+    assert torch.equal(one[:, :, 0], v[:, :, 0])
