@@ -62,9 +62,8 @@ constexpr uint32_t kVOff = kKOff + kStages * kTileBytes;
 constexpr uint32_t kBarOff = kVOff + kStages * kTileBytes;
 // barrier slots
 constexpr int kBarQFull = 0;
-constexpr int kBarKFull = kBarQFull + 1;          // + stage
-constexpr int kBarVFull = kBarKFull + kStages;    // + stage
-constexpr int kBarKVEmpty = kBarVFull + kStages;  // + stage
+constexpr int kBarKFull = kBarQFull + 1;          // + stage: K and V tile
+constexpr int kBarKVEmpty = kBarKFull + kStages;  // + stage
 constexpr int kBarSFull = kBarKVEmpty + kStages;  // + tile
 constexpr int kBarSFree = kBarSFull + kTilesPerCta;
 constexpr int kBarPFull = kBarSFree + kTilesPerCta;
@@ -165,7 +164,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&bars[kBarQFull], 1);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&bars[kBarKFull + s], 1);
-      mbar_init(&bars[kBarVFull + s], 1);
       mbar_init(&bars[kBarKVEmpty + s], 1);
     }
     for (int t = 0; t < kTilesPerCta; ++t) {
@@ -217,11 +215,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           *abort_flag = 1;
           break;
         }
-        mbar_arrive_expect_tx(&bars[kBarKFull + s], kTileBytes);
+        mbar_arrive_expect_tx(&bars[kBarKFull + s], 2 * kTileBytes);
         tma_load_3d(smem + kKOff + s * kTileBytes, &tm_k, &bars[kBarKFull + s],
                     0, j * kBlockN, bh);
-        mbar_arrive_expect_tx(&bars[kBarVFull + s], kTileBytes);
-        tma_load_3d(smem + kVOff + s * kTileBytes, &tm_v, &bars[kBarVFull + s],
+        tma_load_3d(smem + kVOff + s * kTileBytes, &tm_v, &bars[kBarKFull + s],
                     0, j * kBlockN, bh);
         issued = j + 1;
       }
@@ -232,7 +229,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = (issued > kStages ? issued - kStages : 0); j < issued;
              ++j) {
           mbar_wait(&bars[kBarKFull + j % kStages], (j / kStages) & 1);
-          mbar_wait(&bars[kBarVFull + j % kStages], (j / kStages) & 1);
         }
       }
     }
@@ -275,7 +271,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int nt = t ? n1 : n0;
         if (!ok || j >= nt) continue;
         if (j + 1 < nt) {
-          if (!mbar_wait(&bars[kBarKFull + s1], ((j + 1) / kStages) & 1) ||
+          // K/V tile j+1 is waited on once per round (by the first tile
+          // that uses it); V_j was waited on with K_j the round before.
+          const bool need_kv = (t == 0) || (n0 <= j + 1);
+          if ((need_kv &&
+               !mbar_wait(&bars[kBarKFull + s1], ((j + 1) / kStages) & 1)) ||
               !mbar_wait(&bars[kBarSFree + t], j & 1)) {
             ok = false;
             continue;
@@ -291,8 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           FA_TRACE_EVENT(2048 + j * 16 + t * 8 + 1);
         }
-        if (!mbar_wait(&bars[kBarPFull + t], j & 1) ||
-            !mbar_wait(&bars[kBarVFull + s], (j / kStages) & 1)) {
+        if (!mbar_wait(&bars[kBarPFull + t], j & 1)) {
           ok = false;
           continue;
         }
