@@ -254,6 +254,34 @@ py::list occupancy_report() {
   return out;
 }
 
+// legacy_naive / legacy_tiled / legacy_fused: the reference's v1 exports
+// (csrc/legacy/legacy_ops.cu:19-51), same checks and messages; all three
+// run the one fp32 kernel.
+at::Tensor legacy_attention(const at::Tensor &q, const at::Tensor &k,
+                            const at::Tensor &v) {
+  TORCH_CHECK(q.is_cuda() && k.is_cuda() && v.is_cuda(),
+              "legacy kernels expect CUDA tensors");
+  TORCH_CHECK(q.scalar_type() == at::kFloat && k.scalar_type() == at::kFloat &&
+                  v.scalar_type() == at::kFloat,
+              "legacy kernels are fp32 only");
+  TORCH_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous(),
+              "legacy kernels expect contiguous tensors");
+  TORCH_CHECK(q.dim() == 2 && k.dim() == 2 && v.dim() == 2,
+              "legacy kernels are single-head: expected (N, ", kHeadDim,
+              ") tensors");
+  TORCH_CHECK(q.sizes() == k.sizes() && q.sizes() == v.sizes(),
+              "legacy kernels expect identical q/k/v shapes");
+  TORCH_CHECK(q.size(1) == kHeadDim, "legacy kernels expect head_dim == ",
+              kHeadDim);
+  const c10::cuda::CUDAGuard guard(q.device());
+  at::Tensor o = at::empty_like(q);
+  check_status(fa_legacy_attention_f32(q.data_ptr<float>(), k.data_ptr<float>(),
+                                       v.data_ptr<float>(), o.data_ptr<float>(),
+                                       to_int(q.size(0), "N"), current_stream()),
+               "fa_legacy_attention_f32");
+  return o;
+}
+
 // Reads and clears the device-side error word (0: every kernel completed).
 int64_t take_device_error() {
   unsigned int bits = 0;
@@ -286,6 +314,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("merge_partials", &merge_partials,
         "Merge (G, B, H, 68) decode partials into the fp16 output",
         py::arg("partials"));
+  m.def("legacy_naive", &legacy_attention, "v1 single-head kernel (N, 64) fp32");
+  m.def("legacy_tiled", &legacy_attention, "v1 single-head kernel (N, 64) fp32");
+  m.def("legacy_fused", &legacy_attention, "v1 single-head kernel (N, 64) fp32");
   m.def("take_device_error", &take_device_error,
         "Read and clear the device-side error word");
 }

@@ -265,6 +265,19 @@ int fa_merge_partials(const float *partials, int G, void *o, int B, int H,
              : FA_ECUDA;
 }
 
+int fa_legacy_attention_f32(const float *q, const float *k, const float *v,
+                            float *o, int N, void *stream) {
+  if (!q || !k || !v || !o || N <= 0) return FA_EINVAL;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+    return FA_EALIGN;
+  int rc = ensure_device(nullptr);
+  if (rc != FA_OK) return rc;
+  return launch_legacy_kernel(q, k, v, o, N, static_cast<cudaStream_t>(stream)) ==
+                 cudaSuccess
+             ? FA_OK
+             : FA_ECUDA;
+}
+
 int fa_choose_decode_split(int max_seq, int batch, int heads, int min_blocks) {
   const long long per_split = static_cast<long long>(batch) * heads;
   for (int split = 1024; split > 128; split >>= 1) {

@@ -4,4 +4,5 @@
 #include "capi.cu"
 #include "decode_sm100.cu"
 #include "prefill_sm100.cu"
+#include "legacy_sm100.cu"
 #include "noalloc.cu"

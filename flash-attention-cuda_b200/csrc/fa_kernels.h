@@ -48,4 +48,8 @@ int merge_threads();
 cudaError_t launch_merge_kernel(const float *partials, int G, __half *out,
                                 int B, int H, cudaStream_t stream);
 
+// ---- single-head fp32 attention (legacy_sm100.cu) -------------------------
+cudaError_t launch_legacy_kernel(const float *q, const float *k, const float *v,
+                                 float *o, int N, cudaStream_t stream);
+
 }  // namespace fa

@@ -17,6 +17,9 @@ from ._C import (  # noqa: F401
     decode,
     decode_partial,
     head_dim,
+    legacy_fused,
+    legacy_naive,
+    legacy_tiled,
     merge_partials,
     occupancy_report,
     prefill,
@@ -29,6 +32,9 @@ __all__ = [
     "head_dim",
     "occupancy_report",
     "choose_decode_split",
+    "legacy_naive",
+    "legacy_tiled",
+    "legacy_fused",
     "decode_partial",
     "merge_partials",
     "take_device_error",

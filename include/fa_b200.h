@@ -164,6 +164,15 @@ int fa_occupancy(fa_occupancy_entry *out, int max_entries, int *count);
  */
 int fa_take_device_error(unsigned int *bits);
 
+/*
+ * Single-head fp32 attention O = softmax(Q K^T / 8) V on (N, 64) fp32
+ * device arrays (non-causal), the function behind the reference's v1
+ * legacy_naive / legacy_tiled / legacy_fused exports
+ * (csrc/legacy/legacy_ops.cu:39-51, csrc/bindings.cpp:131-133).
+ */
+int fa_legacy_attention_f32(const float *q, const float *k, const float *v,
+                            float *o, int N, void *stream);
+
 /* Name of a status code. */
 const char *fa_status_string(int status);
 

@@ -127,7 +127,8 @@ def test_python_package_exports_the_reference_surface():
     import flashattn_cuda
 
     for name in ("prefill", "decode", "head_dim", "occupancy_report",
-                 "choose_decode_split", "_decode_with_split"):
+                 "choose_decode_split", "_decode_with_split", "legacy_naive",
+                 "legacy_tiled", "legacy_fused"):
         assert hasattr(flashattn_cuda, name)
     assert flashattn_cuda.head_dim == 64
     assert flashattn_cuda.choose_decode_split(512, 1, 12, 296) == 128
