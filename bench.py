@@ -336,6 +336,35 @@ def run_ours(args, rank, world, local_rank):
                        "partials + merge)" if world > 1 else "single GPU"}
         del qd, kc, vc
 
+        # ------- grouped-query variants (Qwen2.5-0.5B really has 2 K/V heads):
+        # same outputs as the pre-expanded configs without repeating K/V
+        if world == 1:
+            qg = randn(C3["B"], C3["H"], C3["N"], HEAD_DIM, seed=90)
+            kg = randn(C3["B"], 2, C3["N"], HEAD_DIM, seed=91)
+            vg = randn(C3["B"], 2, C3["N"], HEAD_DIM, seed=92)
+            t = timer.run(lambda: fa.prefill(qg, kg, vg, True, SCALE), args.steps,
+                          args.warmup) / args.steps
+            launches += args.steps
+            secondary["c3_prefill_gqa_kv2"] = {
+                "ms": round(t, 5),
+                "tflops": round(prefill_flops(C3["B"], C3["H"], C3["N"], True)
+                                / (t * 1e-3) / 1e12, 2)}
+            del qg, kg, vg
+            qd = randn(1, C5["H"], 1, HEAD_DIM, seed=93)
+            kc = randn(1, 2, C5["S"], HEAD_DIM, seed=94)
+            vc = randn(1, 2, C5["S"], HEAD_DIM, seed=95)
+            lens1 = torch.tensor([C5["S"]], dtype=torch.int32, device="cuda")
+            t = timer.run(lambda: fa.decode(qd, kc, vc, lens1, SCALE), args.steps,
+                          args.warmup) / args.steps
+            launches += args.steps
+            kv_bytes = C5["S"] * 2 * HEAD_DIM * 2 * 2
+            secondary["c5_decode_gqa_kv2"] = {
+                "ms": round(t, 5),
+                "kv_gbs": round(kv_bytes / (t * 1e-3) / 1e9, 1),
+                "note": "14 query heads over 2 K/V heads; GB/s of the K/V "
+                        "bytes that exist (each read by 7 query heads)"}
+            del qd, kc, vc
+
         # ------- the reference's own CUDA kernels on this B200 (baseline) ----
         if world == 1 and not args.no_ref_cuda:
             secondary["reference_cuda_kernels"] = ref_cuda_measure(

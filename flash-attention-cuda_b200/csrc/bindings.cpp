@@ -99,7 +99,8 @@ void check_decode_inputs(const at::Tensor &q, const at::Tensor &k_cache,
   TORCH_CHECK(k_cache.sizes() == v_cache.sizes(),
               "k_cache and v_cache must have identical shapes, got ",
               k_cache.sizes(), " and ", v_cache.sizes());
-  TORCH_CHECK(q.size(0) == k_cache.size(0) && q.size(1) == k_cache.size(1),
+  TORCH_CHECK(q.size(0) == k_cache.size(0) && k_cache.size(1) > 0 &&
+                  q.size(1) % k_cache.size(1) == 0,
               "q and the caches must agree on batch and head count, got q=",
               q.sizes(), " cache=", k_cache.sizes());
   TORCH_CHECK(k_cache.size(2) > 0, "cache length must be > 0");
@@ -125,7 +126,13 @@ at::Tensor prefill(const at::Tensor &q, const at::Tensor &k,
   check_bhnd(q, "q");
   check_bhnd(k, "k");
   check_bhnd(v, "v");
-  TORCH_CHECK(q.sizes() == k.sizes() && q.sizes() == v.sizes(),
+  // Identical shapes as in the reference; additionally k and v may have
+  // fewer heads than q when they divide it (grouped-query attention).
+  const bool same = q.sizes() == k.sizes() && q.sizes() == v.sizes();
+  const bool grouped = k.sizes() == v.sizes() && q.size(0) == k.size(0) &&
+                       q.size(2) == k.size(2) && k.size(1) > 0 &&
+                       q.size(1) % k.size(1) == 0;
+  TORCH_CHECK(same || grouped,
               "prefill expects q, k and v to have identical shapes, got q=",
               q.sizes(), " k=", k.sizes(), " v=", v.sizes());
   TORCH_CHECK(q.device() == k.device() && q.device() == v.device(),
@@ -135,11 +142,13 @@ at::Tensor prefill(const at::Tensor &q, const at::Tensor &k,
 
   const c10::cuda::CUDAGuard guard(q.device());
   at::Tensor o = at::empty_like(q);
-  check_status(fa_prefill(q.data_ptr(), k.data_ptr(), v.data_ptr(),
-                          o.data_ptr(), to_int(q.size(0), "batch"),
-                          to_int(q.size(1), "heads"),
-                          to_int(q.size(2), "sequence length"), causal ? 1 : 0,
-                          static_cast<float>(scale), current_stream()),
+  check_status(fa_prefill_gqa(q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                              o.data_ptr(), to_int(q.size(0), "batch"),
+                              to_int(q.size(1), "heads"),
+                              to_int(k.size(1), "kv heads"),
+                              to_int(q.size(2), "sequence length"),
+                              causal ? 1 : 0, static_cast<float>(scale),
+                              current_stream()),
                "fa_prefill");
   return o;
 }
@@ -164,14 +173,26 @@ at::Tensor decode_impl(const at::Tensor &q, const at::Tensor &k_cache,
       fa_decode_workspace_bytes(B, H, S, split, q.get_device());
   TORCH_CHECK(bytes > 0, "fa_decode_workspace_bytes failed");
   DecodeScratch &ws = decode_scratch(q, bytes, static_cast<size_t>(B) * H);
-  check_status(
-      fa_decode(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
-                seq_lens.data_ptr<int32_t>(), o.data_ptr(), B, H, S,
-                static_cast<float>(scale), split, ws.partials.data_ptr(),
-                static_cast<size_t>(ws.partials.numel()),
-                reinterpret_cast<uint32_t *>(ws.counters.data_ptr<int32_t>()),
-                static_cast<size_t>(ws.counters.numel()), current_stream()),
-      "fa_decode");
+  const int H_kv = to_int(k_cache.size(1), "kv heads");
+  uint32_t *ctr = reinterpret_cast<uint32_t *>(ws.counters.data_ptr<int32_t>());
+  if (H_kv == H) {
+    check_status(
+        fa_decode(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                  seq_lens.data_ptr<int32_t>(), o.data_ptr(), B, H, S,
+                  static_cast<float>(scale), split, ws.partials.data_ptr(),
+                  static_cast<size_t>(ws.partials.numel()), ctr,
+                  static_cast<size_t>(ws.counters.numel()), current_stream()),
+        "fa_decode");
+  } else {
+    TORCH_CHECK(split == 0, "a forced split size needs one K/V head per query head");
+    check_status(
+        fa_decode_gqa(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                      seq_lens.data_ptr<int32_t>(), o.data_ptr(), B, H, H_kv, S,
+                      static_cast<float>(scale), ws.partials.data_ptr(),
+                      static_cast<size_t>(ws.partials.numel()), ctr,
+                      static_cast<size_t>(ws.counters.numel()), current_stream()),
+        "fa_decode_gqa");
+  }
   return o;
 }
 
@@ -187,6 +208,8 @@ at::Tensor decode_partial(const at::Tensor &q, const at::Tensor &k_cache,
                           const at::Tensor &v_cache,
                           const at::Tensor &seq_lens, double scale) {
   check_decode_inputs(q, k_cache, v_cache, seq_lens, scale);
+  TORCH_CHECK(k_cache.size(1) == q.size(1),
+              "decode_partial needs one K/V head per query head");
   const c10::cuda::CUDAGuard guard(q.device());
   const int B = to_int(q.size(0), "batch");
   const int H = to_int(q.size(1), "heads");

@@ -147,12 +147,13 @@ bool decode_shape_ok(int B, int H, int S_max, float scale) {
   return rows < (1ll << 40) && static_cast<long long>(B) * H < (1ll << 30);
 }
 
-int run_decode(const void *q, const void *k_cache, const void *v_cache,
-               const int32_t *seq_lens, void *o, float *partial_out, int B,
-               int H, int S_max, float scale, int split_size, void *workspace,
-               size_t workspace_bytes, uint32_t *counters,
-               size_t counter_count, void *stream) {
+int run_decode_gqa(const void *q, const void *k_cache, const void *v_cache,
+                   const int32_t *seq_lens, void *o, float *partial_out, int B,
+                   int H, int H_kv, int S_max, float scale, int split_size,
+                   void *workspace, size_t workspace_bytes, uint32_t *counters,
+                   size_t counter_count, void *stream) {
   if (!decode_shape_ok(B, H, S_max, scale)) return FA_EINVAL;
+  if (H_kv <= 0 || H % H_kv != 0) return FA_EINVAL;
   if (split_size > 0 && split_size % 4 != 0) return FA_EINVAL;
   if (!q || !k_cache || !v_cache || !seq_lens || (!o && !partial_out) ||
       !workspace || !counters)
@@ -181,6 +182,7 @@ int run_decode(const void *q, const void *k_cache, const void *v_cache,
   a.B = B;
   a.H = H;
   a.S_max = S_max;
+  a.H_kv = H_kv;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.rows_per_cta = split_size > 0 ? split_size : 0;
   a.grid = grid;
@@ -188,6 +190,16 @@ int run_decode(const void *q, const void *k_cache, const void *v_cache,
                  cudaSuccess
              ? FA_OK
              : FA_ECUDA;
+}
+
+int run_decode(const void *q, const void *k_cache, const void *v_cache,
+               const int32_t *seq_lens, void *o, float *partial_out, int B,
+               int H, int S_max, float scale, int split_size, void *workspace,
+               size_t workspace_bytes, uint32_t *counters,
+               size_t counter_count, void *stream) {
+  return run_decode_gqa(q, k_cache, v_cache, seq_lens, o, partial_out, B, H, H,
+                        S_max, scale, split_size, workspace, workspace_bytes,
+                        counters, counter_count, stream);
 }
 
 }  // namespace
@@ -199,7 +211,14 @@ extern "C" {
 
 int fa_prefill(const void *q, const void *k, const void *v, void *o, int B,
                int H, int N, int causal, float scale, void *stream) {
+  return fa_prefill_gqa(q, k, v, o, B, H, H, N, causal, scale, stream);
+}
+
+int fa_prefill_gqa(const void *q, const void *k, const void *v, void *o, int B,
+                   int H, int H_kv, int N, int causal, float scale,
+                   void *stream) {
   if (B <= 0 || H <= 0 || N <= 0 || !isfinite(scale)) return FA_EINVAL;
+  if (H_kv <= 0 || H % H_kv != 0) return FA_EINVAL;
   if (static_cast<long long>(B) * H >= (1ll << 31) / 64 ||
       static_cast<long long>(N) >= (1ll << 31))
     return FA_EINVAL;
@@ -210,11 +229,11 @@ int fa_prefill(const void *q, const void *k, const void *v, void *o, int B,
   if (rc != FA_OK) return rc;
   CUtensorMap tq, tk, tv;
   if (make_bhn64_map(&tq, q, B * H, N) != FA_OK ||
-      make_bhn64_map(&tk, k, B * H, N) != FA_OK ||
-      make_bhn64_map(&tv, v, B * H, N) != FA_OK)
+      make_bhn64_map(&tk, k, B * H_kv, N) != FA_OK ||
+      make_bhn64_map(&tv, v, B * H_kv, N) != FA_OK)
     return FA_EINVAL;
   return launch_prefill_kernel(tq, tk, tv, static_cast<__half *>(o), B, H, N,
-                               causal != 0, scale,
+                               causal != 0, scale, H_kv,
                                static_cast<cudaStream_t>(stream)) == cudaSuccess
              ? FA_OK
              : FA_ECUDA;
@@ -239,6 +258,17 @@ int fa_decode(const void *q, const void *k_cache, const void *v_cache,
   return run_decode(q, k_cache, v_cache, seq_lens, o, nullptr, B, H, S_max,
                     scale, split_size, workspace, workspace_bytes, counters,
                     counter_count, stream);
+}
+
+int fa_decode_gqa(const void *q, const void *k_cache, const void *v_cache,
+                  const int32_t *seq_lens, void *o, int B, int H, int H_kv,
+                  int S_max, float scale, void *workspace,
+                  size_t workspace_bytes, uint32_t *counters,
+                  size_t counter_count, void *stream) {
+  if (!o) return FA_EINVAL;
+  return run_decode_gqa(q, k_cache, v_cache, seq_lens, o, nullptr, B, H, H_kv,
+                        S_max, scale, 0, workspace, workspace_bytes, counters,
+                        counter_count, stream);
 }
 
 int fa_decode_partial(const void *q, const void *k_cache, const void *v_cache,

@@ -306,7 +306,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         const int c0 = static_cast<int>(seg_start / per);
         const int c1 = static_cast<int>((seg_end - 1) / per);
         const int g = b * a.H + h;
-        const size_t row0 = static_cast<size_t>(g) * a.S_max + r;
+        // cache rows of this segment's K/V head
+        const int g_kv = b * a.H_kv + h / (a.H / a.H_kv);
+        const size_t row0 = static_cast<size_t>(g_kv) * a.S_max + r;
         for (long long r0 = cur; r0 < piece_end; r0 += kStageRows) {
           const int n = static_cast<int>(
               piece_end - r0 < kStageRows ? piece_end - r0 : kStageRows);

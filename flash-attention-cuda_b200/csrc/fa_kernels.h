@@ -16,7 +16,7 @@ cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
                                   const CUtensorMap &tm_k,
                                   const CUtensorMap &tm_v, __half *out, int B,
                                   int H, int N, bool causal, float scale,
-                                  cudaStream_t stream);
+                                  int H_kv, cudaStream_t stream);
 
 // ---- decode (decode_sm100.cu) ---------------------------------------------
 struct DecodeArgs {
@@ -29,6 +29,7 @@ struct DecodeArgs {
   float *ws_partials;    // (B*H + grid) x 68 fp32
   uint32_t *ws_counters; // B*H arrival counters, zero between calls
   int B, H, S_max;
+  int H_kv;  // K/V heads; H / H_kv query heads share each
   float scale_log2;
   long long rows_per_cta;  // 0: balance the valid rows over the grid
   int grid;

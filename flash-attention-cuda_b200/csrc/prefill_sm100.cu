@@ -134,7 +134,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v,
                    __half *__restrict__ out, int N, int BH, int causal,
-                   float scale_log2) {
+                   float scale_log2, int H, int group) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -151,6 +151,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_pairs = (n_qt + 1) / 2;
   const int pair = n_pairs - 1 - static_cast<int>(blockIdx.x / BH);
   const int bh = static_cast<int>(blockIdx.x % BH);
+  // K/V head of this query head: `group` query heads share one K/V head
+  // (group == 1 without grouped-query attention).
+  const int kv_bh = (bh / H) * (H / group) + (bh % H) / group;
   const TileInfo t0 = tile_info(pair, 0, N, causal);
   const TileInfo t1 = tile_info(pair, 1, N, causal);
   const int n_kv = t0.n_kv > t1.n_kv ? t0.n_kv : t1.n_kv;
@@ -217,9 +220,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_arrive_expect_tx(&bars[kBarKFull + s], 2 * kTileBytes);
         tma_load_3d(smem + kKOff + s * kTileBytes, &tm_k, &bars[kBarKFull + s],
-                    0, j * kBlockN, bh);
+                    0, j * kBlockN, kv_bh);
         tma_load_3d(smem + kVOff + s * kTileBytes, &tm_v, &bars[kBarKFull + s],
-                    0, j * kBlockN, bh);
+                    0, j * kBlockN, kv_bh);
         issued = j + 1;
       }
       // No copy of ours may still be landing when the CTA exits (matters
@@ -507,7 +510,7 @@ cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
                                   const CUtensorMap &tm_k,
                                   const CUtensorMap &tm_v, __half *out, int B,
                                   int H, int N, bool causal, float scale,
-                                  cudaStream_t stream) {
+                                  int H_kv, cudaStream_t stream) {
   static_assert(prefill::kBlockM == prefill::kBlockN,
                 "causal tile skipping assumes square tiles");
   const int BH = B * H;
@@ -518,7 +521,7 @@ cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
   const float scale_log2 = scale * 1.4426950408889634f;
   prefill::prefill_kernel<<<grid, prefill::kThreads, prefill::kSmemBytes,
                             stream>>>(tm_q, tm_k, tm_v, out, N, BH,
-                                      causal ? 1 : 0, scale_log2);
+                                      causal ? 1 : 0, scale_log2, H, H / H_kv);
   return cudaGetLastError();
 }
 

@@ -50,6 +50,18 @@ int fa_prefill(const void *q, const void *k, const void *v, void *o, int B,
                int H, int N, int causal, float scale, void *stream);
 
 /*
+ * Grouped-query prefill: q, o are (B, H, N, 64), k, v are (B, H_kv, N, 64)
+ * with H % H_kv == 0; query head h reads K/V head h / (H / H_kv). Same as
+ * fa_prefill when H_kv == H, and equal to fa_prefill on K/V heads repeated
+ * H / H_kv times, without materialising the repeat. No reference
+ * counterpart (the reference's future work, README.md:398); the BASELINE
+ * Qwen2.5-0.5B shapes have H=14, H_kv=2.
+ */
+int fa_prefill_gqa(const void *q, const void *k, const void *v, void *o, int B,
+                   int H, int H_kv, int N, int causal, float scale,
+                   void *stream);
+
+/*
  * Bytes of scratch memory fa_decode / fa_decode_partial need for this shape
  * and split choice (the log-sum-exp partials of segments split across CTAs).
  * It needs no initialisation. split_size <= 0 selects the automatic,
@@ -82,6 +94,18 @@ int fa_decode(const void *q, const void *k_cache, const void *v_cache,
               float scale, int split_size, void *workspace,
               size_t workspace_bytes, uint32_t *counters,
               size_t counter_count, void *stream);
+
+/*
+ * Grouped-query decode: q, o (B, H, 1, 64); caches (B, H_kv, S_max, 64) with
+ * H % H_kv == 0 (query head h reads K/V head h / (H / H_kv)); automatic
+ * schedule; workspace / counters as for fa_decode with the same B, H.
+ * No reference counterpart (see fa_prefill_gqa).
+ */
+int fa_decode_gqa(const void *q, const void *k_cache, const void *v_cache,
+                  const int32_t *seq_lens, void *o, int B, int H, int H_kv,
+                  int S_max, float scale, void *workspace,
+                  size_t workspace_bytes, uint32_t *counters,
+                  size_t counter_count, void *stream);
 
 /*
  * Decode that stops before normalisation and writes, per (b, h), the
