@@ -111,11 +111,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking probe of the phase. On sm_100 it answers an already completed
+// phase in a few cycles, where try_wait costs about a hundred.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Waits for the phase with the given parity to complete. Returns false (and
 // records FA_ERR_TIMEOUT) if it has not completed within kWaitLimitNs, so a
 // lost arrival turns into an error status instead of a hung GPU.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
   const uint32_t addr = smem_u32(bar);
+  if (mbar_test_wait(addr, parity)) return true;
   if (mbar_try_wait(addr, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
   while (true) {
