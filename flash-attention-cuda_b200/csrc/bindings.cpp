@@ -169,11 +169,12 @@ at::Tensor decode_impl(const at::Tensor &q, const at::Tensor &k_cache,
   const int S = to_int(k_cache.size(2), "cache length");
   const int split = split_size > 0 ? to_int(split_size, "split_size") : 0;
   at::Tensor o = at::empty_like(q);
+  const int H_kv = to_int(k_cache.size(1), "kv heads");
   const size_t bytes =
-      fa_decode_workspace_bytes(B, H, S, split, q.get_device());
+      H_kv == H ? fa_decode_workspace_bytes(B, H, S, split, q.get_device())
+                : fa_decode_gqa_workspace_bytes(B, H, H_kv, S, q.get_device());
   TORCH_CHECK(bytes > 0, "fa_decode_workspace_bytes failed");
   DecodeScratch &ws = decode_scratch(q, bytes, static_cast<size_t>(B) * H);
-  const int H_kv = to_int(k_cache.size(1), "kv heads");
   uint32_t *ctr = reinterpret_cast<uint32_t *>(ws.counters.data_ptr<int32_t>());
   if (H_kv == H) {
     check_status(

@@ -76,6 +76,9 @@ int ensure_device(int *device_out) {
       cudaFuncSetAttribute(decode_kernel_ptr(),
                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                            decode_smem_bytes()) != cudaSuccess ||
+      cudaFuncSetAttribute(decode_gqa_kernel_ptr(),
+                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           decode_gqa_smem_bytes()) != cudaSuccess ||
       // Both kernels are sized for two CTAs per SM, which needs the whole
       // unified L1/shared array configured as shared memory.
       cudaFuncSetAttribute(prefill_kernel_ptr(),
@@ -141,6 +144,42 @@ size_t workspace_bytes_for(int B, int H, int grid) {
   return (static_cast<size_t>(B) * H + grid) * kPartialFloats * sizeof(float);
 }
 
+// Grouped-query decode: segments are (b, K/V head, chunk of up to
+// decode_gqa_max_heads() query heads); partial slots hold one 68-float
+// record per query head of a segment.
+struct GqaPlan {
+  int n_seg_per_b;   // segments per batch entry
+  int heads_per_seg; // query heads per segment (at most 16)
+};
+
+GqaPlan gqa_plan(int H, int H_kv) {
+  const int group = H / H_kv;
+  const int mh = decode_gqa_max_heads();
+  GqaPlan p;
+  const int n_hc = (group + mh - 1) / mh;
+  p.n_seg_per_b = H_kv * n_hc;
+  p.heads_per_seg = group < mh ? group : mh;
+  return p;
+}
+
+int decode_gqa_grid(int sms, int B, const GqaPlan &p, int S_max,
+                    int split_size) {
+  const long long cap_rows = static_cast<long long>(B) * p.n_seg_per_b * S_max;
+  long long g;
+  if (split_size > 0) {
+    g = (cap_rows + split_size - 1) / split_size;
+  } else {
+    g = (cap_rows + decode_min_rows_per_cta() - 1) / decode_min_rows_per_cta();
+    if (g > sms) g = sms;  // one CTA per SM
+  }
+  return static_cast<int>(g < 1 ? 1 : g);
+}
+
+size_t gqa_workspace_bytes_for(int B, const GqaPlan &p, int grid) {
+  return (static_cast<size_t>(B) * p.n_seg_per_b + grid) * p.heads_per_seg *
+         kPartialFloats * sizeof(float);
+}
+
 bool decode_shape_ok(int B, int H, int S_max, float scale) {
   if (B <= 0 || H <= 0 || S_max <= 0 || !isfinite(scale)) return false;
   const long long rows = static_cast<long long>(B) * H * S_max;
@@ -166,9 +205,14 @@ int run_decode_gqa(const void *q, const void *k_cache, const void *v_cache,
   int dev = 0;
   int rc = ensure_device(&dev);
   if (rc != FA_OK) return rc;
-  const int grid = decode_grid(g_devices[dev].sms, B, H, S_max, split_size);
-  if (workspace_bytes < workspace_bytes_for(B, H, grid) ||
-      counter_count < static_cast<size_t>(B) * H)
+  const bool grouped = H_kv < H;
+  const GqaPlan plan = gqa_plan(H, H_kv);
+  const int grid =
+      grouped ? decode_gqa_grid(g_devices[dev].sms, B, plan, S_max, split_size)
+              : decode_grid(g_devices[dev].sms, B, H, S_max, split_size);
+  const size_t need = grouped ? gqa_workspace_bytes_for(B, plan, grid)
+                              : workspace_bytes_for(B, H, grid);
+  if (workspace_bytes < need || counter_count < static_cast<size_t>(B) * H)
     return FA_ENOSPACE;
   DecodeArgs a;
   a.q = static_cast<const __half *>(q);
@@ -186,6 +230,17 @@ int run_decode_gqa(const void *q, const void *k_cache, const void *v_cache,
   a.scale_log2 = scale * 1.4426950408889634f;
   a.rows_per_cta = split_size > 0 ? split_size : 0;
   a.grid = grid;
+  if (grouped) {
+    CUtensorMap tk, tv;
+    if (make_bhn64_map(&tk, k_cache, B * H_kv, S_max) != FA_OK ||
+        make_bhn64_map(&tv, v_cache, B * H_kv, S_max) != FA_OK)
+      return FA_EINVAL;
+    return launch_decode_gqa_kernel(a, tk, tv,
+                                    static_cast<cudaStream_t>(stream)) ==
+                   cudaSuccess
+               ? FA_OK
+               : FA_ECUDA;
+  }
   return launch_decode_kernel(a, static_cast<cudaStream_t>(stream)) ==
                  cudaSuccess
              ? FA_OK
@@ -247,6 +302,19 @@ size_t fa_decode_workspace_bytes(int B, int H, int S_max, int split_size,
       cudaSuccess)
     return 0;
   return workspace_bytes_for(B, H, decode_grid(sms, B, H, S_max, split_size));
+}
+
+size_t fa_decode_gqa_workspace_bytes(int B, int H, int H_kv, int S_max,
+                                     int device) {
+  if (B <= 0 || H <= 0 || S_max <= 0 || H_kv <= 0 || H % H_kv != 0) return 0;
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) !=
+      cudaSuccess)
+    return 0;
+  if (H_kv == H)
+    return workspace_bytes_for(B, H, decode_grid(sms, B, H, S_max, 0));
+  const GqaPlan p = gqa_plan(H, H_kv);
+  return gqa_workspace_bytes_for(B, p, decode_gqa_grid(sms, B, p, S_max, 0));
 }
 
 int fa_decode(const void *q, const void *k_cache, const void *v_cache,

@@ -44,6 +44,17 @@ int decode_ctas_per_sm();
 int decode_min_rows_per_cta();
 cudaError_t launch_decode_kernel(const DecodeArgs &args, cudaStream_t stream);
 
+// Grouped-query decode: K/V read once per group of query heads. The grid is
+// one CTA per SM at most; segments are (b, K/V head, chunk of up to
+// decode_gqa_max_heads() query heads).
+const void *decode_gqa_kernel_ptr();
+int decode_gqa_smem_bytes();
+int decode_gqa_max_heads();
+cudaError_t launch_decode_gqa_kernel(const DecodeArgs &args,
+                                     const CUtensorMap &tm_k,
+                                     const CUtensorMap &tm_v,
+                                     cudaStream_t stream);
+
 const void *merge_kernel_ptr();
 int merge_threads();
 cudaError_t launch_merge_kernel(const float *partials, int G, __half *out,

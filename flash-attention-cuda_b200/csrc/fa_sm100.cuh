@@ -329,6 +329,39 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n,
 }
 
 // ---------------------------------------------------------------------------
+// Warp-level tensor-core operations (register operands)
+// ---------------------------------------------------------------------------
+// Four 8x8 16-bit matrices from shared memory; lanes 8i..8i+7 give the row
+// addresses of matrix i. Lane t receives row t / 4, elements 2 (t % 4) and
+// 2 (t % 4) + 1 of each matrix (the transposed variant: column t / 4, rows
+// 2 (t % 4) and 2 (t % 4) + 1).
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile(
+      "ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+      : "r"(addr)
+      : "memory");
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr,
+                                              uint32_t (&r)[4]) {
+  asm volatile(
+      "ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+      : "r"(addr)
+      : "memory");
+}
+
+// D (16x8 fp32) += A (16x16 fp16, row) * B (16x8 fp16, col).
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4],
+                                          uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, "
+      "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// ---------------------------------------------------------------------------
 // Math helpers
 // ---------------------------------------------------------------------------
 // 2^x with the MUFU approximation (hardware ex2, flush-to-zero).

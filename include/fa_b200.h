@@ -96,9 +96,19 @@ int fa_decode(const void *q, const void *k_cache, const void *v_cache,
               size_t counter_count, void *stream);
 
 /*
+ * Scratch bytes fa_decode_gqa needs for this shape (0 on invalid arguments).
+ * No reference counterpart.
+ */
+size_t fa_decode_gqa_workspace_bytes(int B, int H, int H_kv, int S_max,
+                                     int device);
+
+/*
  * Grouped-query decode: q, o (B, H, 1, 64); caches (B, H_kv, S_max, 64) with
  * H % H_kv == 0 (query head h reads K/V head h / (H / H_kv)); automatic
- * schedule; workspace / counters as for fa_decode with the same B, H.
+ * schedule; workspace of fa_decode_gqa_workspace_bytes() bytes; counters as
+ * for fa_decode with the same B, H.
+ * With H_kv < H every K/V row is read once for its whole group of query
+ * heads (up to 16 per pass; larger groups take several passes).
  * No reference counterpart (see fa_prefill_gqa).
  */
 int fa_decode_gqa(const void *q, const void *k_cache, const void *v_cache,
