@@ -309,7 +309,33 @@ def run_ours(args, rank, world, local_rank):
             "tokens_per_s": round(C4["B"] / (t * 1e-3), 1),
             "traffic_bytes_per_launch_ncu": read_profile_traffic("decode_kernel_c4"),
             "scaling": "strong (batch sharded, LPT by length)"}
-        del qd, kc, vc
+
+        # the same step with the new token's K/V row appended in the launch,
+        # against the unfused sequence (cache row write, then decode)
+        lens_a = (lens - 1).contiguous()
+        kn = randn(bm, C4["H"], 1, HEAD_DIM, seed=43 + rank)
+        vn = randn(bm, C4["H"], 1, HEAD_DIM, seed=44 + rank)
+        rows = torch.arange(bm, device="cuda")
+        pos = lens_a.long()
+        t_fused = timer.run(
+            lambda: fa.decode_append(qd, kn, vn, kc, vc, lens_a, SCALE),
+            args.steps, args.warmup) / args.steps
+        launches += args.steps
+
+        def unfused():
+            kc[rows, :, pos] = kn[:, :, 0]
+            vc[rows, :, pos] = vn[:, :, 0]
+            return fa.decode(qd, kc, vc, lens, SCALE)
+
+        t_unfused = timer.run(unfused, args.steps, args.warmup) / args.steps
+        launches += args.steps
+        secondary["c4_decode_append"] = {
+            "ms": round(t_fused, 5),
+            "gbs_per_gpu_rank0": round(bytes_rank / (t_fused * 1e-3) / 1e9, 1),
+            "unfused_ms": round(t_unfused, 5),
+            "note": "decode_append (row store + attention in one launch) vs "
+                    "two index_put copies + decode"}
+        del qd, kc, vc, kn, vn
 
         # ---------------- secondary: C5 long decode, sequence-sharded ----
         S = C5["S"]

@@ -231,6 +231,45 @@ at::Tensor decode_partial(const at::Tensor &q, const at::Tensor &k_cache,
   return part;
 }
 
+// decode_append(q, k_new, v_new, k_cache, v_cache, seq_lens, scale): stores
+// the new token's K/V rows at row seq_lens[b] of the caches (in place) and
+// attends rows [0, seq_lens[b] + 1) in the same launch. No reference
+// counterpart (its callers copy the row into the cache before decode()).
+at::Tensor decode_append(const at::Tensor &q, const at::Tensor &k_new,
+                         const at::Tensor &v_new, at::Tensor k_cache,
+                         at::Tensor v_cache, const at::Tensor &seq_lens,
+                         double scale) {
+  check_decode_inputs(q, k_cache, v_cache, seq_lens, scale);
+  check_bhnd(k_new, "k_new");
+  check_bhnd(v_new, "v_new");
+  TORCH_CHECK(k_new.sizes() == v_new.sizes() && k_new.size(0) == k_cache.size(0) &&
+                  k_new.size(1) == k_cache.size(1) && k_new.size(2) == 1,
+              "k_new and v_new must be (B, H_kv, 1, 64) matching the caches, got ",
+              k_new.sizes(), " and ", v_new.sizes());
+  TORCH_CHECK(k_new.device() == q.device() && v_new.device() == q.device(),
+              "k_new and v_new must live on the device of q");
+  const c10::cuda::CUDAGuard guard(q.device());
+  const int B = to_int(q.size(0), "batch");
+  const int H = to_int(q.size(1), "heads");
+  const int H_kv = to_int(k_cache.size(1), "kv heads");
+  const int S = to_int(k_cache.size(2), "cache length");
+  at::Tensor o = at::empty_like(q);
+  const size_t bytes =
+      fa_decode_gqa_workspace_bytes(B, H, H_kv, S, q.get_device());
+  TORCH_CHECK(bytes > 0, "fa_decode_gqa_workspace_bytes failed");
+  DecodeScratch &ws = decode_scratch(q, bytes, static_cast<size_t>(B) * H);
+  check_status(
+      fa_decode_append(q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(),
+                       k_cache.data_ptr(), v_cache.data_ptr(),
+                       seq_lens.data_ptr<int32_t>(), o.data_ptr(), B, H, H_kv,
+                       S, static_cast<float>(scale), ws.partials.data_ptr(),
+                       static_cast<size_t>(ws.partials.numel()),
+                       reinterpret_cast<uint32_t *>(ws.counters.data_ptr<int32_t>()),
+                       static_cast<size_t>(ws.counters.numel()), current_stream()),
+      "fa_decode_append");
+  return o;
+}
+
 // Merges (G, B, H, 68) partials into the fp16 (B, H, 1, 64) output.
 at::Tensor merge_partials(const at::Tensor &partials) {
   check_cuda(partials, "partials");
@@ -335,6 +374,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "Log-sum-exp partials of decode over this device's cache rows",
         py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
         py::arg("seq_lens"), py::arg("scale"));
+  m.def("decode_append", &decode_append,
+        "Decode with the new token's K/V row stored into the cache in the same launch",
+        py::arg("q"), py::arg("k_new"), py::arg("v_new"), py::arg("k_cache"),
+        py::arg("v_cache"), py::arg("seq_lens"), py::arg("scale"));
   m.def("merge_partials", &merge_partials,
         "Merge (G, B, H, 68) decode partials into the fp16 output",
         py::arg("partials"));

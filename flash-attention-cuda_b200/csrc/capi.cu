@@ -190,7 +190,8 @@ int run_decode_gqa(const void *q, const void *k_cache, const void *v_cache,
                    const int32_t *seq_lens, void *o, float *partial_out, int B,
                    int H, int H_kv, int S_max, float scale, int split_size,
                    void *workspace, size_t workspace_bytes, uint32_t *counters,
-                   size_t counter_count, void *stream) {
+                   size_t counter_count, void *stream,
+                   const void *k_new = nullptr, const void *v_new = nullptr) {
   if (!decode_shape_ok(B, H, S_max, scale)) return FA_EINVAL;
   if (H_kv <= 0 || H % H_kv != 0) return FA_EINVAL;
   if (split_size > 0 && split_size % 4 != 0) return FA_EINVAL;
@@ -214,7 +215,13 @@ int run_decode_gqa(const void *q, const void *k_cache, const void *v_cache,
                               : workspace_bytes_for(B, H, grid);
   if (workspace_bytes < need || counter_count < static_cast<size_t>(B) * H)
     return FA_ENOSPACE;
+  if ((k_new == nullptr) != (v_new == nullptr)) return FA_EINVAL;
+  if (k_new && (!aligned16(k_new) || !aligned16(v_new))) return FA_EALIGN;
   DecodeArgs a;
+  a.k_new = static_cast<const __half *>(k_new);
+  a.v_new = static_cast<const __half *>(v_new);
+  a.k_cache_w = k_new ? static_cast<__half *>(const_cast<void *>(k_cache)) : nullptr;
+  a.v_cache_w = k_new ? static_cast<__half *>(const_cast<void *>(v_cache)) : nullptr;
   a.q = static_cast<const __half *>(q);
   a.k = static_cast<const __half *>(k_cache);
   a.v = static_cast<const __half *>(v_cache);
@@ -337,6 +344,17 @@ int fa_decode_gqa(const void *q, const void *k_cache, const void *v_cache,
   return run_decode_gqa(q, k_cache, v_cache, seq_lens, o, nullptr, B, H, H_kv,
                         S_max, scale, 0, workspace, workspace_bytes, counters,
                         counter_count, stream);
+}
+
+int fa_decode_append(const void *q, const void *k_new, const void *v_new,
+                     void *k_cache, void *v_cache, const int32_t *seq_lens,
+                     void *o, int B, int H, int H_kv, int S_max, float scale,
+                     void *workspace, size_t workspace_bytes,
+                     uint32_t *counters, size_t counter_count, void *stream) {
+  if (!o || !k_new || !v_new) return FA_EINVAL;
+  return run_decode_gqa(q, k_cache, v_cache, seq_lens, o, nullptr, B, H, H_kv,
+                        S_max, scale, 0, workspace, workspace_bytes, counters,
+                        counter_count, stream, k_new, v_new);
 }
 
 int fa_decode_partial(const void *q, const void *k_cache, const void *v_cache,

@@ -59,7 +59,8 @@ struct StageHeader {
   int flags;  // kLast | kWhole | kDone
   int c0;     // first CTA covering the segment
   int c1;     // last CTA covering the segment
-  int pad[3];
+  int r0;     // segment row of the stage's first row
+  int pad[2];
 };
 constexpr int kLast = 1;   // last stage of this CTA's piece of the segment
 constexpr int kWhole = 2;  // the segment lies entirely inside this CTA
@@ -82,6 +83,61 @@ constexpr float kNegBig = -1e30f;  // finite "no max yet", as the reference
 
 __device__ __forceinline__ int clamp_len(int len, int s_max) {
   return len < 0 ? 0 : (len > s_max ? s_max : len);
+}
+
+// Rows sequence b attends. With a fused append the new token's row
+// (index max(len, 0)) is added while it still fits in the cache.
+__device__ __forceinline__ int seq_rows(const DecodeArgs &a, int b) {
+  const int len = a.seq_lens[b];
+  if (!a.k_new) return clamp_len(len, a.S_max);
+  return clamp_len((len < 0 ? 0 : len) + 1, a.S_max);
+}
+
+// Row of sequence b that holds the appended token, or -1 (no append, or the
+// cache is full and the token is not stored).
+__device__ __forceinline__ int appended_row(const DecodeArgs &a, int b) {
+  if (!a.k_new) return -1;
+  const int len = a.seq_lens[b] < 0 ? 0 : a.seq_lens[b];
+  return len < a.S_max ? len : -1;
+}
+
+// The appended token's 16-byte chunk held by this lane (lanes 0-7: K,
+// 8-15: V; other lanes get zeros), loaded when a segment starts so the load
+// overlaps the query load.
+__device__ __forceinline__ uint4 load_new_row(const DecodeArgs &a, int g_kv) {
+  const int lane = threadIdx.x & 31;
+  if (lane >= 16) return make_uint4(0, 0, 0, 0);
+  const __half *src =
+      (lane >= 8 ? a.v_new : a.k_new) + static_cast<size_t>(g_kv) * kHeadDim;
+  return reinterpret_cast<const uint4 *>(src)[lane & 7];
+}
+
+// Fused append, run by the warp that owns stage row `local` of plane g_kv:
+// the new K/V row (val from load_new_row) replaces the stale cache row in
+// shared memory (16-byte chunk c of a row sits at chunk c ^ (row & 7) when
+// the stage is swizzled) and, when `store` is set, is written to the cache.
+template <bool kSwizzled>
+__device__ __forceinline__ void patch_new_row(const DecodeArgs &a, int g_kv,
+                                              int row_in_plane, int local,
+                                              uint8_t *k_stage,
+                                              uint8_t *v_stage, bool store,
+                                              uint4 val) {
+  const int lane = threadIdx.x & 31;
+  if (lane < 16) {
+    const int c = lane & 7;
+    const bool is_v = lane >= 8;
+    const int pc = kSwizzled ? (c ^ (local & 7)) : c;
+    uint8_t *stage = is_v ? v_stage : k_stage;
+    *reinterpret_cast<uint4 *>(stage + local * kRowBytes + pc * 16) = val;
+    if (store) {
+      __half *dst = (is_v ? a.v_cache_w : a.k_cache_w) +
+                    (static_cast<size_t>(g_kv) * a.S_max + row_in_plane) * kHeadDim;
+      reinterpret_cast<uint4 *>(dst)[c] = val;
+    }
+  }
+  // the stage is refilled by the async proxy once it is released
+  fence_proxy_async_smem();
+  __syncwarp();
 }
 
 __device__ __forceinline__ long long warp_sum_ll(long long v) {
@@ -222,7 +278,7 @@ __device__ void produce(const DecodeArgs &a, int nseg, int seg_per_plane,
     // ------------------------------------------------------------ planning
     long long sum_len = 0;
     for (int b = lane; b < a.B; b += 32) {
-      const int len = clamp_len(a.seq_lens[b], a.S_max);
+      const int len = seq_rows(a, b);
       sum_len += len;
       if (len == 0 && (b % static_cast<int>(gridDim.x)) ==
                           static_cast<int>(blockIdx.x)) {
@@ -247,8 +303,7 @@ __device__ void produce(const DecodeArgs &a, int nseg, int seg_per_plane,
       for (int chunk = 0; chunk < a.B; chunk += 32) {
         const int b = chunk + lane;
         const long long rows =
-            b < a.B ? static_cast<long long>(clamp_len(a.seq_lens[b], a.S_max)) *
-                          nseg
+            b < a.B ? static_cast<long long>(seq_rows(a, b)) * nseg
                     : 0;
         long long incl = rows;
 #pragma unroll
@@ -278,7 +333,7 @@ __device__ void produce(const DecodeArgs &a, int nseg, int seg_per_plane,
       long long cur = start;
       int b = b_start;
       while (ok && cur < end && b < a.B) {
-        const int len = clamp_len(a.seq_lens[b], a.S_max);
+        const int len = seq_rows(a, b);
         if (len == 0) {
           ++b;
           continue;
@@ -310,6 +365,7 @@ __device__ void produce(const DecodeArgs &a, int nseg, int seg_per_plane,
           hd.flags = (r0 + n == piece_end ? kLast : 0) | (c0 == c1 ? kWhole : 0);
           hd.c0 = c0;
           hd.c1 = c1;
+          hd.r0 = r + static_cast<int>(r0 - cur);
           if (kTiled) {
             // whole 128-row boxes, 128-byte swizzled; rows past the piece
             // are loaded but masked by the consumers
@@ -393,6 +449,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   const int sub = lane & 7;   // head dims [8*sub, 8*sub + 8)
   float qf[8];
   int cur_g = -1;
+  int app_row = -1;  // segment row of the appended token, -1 for none
+  uint4 app_val = make_uint4(0, 0, 0, 0);
   float m_run = kNegBig, l_run = 0.f;
   int piece = 0;  // pieces handed to the merger warp so far
   float acc[8];
@@ -420,6 +478,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     }
     if (hd.g != cur_g) {
       cur_g = hd.g;
+      if (a.k_new) {
+        const int b = cur_g / a.H;
+        app_row = appended_row(a, b);
+        if (app_row >= 0)
+          app_val = load_new_row(a, b * a.H_kv + (cur_g - b * a.H) / (a.H / a.H_kv));
+      }
       const uint4 qv = *reinterpret_cast<const uint4 *>(
           a.q + static_cast<size_t>(cur_g) * kHeadDim + sub * 8);
       const __half2 *qh = reinterpret_cast<const __half2 *>(&qv);
@@ -431,6 +495,18 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       }
     }
 
+    if (app_row >= 0) {
+      const int local = app_row - hd.r0;
+      if (local >= 0 && local < hd.n && warp == local / kRowsPerWarp) {
+        const int b = hd.g / a.H;
+        const int h = hd.g - b * a.H;
+        const int group = a.H / a.H_kv;
+        patch_new_row<false>(a, b * a.H_kv + h / group, app_row, local,
+                             smem + kKOff + slot * kStageBytes,
+                             smem + kVOff + slot * kStageBytes, h % group == 0,
+                             app_val);
+      }
+    }
     const uint32_t kb = smem_u32(smem + kKOff + slot * kStageBytes);
     const uint32_t vb = smem_u32(smem + kVOff + slot * kStageBytes);
     const int row_base = warp * kRowsPerWarp + grp;
@@ -869,6 +945,8 @@ __device__ __forceinline__ void gqa_consume(
   float o[8][4];               // O: dims 8dt + 2qid (+1), rows quad / quad+8
   float m_r[2], l_r[2];
   int cur_g = -1;
+  int app_row = -1;  // segment row of the appended token, -1 for none
+  uint4 app_val = make_uint4(0, 0, 0, 0);
   int piece = 0;
   auto reset = [&]() {
     m_r[0] = m_r[1] = kNegBig;
@@ -902,6 +980,9 @@ __device__ __forceinline__ void gqa_consume(
     if (hd.g != cur_g) {
       cur_g = hd.g;
       const GqaSegment sg = gqa_segment(a, cur_g, nseg, n_hc, group);
+      app_row = a.k_new ? appended_row(a, sg.b) : -1;
+      if (app_row >= 0)
+        app_val = load_new_row(a, sg.b * a.H_kv + (cur_g - sg.b * nseg) / n_hc);
       const uint32_t *q0 =
           quad < sg.hv
               ? reinterpret_cast<const uint32_t *>(
@@ -921,6 +1002,17 @@ __device__ __forceinline__ void gqa_consume(
       }
     }
 
+    if (app_row >= 0) {
+      const int local = app_row - hd.r0;
+      if (local >= key0 && local < key0 + 16 && local < hd.n) {
+        const int b = hd.g / nseg;
+        const int s_in_b = hd.g - b * nseg;
+        patch_new_row<true>(a, b * a.H_kv + s_in_b / n_hc, app_row, local,
+                            smem + kGqaKOff + slot * kStageBytes,
+                            smem + kGqaVOff + slot * kStageBytes,
+                            s_in_b % n_hc == 0, app_val);
+      }
+    }
     if (key0 < hd.n) {  // warp-uniform
       const uint32_t kb = smem_u32(smem + kGqaKOff + slot * kStageBytes);
       const uint32_t vb = smem_u32(smem + kGqaVOff + slot * kStageBytes);

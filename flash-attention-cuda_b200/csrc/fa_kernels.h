@@ -28,6 +28,13 @@ struct DecodeArgs {
   float *partial_out;    // (B, H, 68) log-sum-exp partials when non-null
   float *ws_partials;    // (B*H + grid) x 68 fp32
   uint32_t *ws_counters; // B*H arrival counters, zero between calls
+  // fused append (null when not appending): the new token's K/V rows
+  // (B, H_kv, 64), stored at row seq_lens[b] of the caches (written through
+  // k_cache_w / v_cache_w, the same caches as k / v) and attended
+  const __half *k_new;
+  const __half *v_new;
+  __half *k_cache_w;
+  __half *v_cache_w;
   int B, H, S_max;
   int H_kv;  // K/V heads; H / H_kv query heads share each
   float scale_log2;

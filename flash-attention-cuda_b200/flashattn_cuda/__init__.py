@@ -15,6 +15,7 @@ from ._C import (  # noqa: F401
     _decode_with_split,
     choose_decode_split,
     decode,
+    decode_append,
     decode_partial,
     head_dim,
     legacy_fused,
@@ -35,6 +36,7 @@ __all__ = [
     "legacy_naive",
     "legacy_tiled",
     "legacy_fused",
+    "decode_append",
     "decode_partial",
     "merge_partials",
     "take_device_error",

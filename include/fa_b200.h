@@ -103,6 +103,24 @@ size_t fa_decode_gqa_workspace_bytes(int B, int H, int H_kv, int S_max,
                                      int device);
 
 /*
+ * Decode with the KV-cache append fused in: for every sequence b the new
+ * token's k_new / v_new rows (B, H_kv, 1, 64) fp16 are stored at row
+ * p = max(seq_lens[b], 0) of k_cache / v_cache (B, H_kv, S_max, 64) and the
+ * query attends rows [0, p + 1). When p >= S_max the cache is full: nothing
+ * is stored and rows [0, S_max) are attended. seq_lens is only read (the
+ * caller advances it). H_kv == H or H % H_kv == 0 as for fa_decode_gqa;
+ * workspace of fa_decode_gqa_workspace_bytes(B, H, H_kv, S_max) bytes,
+ * counters as for fa_decode. The reference has no append; its callers write
+ * the cache row with a separate copy before decode (the step named as the
+ * caller of csrc/decode.cu:194-240).
+ */
+int fa_decode_append(const void *q, const void *k_new, const void *v_new,
+                     void *k_cache, void *v_cache, const int32_t *seq_lens,
+                     void *o, int B, int H, int H_kv, int S_max, float scale,
+                     void *workspace, size_t workspace_bytes,
+                     uint32_t *counters, size_t counter_count, void *stream);
+
+/*
  * Grouped-query decode: q, o (B, H, 1, 64); caches (B, H_kv, S_max, 64) with
  * H % H_kv == 0 (query head h reads K/V head h / (H / H_kv)); automatic
  * schedule; workspace of fa_decode_gqa_workspace_bytes() bytes; counters as
