@@ -22,13 +22,17 @@ import flashattn_cuda as fa  # noqa: E402
 SCALE = 1.0 / math.sqrt(64)
 
 CASES = {
-    # name: (kind, shape, causal)
-    "prefill_c3": ("prefill", (4, 14, 4096), True),
-    "prefill_c2_causal": ("prefill", (8, 12, 1024), True),
-    "prefill_c2_full": ("prefill", (8, 12, 1024), False),
-    "prefill_small": ("prefill", (1, 8, 2048), True),
-    "decode_c4": ("decode", (64, 12, 8192), None),
-    "decode_c5": ("decode", (1, 14, 131072), None),
+    # name: (kind, shape, causal, K/V heads (None: as many as query heads))
+    "prefill_c3": ("prefill", (4, 14, 4096), True, None),
+    "prefill_c2_causal": ("prefill", (8, 12, 1024), True, None),
+    "prefill_c2_full": ("prefill", (8, 12, 1024), False, None),
+    "prefill_small": ("prefill", (1, 8, 2048), True, None),
+    "decode_c4": ("decode", (64, 12, 8192), None, None),
+    "decode_c5": ("decode", (1, 14, 131072), None, None),
+    # Qwen2.5-0.5B's real 2 K/V heads, and a wider grouped batch
+    "decode_gqa_c5": ("decode", (1, 14, 131072), None, 2),
+    "decode_gqa_b8": ("decode", (8, 32, 32768), None, 8),
+    "decode_append_c4": ("decode_append", (64, 12, 8192), None, None),
 }
 
 
@@ -37,7 +41,8 @@ def main():
     ap.add_argument("--case", choices=sorted(CASES), required=True)
     ap.add_argument("--iters", type=int, default=3)
     args = ap.parse_args()
-    kind, (b, h, n), causal = CASES[args.case]
+    kind, (b, h, n), causal, h_kv = CASES[args.case]
+    h_kv = h_kv or h
     g = torch.Generator(device="cuda").manual_seed(0)
     if kind == "prefill":
         q, k, v = (torch.randn(b, h, n, 64, generator=g, device="cuda",
@@ -45,7 +50,7 @@ def main():
         fn = lambda: fa.prefill(q, k, v, causal, SCALE)
     else:
         q = torch.randn(b, h, 1, 64, generator=g, device="cuda", dtype=torch.float16)
-        k, v = (torch.randn(b, h, n, 64, generator=g, device="cuda",
+        k, v = (torch.randn(b, h_kv, n, 64, generator=g, device="cuda",
                             dtype=torch.float16) for _ in range(2))
         cpu_gen = torch.Generator().manual_seed(0)
         if b > 1:
@@ -53,7 +58,13 @@ def main():
         else:
             lens = torch.full((b,), n, dtype=torch.int32)
         lens = lens.cuda()
-        fn = lambda: fa.decode(q, k, v, lens, SCALE)
+        if kind == "decode_append":
+            kn, vn = (torch.randn(b, h_kv, 1, 64, generator=g, device="cuda",
+                                  dtype=torch.float16) for _ in range(2))
+            lens = (lens - 1).contiguous()
+            fn = lambda: fa.decode_append(q, kn, vn, k, v, lens, SCALE)
+        else:
+            fn = lambda: fa.decode(q, k, v, lens, SCALE)
     for _ in range(args.iters):
         fn()
     torch.cuda.synchronize()
