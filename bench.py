@@ -371,6 +371,21 @@ def run_ours(args, rank, world, local_rank):
             t = timer.run(lambda: fa.prefill(qg, kg, vg, True, SCALE), args.steps,
                           args.warmup) / args.steps
             launches += args.steps
+            qh = randn(C3["B"], C3["H"], C3["N"], 128, seed=96)
+            kh = randn(C3["B"], C3["H"], C3["N"], 128, seed=97)
+            vh = randn(C3["B"], C3["H"], C3["N"], 128, seed=98)
+            t128 = timer.run(lambda: fa.prefill(qh, kh, vh, True, 128 ** -0.5),
+                             args.steps, args.warmup) / args.steps
+            launches += args.steps
+            f128 = prefill_flops(C3["B"], C3["H"], C3["N"], True) * 2
+            secondary["c3_prefill_d128"] = {
+                "ms": round(t128, 5),
+                "tflops": round(f128 / (t128 * 1e-3) / 1e12, 2),
+                "frac_of_measured_bf16_peak": round(
+                    f128 / (t128 * 1e-3) / 1e12 / peak, 4),
+                "note": "config 3 shape at head_dim 128 (the reference's named "
+                        "next size), causal"}
+            del qh, kh, vh
             secondary["c3_prefill_gqa_kv2"] = {
                 "ms": round(t, 5),
                 "tflops": round(prefill_flops(C3["B"], C3["H"], C3["N"], True)

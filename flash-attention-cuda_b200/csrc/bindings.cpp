@@ -43,6 +43,18 @@ void check_bhnd(const at::Tensor &t, const char *name) {
               kHeadDim, ", got ", t.size(3));
 }
 
+// Prefill also takes head_dim 128 (a kernel of its own).
+void check_bhnd_prefill(const at::Tensor &t, const char *name) {
+  check_cuda(t, name);
+  check_half(t, name);
+  check_contiguous(t, name);
+  TORCH_CHECK(t.dim() == 4, name, " must be 4-D (B, H, N, ", kHeadDim,
+              "), got ", t.dim(), "-D");
+  TORCH_CHECK(t.size(3) == kHeadDim || t.size(3) == 128, name,
+              " must have head_dim == ", kHeadDim, " (or 128), got ",
+              t.size(3));
+}
+
 void check_status(int rc, const char *what) {
   TORCH_CHECK(rc == FA_OK, what, " failed: ", fa_status_string(rc));
 }
@@ -123,15 +135,15 @@ void check_decode_inputs(const at::Tensor &q, const at::Tensor &k_cache,
 // prefill(q, k, v, causal, scale): reference csrc/bindings.cpp:10-27.
 at::Tensor prefill(const at::Tensor &q, const at::Tensor &k,
                    const at::Tensor &v, bool causal, double scale) {
-  check_bhnd(q, "q");
-  check_bhnd(k, "k");
-  check_bhnd(v, "v");
+  check_bhnd_prefill(q, "q");
+  check_bhnd_prefill(k, "k");
+  check_bhnd_prefill(v, "v");
   // Identical shapes as in the reference; additionally k and v may have
   // fewer heads than q when they divide it (grouped-query attention).
   const bool same = q.sizes() == k.sizes() && q.sizes() == v.sizes();
   const bool grouped = k.sizes() == v.sizes() && q.size(0) == k.size(0) &&
-                       q.size(2) == k.size(2) && k.size(1) > 0 &&
-                       q.size(1) % k.size(1) == 0;
+                       q.size(2) == k.size(2) && q.size(3) == k.size(3) &&
+                       k.size(1) > 0 && q.size(1) % k.size(1) == 0;
   TORCH_CHECK(same || grouped,
               "prefill expects q, k and v to have identical shapes, got q=",
               q.sizes(), " k=", k.sizes(), " v=", v.sizes());
@@ -142,13 +154,13 @@ at::Tensor prefill(const at::Tensor &q, const at::Tensor &k,
 
   const c10::cuda::CUDAGuard guard(q.device());
   at::Tensor o = at::empty_like(q);
-  check_status(fa_prefill_gqa(q.data_ptr(), k.data_ptr(), v.data_ptr(),
-                              o.data_ptr(), to_int(q.size(0), "batch"),
-                              to_int(q.size(1), "heads"),
-                              to_int(k.size(1), "kv heads"),
-                              to_int(q.size(2), "sequence length"),
-                              causal ? 1 : 0, static_cast<float>(scale),
-                              current_stream()),
+  check_status(fa_prefill_hd(q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                             o.data_ptr(), to_int(q.size(0), "batch"),
+                             to_int(q.size(1), "heads"),
+                             to_int(k.size(1), "kv heads"),
+                             to_int(q.size(2), "sequence length"),
+                             to_int(q.size(3), "head_dim"), causal ? 1 : 0,
+                             static_cast<float>(scale), current_stream()),
                "fa_prefill");
   return o;
 }

@@ -76,6 +76,9 @@ int ensure_device(int *device_out) {
       cudaFuncSetAttribute(decode_kernel_ptr(),
                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                            decode_smem_bytes()) != cudaSuccess ||
+      cudaFuncSetAttribute(prefill_d128_kernel_ptr(),
+                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           prefill_d128_smem_bytes()) != cudaSuccess ||
       cudaFuncSetAttribute(decode_gqa_kernel_ptr(),
                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                            decode_gqa_smem_bytes()) != cudaSuccess ||
@@ -107,14 +110,16 @@ int ensure_device(int *device_out) {
 
 // (B*H, N, 64) fp16 view of a (B, H, N, 64) tensor, 128-row x 64-column
 // boxes written with the 128-byte swizzle; rows past N read as zero.
-int make_bhn64_map(CUtensorMap *map, const void *base, int BH, int N) {
-  cuuint64_t dims[3] = {static_cast<cuuint64_t>(FA_HEAD_DIM),
+// Boxes are always 64 columns (128 bytes, the swizzle span); a 128-wide
+// head is loaded as two boxes at columns 0 and 64.
+int make_bhnd_map(CUtensorMap *map, const void *base, int BH, int N, int D,
+                  int box_rows) {
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(D),
                         static_cast<cuuint64_t>(N),
                         static_cast<cuuint64_t>(BH)};
-  cuuint64_t strides[2] = {
-      static_cast<cuuint64_t>(FA_HEAD_DIM) * 2,
-      static_cast<cuuint64_t>(N) * FA_HEAD_DIM * 2};
-  cuuint32_t box[3] = {FA_HEAD_DIM, 128, 1};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * 2,
+                           static_cast<cuuint64_t>(N) * D * 2};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(box_rows), 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
                         const_cast<void *>(base), dims, strides, box, estr,
@@ -123,6 +128,10 @@ int make_bhn64_map(CUtensorMap *map, const void *base, int BH, int N) {
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? FA_OK : FA_EINVAL;
+}
+
+int make_bhn64_map(CUtensorMap *map, const void *base, int BH, int N) {
+  return make_bhnd_map(map, base, BH, N, FA_HEAD_DIM, 128);
 }
 
 int decode_grid(int sms, int B, int H, int S_max, int split_size) {
@@ -274,6 +283,35 @@ extern "C" {
 int fa_prefill(const void *q, const void *k, const void *v, void *o, int B,
                int H, int N, int causal, float scale, void *stream) {
   return fa_prefill_gqa(q, k, v, o, B, H, H, N, causal, scale, stream);
+}
+
+int fa_prefill_hd(const void *q, const void *k, const void *v, void *o, int B,
+                  int H, int H_kv, int N, int head_dim, int causal,
+                  float scale, void *stream) {
+  if (head_dim == FA_HEAD_DIM)
+    return fa_prefill_gqa(q, k, v, o, B, H, H_kv, N, causal, scale, stream);
+  if (head_dim != 128) return FA_EINVAL;
+  if (B <= 0 || H <= 0 || N <= 0 || !isfinite(scale)) return FA_EINVAL;
+  if (H_kv <= 0 || H % H_kv != 0) return FA_EINVAL;
+  if (static_cast<long long>(B) * H >= (1ll << 31) / 128 ||
+      static_cast<long long>(N) >= (1ll << 31))
+    return FA_EINVAL;
+  if (!q || !k || !v || !o) return FA_EINVAL;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+    return FA_EALIGN;
+  int rc = ensure_device(nullptr);
+  if (rc != FA_OK) return rc;
+  CUtensorMap tq, tk, tv;
+  if (make_bhnd_map(&tq, q, B * H, N, 128, 128) != FA_OK ||
+      make_bhnd_map(&tk, k, B * H_kv, N, 128, 64) != FA_OK ||
+      make_bhnd_map(&tv, v, B * H_kv, N, 128, 64) != FA_OK)
+    return FA_EINVAL;
+  return launch_prefill_d128_kernel(tq, tk, tv, static_cast<__half *>(o), B,
+                                    H, N, causal != 0, scale, H_kv,
+                                    static_cast<cudaStream_t>(stream)) ==
+                 cudaSuccess
+             ? FA_OK
+             : FA_ECUDA;
 }
 
 int fa_prefill_gqa(const void *q, const void *k, const void *v, void *o, int B,

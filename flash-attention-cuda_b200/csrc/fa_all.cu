@@ -4,5 +4,6 @@
 #include "capi.cu"
 #include "decode_sm100.cu"
 #include "prefill_sm100.cu"
+#include "prefill_d128_sm100.cu"
 #include "legacy_sm100.cu"
 #include "noalloc.cu"

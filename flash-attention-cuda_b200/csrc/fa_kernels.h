@@ -18,6 +18,16 @@ cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
                                   int H, int N, bool causal, float scale,
                                   int H_kv, cudaStream_t stream);
 
+// ---- prefill, head_dim 128 (prefill_d128_sm100.cu) -------------------------
+const void *prefill_d128_kernel_ptr();
+int prefill_d128_smem_bytes();
+cudaError_t launch_prefill_d128_kernel(const CUtensorMap &tm_q,
+                                       const CUtensorMap &tm_k,
+                                       const CUtensorMap &tm_v, __half *out,
+                                       int B, int H, int N, bool causal,
+                                       float scale, int H_kv,
+                                       cudaStream_t stream);
+
 // ---- decode (decode_sm100.cu) ---------------------------------------------
 struct DecodeArgs {
   const __half *q;

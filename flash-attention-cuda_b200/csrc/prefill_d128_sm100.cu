@@ -1,0 +1,493 @@
+// Prefill attention forward for head_dim 128 on B200: fp16 in, fp32
+// accumulate, fp16 out. Same semantics as the head_dim-64 kernel
+// (prefill_sm100.cu; reference csrc/prefill.cu:164-343 for the math, the
+// reference itself is specialised to 64 and names 128 as its next size).
+//
+// With 128-wide rows the PV accumulator needs 128 tensor-memory columns per
+// query tile, so the key tiles are 64 wide: per query tile S (64 columns),
+// O (128) and P (32) fit twice in the 512 columns, and the two 128-row
+// query tiles of a (batch, head) ping-pong as in the 64 kernel. Per 64-key
+// step the tensor core does twice the work of the 64 kernel per
+// exponential, so this kernel leans towards the tensor-core bound.
+//
+// CTA = 12 warps (384 threads):
+//   warps 0-3 / 4-7  softmax of query tile 0 / 1 (thread = row = TMEM lane)
+//   warp 8     TMA producer: Q tiles once, then K_j, V_j per 64-key tile
+//   warp 9     MMA issuer (one elected thread); owns the TMEM allocation
+//   warps 10-11 idle (they give their registers to the softmax warps)
+//
+// Shared memory (1 KiB aligned). Every row is 256 bytes, stored as two
+// 128-byte-swizzled halves (head dims 0-63 and 64-127) in separate blocks,
+// the layout TMA writes with one 64-column box per half:
+//   Q0, Q1  2 x [128 rows x 128 B] each            64 KiB
+//   K       3 stages x 2 x [64 keys x 128 B]        48 KiB
+//   V       3 stages x 2 x [64 keys x 128 B]        48 KiB
+// Tensor memory (512 columns x 128 lanes, fp32 words):
+//   S_t [64t, 64t+64)   O_t [128+128t, 256+128t)   P_t [384+32t, 416+32t)
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include "fa_kernels.h"
+#include "fa_sm100.cuh"
+
+namespace fa {
+namespace prefill128 {
+
+constexpr int kD = 128;
+constexpr int kHalfBytes = 128;  // one swizzled half-row (64 dims)
+constexpr int kBlockM = 128;     // query rows per tile
+constexpr int kBlockN = 64;      // keys per K/V tile
+constexpr int kTilesPerCta = 2;
+constexpr int kStages = 3;
+constexpr int kSoftmaxThreads = 128;
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kThreads = 384;
+constexpr int kCtrlRegs = 24;
+constexpr int kSoftmaxRegs = 240;
+static_assert(128 * kCtrlRegs + 256 * kSoftmaxRegs <= kThreads * 168,
+              "register split exceeds the launch allocation");
+constexpr uint32_t kQHalf = kBlockM * kHalfBytes;   // 16 KiB
+constexpr uint32_t kQTile = 2 * kQHalf;             // 32 KiB
+constexpr uint32_t kKVHalf = kBlockN * kHalfBytes;  // 8 KiB
+constexpr uint32_t kKVTile = 2 * kKVHalf;           // 16 KiB
+
+constexpr uint32_t kQOff = 0;
+constexpr uint32_t kKOff = kQOff + kTilesPerCta * kQTile;
+constexpr uint32_t kVOff = kKOff + kStages * kKVTile;
+constexpr uint32_t kBarOff = kVOff + kStages * kKVTile;
+constexpr int kBarQFull = 0;
+constexpr int kBarKFull = kBarQFull + 1;          // + stage: K and V tile
+constexpr int kBarKVEmpty = kBarKFull + kStages;  // + stage
+constexpr int kBarSFull = kBarKVEmpty + kStages;  // + tile
+constexpr int kBarSFree = kBarSFull + kTilesPerCta;
+constexpr int kBarPFull = kBarSFree + kTilesPerCta;
+constexpr int kBarODone = kBarPFull + kTilesPerCta;
+constexpr int kBarDrain = kBarODone + kTilesPerCta;
+constexpr int kNumBars = kBarDrain + 1;
+constexpr uint32_t kTmemSlotOff = kBarOff + kNumBars * 8;
+constexpr uint32_t kAbortOff = kTmemSlotOff + 4;
+constexpr uint32_t kSmemBytes = kAbortOff + 4 + 8;
+
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemS = 0;    // + 64 * tile
+constexpr uint32_t kTmemO = 128;  // + 128 * tile
+constexpr uint32_t kTmemP = 384;  // + 32 * tile
+
+constexpr uint32_t kIdescS = idesc_f16_f32(kBlockM, kBlockN, false);
+constexpr uint32_t kIdescPV = idesc_f16_f32(kBlockM, kD, true);
+constexpr float kRescaleThreshold = 8.0f;
+constexpr int kMufuPairsOf4 = 2;
+
+// S = Q K^T for one 128x64 tile: 8 MMAs of K=16; steps 0-3 read the first
+// 64-dim half of Q and K, steps 4-7 the second half (a separate block).
+__device__ __forceinline__ void issue_s_tile(uint32_t d, uint64_t q_desc,
+                                             uint64_t k_desc) {
+#pragma unroll
+  for (int kk = 0; kk < kD / 16; ++kk) {
+    const uint64_t off_q = (kk >> 2) * (kQHalf >> 4) + 2 * (kk & 3);
+    const uint64_t off_k = (kk >> 2) * (kKVHalf >> 4) + 2 * (kk & 3);
+    mma_f16_ss(d, q_desc + off_q, k_desc + off_k, kIdescS, kk > 0 ? 1u : 0u);
+  }
+}
+
+// O (+)= P V for one tile: 4 MMAs of K=16 keys, N=128 head dims. V is the
+// MN-major B operand whose two 64-dim halves are kKVHalf bytes apart (the
+// descriptor's leading byte offset); each step advances 16 rows.
+__device__ __forceinline__ void issue_pv_tile(uint32_t d, uint32_t p_tmem,
+                                              uint64_t v_desc, bool accumulate) {
+#pragma unroll
+  for (int kk = 0; kk < kBlockN / 16; ++kk)
+    mma_f16_ts(d, p_tmem + 8 * kk, v_desc + 128 * kk, kIdescPV,
+               (accumulate || kk > 0) ? 1u : 0u);
+}
+
+// Shared-memory descriptor of a 128-byte-swizzled operand whose blocks of
+// 64 elements along M/N are `lbo` bytes apart.
+__device__ __forceinline__ uint64_t sw128_desc_lbo(uint32_t smem_addr,
+                                                   uint32_t lbo) {
+  return (sw128_desc(smem_addr) & ~(static_cast<uint64_t>(0x3FFFu) << 16)) |
+         (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16);
+}
+
+struct TileInfo {
+  int qt;    // query tile index along the sequence
+  int n_kv;  // 64-key tiles this query tile attends (0: tile past the end)
+};
+
+__device__ __forceinline__ TileInfo tile_info(int pair, int t, int N,
+                                              int causal) {
+  TileInfo ti;
+  ti.qt = kTilesPerCta * pair + t;
+  const int n_qt = (N + kBlockM - 1) / kBlockM;
+  if (ti.qt >= n_qt) {
+    ti.n_kv = 0;
+  } else {
+    const int keys = causal ? min((ti.qt + 1) * kBlockM, N) : N;
+    ti.n_kv = (keys + kBlockN - 1) / kBlockN;
+  }
+  return ti;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    prefill_d128_kernel(const __grid_constant__ CUtensorMap tm_q,
+                        const __grid_constant__ CUtensorMap tm_k,
+                        const __grid_constant__ CUtensorMap tm_v,
+                        __half *__restrict__ out, int N, int BH, int causal,
+                        float scale_log2, int H, int group) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (device_failed()) return;
+  if (smem_u32(smem) & 1023u) {
+    if (threadIdx.x == 0) record_error(FA_ERR_SMEM_ALIGN);
+    return;
+  }
+
+  // Heaviest causal pairs first, heads fastest.
+  const int n_qt = (N + kBlockM - 1) / kBlockM;
+  const int n_pairs = (n_qt + kTilesPerCta - 1) / kTilesPerCta;
+  const int pair = n_pairs - 1 - static_cast<int>(blockIdx.x / BH);
+  const int bh = static_cast<int>(blockIdx.x % BH);
+  const int kv_bh = (bh / H) * (H / group) + (bh % H) / group;
+  const TileInfo t0 = tile_info(pair, 0, N, causal);
+  const TileInfo t1 = tile_info(pair, 1, N, causal);
+  const int n_kv = t0.n_kv > t1.n_kv ? t0.n_kv : t1.n_kv;
+
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kBarOff);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kTmemSlotOff);
+  volatile uint32_t *abort_flag =
+      reinterpret_cast<volatile uint32_t *>(smem + kAbortOff);
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[kBarQFull], 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars[kBarKFull + s], 1);
+      mbar_init(&bars[kBarKVEmpty + s], 1);
+    }
+    for (int t = 0; t < kTilesPerCta; ++t) {
+      mbar_init(&bars[kBarSFull + t], 1);
+      mbar_init(&bars[kBarSFree + t], kSoftmaxThreads);
+      mbar_init(&bars[kBarPFull + t], kSoftmaxThreads);
+      mbar_init(&bars[kBarODone + t], 1);
+    }
+    mbar_init(&bars[kBarDrain], 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t sbase = smem_u32(smem);
+
+  if (warp >= 8) {
+    setmaxnreg_dec<kCtrlRegs>();
+    if (warp == kProducerWarp) {
+      // ---------------------------------------------------------------- TMA
+      if (lane == 0) {
+        prefetch_tensormap(&tm_q);
+        prefetch_tensormap(&tm_k);
+        prefetch_tensormap(&tm_v);
+        const bool two = t1.n_kv > 0;
+        mbar_arrive_expect_tx(&bars[kBarQFull], (two ? 2 : 1) * kQTile);
+        for (int t = 0; t < (two ? 2 : 1); ++t) {
+          const int row0 = (kTilesPerCta * pair + t) * kBlockM;
+          for (int h = 0; h < 2; ++h)
+            tma_load_3d(smem + kQOff + t * kQTile + h * kQHalf, &tm_q,
+                        &bars[kBarQFull], 64 * h, row0, bh);
+        }
+        int issued = 0;
+        for (int j = 0; j < n_kv; ++j) {
+          if (*abort_flag) break;
+          const int s = j % kStages;
+          const int use = j / kStages;
+          if (use > 0 && !mbar_wait(&bars[kBarKVEmpty + s], (use - 1) & 1)) {
+            *abort_flag = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(&bars[kBarKFull + s], 2 * kKVTile);
+          for (int h = 0; h < 2; ++h) {
+            tma_load_3d(smem + kKOff + s * kKVTile + h * kKVHalf, &tm_k,
+                        &bars[kBarKFull + s], 64 * h, j * kBlockN, kv_bh);
+            tma_load_3d(smem + kVOff + s * kKVTile + h * kKVHalf, &tm_v,
+                        &bars[kBarKFull + s], 64 * h, j * kBlockN, kv_bh);
+          }
+          issued = j + 1;
+        }
+        if (*abort_flag) {
+          mbar_wait(&bars[kBarQFull], 0);
+          for (int j = (issued > kStages ? issued - kStages : 0); j < issued;
+               ++j)
+            mbar_wait(&bars[kBarKFull + j % kStages], (j / kStages) & 1);
+        }
+      }
+    } else if (warp == kMmaWarp) {
+      // ---------------------------------------------------------------- MMA
+      const bool leader = elect_one();
+      const uint32_t tmem = __shfl_sync(0xffffffffu, tmem_base, 0);
+      const int n_t[2] = {t0.n_kv, t1.n_kv};
+      const uint64_t desc0 = sw128_desc(sbase);
+      const uint64_t vdesc0 = sw128_desc_lbo(sbase, kKVHalf);
+      bool ok = mbar_wait(&bars[kBarQFull], 0) &&
+                mbar_wait(&bars[kBarKFull + 0], 0);
+      if (ok) {
+        tc_fence_after();
+        if (leader) {
+          for (int t = 0; t < kTilesPerCta; ++t) {
+            if (n_t[t] == 0) continue;
+            issue_s_tile(tmem + kTmemS + 64 * t,
+                         desc0 + ((kQOff + t * kQTile) >> 4),
+                         desc0 + (kKOff >> 4));
+            mma_commit(&bars[kBarSFull + t]);
+          }
+        }
+        __syncwarp();
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        if (*abort_flag) {
+          ok = false;
+          break;
+        }
+        const int s = j % kStages;
+        const int s1 = (j + 1) % kStages;
+#pragma unroll
+        for (int t = 0; t < kTilesPerCta; ++t) {
+          const int nt = n_t[t];
+          if (!ok || j >= nt) continue;
+          if (j + 1 < nt) {
+            const bool need_kv = (t == 0) || (n_t[0] <= j + 1);
+            if ((need_kv &&
+                 !mbar_wait(&bars[kBarKFull + s1], ((j + 1) / kStages) & 1)) ||
+                !mbar_wait(&bars[kBarSFree + t], j & 1)) {
+              ok = false;
+              continue;
+            }
+            tc_fence_after();
+            if (leader) {
+              issue_s_tile(tmem + kTmemS + 64 * t,
+                           desc0 + ((kQOff + t * kQTile) >> 4),
+                           desc0 + ((kKOff + s1 * kKVTile) >> 4));
+              mma_commit(&bars[kBarSFull + t]);
+            }
+            __syncwarp();
+          }
+          if (!mbar_wait(&bars[kBarPFull + t], j & 1)) {
+            ok = false;
+            continue;
+          }
+          tc_fence_after();
+          if (leader) {
+            issue_pv_tile(tmem + kTmemO + 128 * t, tmem + kTmemP + 32 * t,
+                          vdesc0 + ((kVOff + s * kKVTile) >> 4), j > 0);
+            mma_commit(&bars[kBarODone + t]);
+          }
+          __syncwarp();
+        }
+        if (!ok) break;
+        if (leader) mma_commit(&bars[kBarKVEmpty + s]);
+        __syncwarp();
+      }
+      if (!ok && leader) *abort_flag = 1;
+      if (leader) mma_commit(&bars[kBarDrain]);
+      __syncwarp();
+      mbar_wait(&bars[kBarDrain], 0);
+    }
+  } else {
+    setmaxnreg_inc<kSoftmaxRegs>();
+    // -------------------------------------------------------------- softmax
+    const int t = warp >> 2;
+    const int row = threadIdx.x & 127;
+    const TileInfo ti = t == 0 ? t0 : t1;
+    const uint32_t lane_addr = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem_base + lane_addr + kTmemS + 64 * t;
+    const uint32_t tO = tmem_base + lane_addr + kTmemO + 128 * t;
+    const uint32_t tP = tmem_base + lane_addr + kTmemP + 32 * t;
+    uint64_t *s_full = &bars[kBarSFull + t];
+    uint64_t *s_free = &bars[kBarSFree + t];
+    uint64_t *p_full = &bars[kBarPFull + t];
+    uint64_t *o_done = &bars[kBarODone + t];
+    const int q_row = ti.qt * kBlockM + row;
+    float m_use = -INFINITY;
+    float l_sum = 0.f;
+    bool ok = true;
+
+    for (int j = 0; j < ti.n_kv; ++j) {
+      if (*abort_flag || !mbar_wait(s_full, j & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sr[2][32];
+      tmem_ld32(tS + 0, sr[0]);
+      tmem_ld32(tS + 32, sr[1]);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(s_free);
+
+      float s[kBlockN];
+#pragma unroll
+      for (int c = 0; c < kBlockN; ++c) s[c] = __uint_as_float(sr[c >> 5][c & 31]);
+      float sl = scale_log2;
+      if (scale_log2 <= 0.f) {
+#pragma unroll
+        for (int c = 0; c < kBlockN; ++c) s[c] *= scale_log2;
+        sl = 1.f;
+      }
+      const int kbase = j * kBlockN;
+      const bool diag = causal && (kbase + kBlockN > ti.qt * kBlockM);
+      if (diag || kbase + kBlockN > N) {
+        int lim = N - kbase;
+        if (diag) lim = min(lim, q_row + 1 - kbase);
+#pragma unroll
+        for (int c = 0; c < kBlockN; ++c) s[c] = (c < lim) ? s[c] : -INFINITY;
+      }
+      float mxp[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mxp[i] = s[i];
+#pragma unroll
+      for (int c = 8; c + 16 <= kBlockN; c += 16) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          mxp[i] = fmax3(mxp[i], s[c + i], s[c + 8 + i]);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mxp[i] = fmaxf(mxp[i], s[kBlockN - 8 + i]);
+      const float mx = fmax3(fmax3(mxp[0], mxp[1], mxp[2]),
+                             fmax3(mxp[3], mxp[4], mxp[5]),
+                             fmaxf(mxp[6], mxp[7]));
+      const float m_tile = mx * sl;
+      float corr = 1.f;
+      const bool rescale = m_tile > m_use + kRescaleThreshold;
+      if (rescale) {
+        corr = fast_exp2(m_use - m_tile);
+        m_use = m_tile;
+      }
+      l_sum *= corr;
+      const float neg_m = -m_use;
+      const float2 sl2 = make_float2(sl, sl);
+      const float2 nm2 = make_float2(neg_m, neg_m);
+      float2 rs[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) rs[i] = make_float2(0.f, 0.f);
+      uint32_t pk[32];
+#pragma unroll
+      for (int c = 0; c < kBlockN; c += 2) {
+        const float2 x = ffma2(make_float2(s[c], s[c + 1]), sl2, nm2);
+        float2 p;
+        if (((c >> 1) & 3) >= kMufuPairsOf4) {
+          p = exp2_poly2(x);
+        } else {
+          p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+        }
+        rs[(c >> 1) & 3] = fadd2(rs[(c >> 1) & 3], p);
+        pk[c >> 1] = pack_half2(p.x, p.y);
+      }
+      const float2 rsum = fadd2(fadd2(rs[0], rs[1]), fadd2(rs[2], rs[3]));
+      l_sum += rsum.x + rsum.y;
+
+      if (j > 0) {
+        if (!mbar_wait(o_done, (j - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+          for (int h = 0; h < kD / 32; ++h) {
+            uint32_t o[32];
+            tmem_ld32(tO + 32 * h, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 32; ++c)
+              o[c] = __float_as_uint(__uint_as_float(o[c]) * corr);
+            tmem_st32(tO + 32 * h, o);
+          }
+        }
+      }
+      tmem_st32(tP, pk);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+
+    if (ti.n_kv > 0) {
+      if (ok && mbar_wait(o_done, (ti.n_kv - 1) & 1)) {
+        tc_fence_after();
+        const float inv_l = (l_sum > 0.f) ? 1.f / l_sum : 0.f;
+        uint4 *dst = reinterpret_cast<uint4 *>(
+            out + (static_cast<size_t>(bh) * N + q_row) * kD);
+#pragma unroll
+        for (int h = 0; h < kD / 32; ++h) {
+          uint32_t o[32];
+          tmem_ld32(tO + 32 * h, o);
+          tmem_wait_ld();
+          if (q_row < N) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const uint32_t *src = &o[c * 8];
+              uint4 v;
+              v.x = pack_half2(__uint_as_float(src[0]) * inv_l,
+                               __uint_as_float(src[1]) * inv_l);
+              v.y = pack_half2(__uint_as_float(src[2]) * inv_l,
+                               __uint_as_float(src[3]) * inv_l);
+              v.z = pack_half2(__uint_as_float(src[4]) * inv_l,
+                               __uint_as_float(src[5]) * inv_l);
+              v.w = pack_half2(__uint_as_float(src[6]) * inv_l,
+                               __uint_as_float(src[7]) * inv_l);
+              dst[4 * h + c] = v;
+            }
+          }
+        }
+      } else {
+        *abort_flag = 1;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace prefill128
+
+const void *prefill_d128_kernel_ptr() {
+  return reinterpret_cast<const void *>(prefill128::prefill_d128_kernel);
+}
+int prefill_d128_smem_bytes() {
+  return static_cast<int>(prefill128::kSmemBytes);
+}
+
+cudaError_t launch_prefill_d128_kernel(const CUtensorMap &tm_q,
+                                       const CUtensorMap &tm_k,
+                                       const CUtensorMap &tm_v, __half *out,
+                                       int B, int H, int N, bool causal,
+                                       float scale, int H_kv,
+                                       cudaStream_t stream) {
+  const int BH = B * H;
+  const int n_qt = (N + prefill128::kBlockM - 1) / prefill128::kBlockM;
+  const int n_pairs =
+      (n_qt + prefill128::kTilesPerCta - 1) / prefill128::kTilesPerCta;
+  const unsigned grid =
+      static_cast<unsigned>(n_pairs) * static_cast<unsigned>(BH);
+  const float scale_log2 = scale * 1.4426950408889634f;
+  prefill128::prefill_d128_kernel<<<grid, prefill128::kThreads,
+                                    prefill128::kSmemBytes, stream>>>(
+      tm_q, tm_k, tm_v, out, N, BH, causal ? 1 : 0, scale_log2, H, H / H_kv);
+  return cudaGetLastError();
+}
+
+}  // namespace fa

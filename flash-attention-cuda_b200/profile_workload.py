@@ -27,6 +27,8 @@ CASES = {
     "prefill_c2_causal": ("prefill", (8, 12, 1024), True, None),
     "prefill_c2_full": ("prefill", (8, 12, 1024), False, None),
     "prefill_small": ("prefill", (1, 8, 2048), True, None),
+    # config 3's shape at head_dim 128
+    "prefill_d128_c3": ("prefill_d128", (4, 14, 4096), True, None),
     "decode_c4": ("decode", (64, 12, 8192), None, None),
     "decode_c5": ("decode", (1, 14, 131072), None, None),
     # Qwen2.5-0.5B's real 2 K/V heads, and a wider grouped batch
@@ -44,10 +46,11 @@ def main():
     kind, (b, h, n), causal, h_kv = CASES[args.case]
     h_kv = h_kv or h
     g = torch.Generator(device="cuda").manual_seed(0)
-    if kind == "prefill":
-        q, k, v = (torch.randn(b, h, n, 64, generator=g, device="cuda",
+    if kind in ("prefill", "prefill_d128"):
+        d = 128 if kind == "prefill_d128" else 64
+        q, k, v = (torch.randn(b, h, n, d, generator=g, device="cuda",
                                dtype=torch.float16) for _ in range(3))
-        fn = lambda: fa.prefill(q, k, v, causal, SCALE)
+        fn = lambda: fa.prefill(q, k, v, causal, d ** -0.5)
     else:
         q = torch.randn(b, h, 1, 64, generator=g, device="cuda", dtype=torch.float16)
         k, v = (torch.randn(b, h_kv, n, 64, generator=g, device="cuda",

@@ -62,6 +62,17 @@ int fa_prefill_gqa(const void *q, const void *k, const void *v, void *o, int B,
                    void *stream);
 
 /*
+ * Prefill for head_dim 64 or 128: q, o (B, H, N, head_dim); k, v
+ * (B, H_kv, N, head_dim) with H % H_kv == 0. head_dim 64 is fa_prefill_gqa;
+ * head_dim 128 runs a kernel of its own (64-key tiles, 128-column O in
+ * tensor memory). The reference is specialised to 64 and names 128 as its
+ * next size (README "Engineering decisions"); no reference counterpart.
+ */
+int fa_prefill_hd(const void *q, const void *k, const void *v, void *o, int B,
+                  int H, int H_kv, int N, int head_dim, int causal,
+                  float scale, void *stream);
+
+/*
  * Bytes of scratch memory fa_decode / fa_decode_partial need for this shape
  * and split choice (the log-sum-exp partials of segments split across CTAs).
  * It needs no initialisation. split_size <= 0 selects the automatic,

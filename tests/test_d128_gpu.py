@@ -1,0 +1,75 @@
+"""Prefill at head_dim 128 (the reference's named next size): against fp32
+attention at the north star's 2e-3 tolerance, causal and full, ragged
+lengths, grouped K/V heads, unusual scales."""
+
+import math
+
+import pytest
+import torch
+
+from conftest import requires_gpu
+
+import flashattn_cuda
+
+pytestmark = [pytest.mark.gpu, requires_gpu]
+
+
+def reference(q, k, v, causal, scale):
+    group = q.shape[1] // k.shape[1]
+    kf = k.float().repeat_interleave(group, dim=1)
+    vf = v.float().repeat_interleave(group, dim=1)
+    return torch.nn.functional.scaled_dot_product_attention(
+        q.float(), kf, vf, is_causal=causal, scale=scale)
+
+
+@pytest.mark.parametrize("b,h,n", [(2, 3, 1000), (1, 4, 4096), (2, 2, 513),
+                                   (1, 1, 1), (3, 2, 129), (1, 2, 64),
+                                   (1, 1, 65), (2, 5, 256)])
+@pytest.mark.parametrize("causal", [True, False])
+def test_prefill_d128_matches_fp32(b, h, n, causal):
+    torch.manual_seed(b * 1000 + h * 10 + n)
+    q, k, v = (torch.randn(b, h, n, 128, device="cuda").half() for _ in range(3))
+    scale = 1.0 / math.sqrt(128)
+    got = flashattn_cuda.prefill(q, k, v, causal, scale)
+    assert got.shape == q.shape and got.dtype == torch.float16
+    want = reference(q, k, v, causal, scale)
+    assert (got.float() - want).abs().max().item() <= 2e-3
+    assert flashattn_cuda.take_device_error() == 0
+
+
+def test_prefill_d128_grouped_heads():
+    torch.manual_seed(11)
+    q = torch.randn(2, 8, 777, 128, device="cuda").half()
+    k, v = (torch.randn(2, 2, 777, 128, device="cuda").half() for _ in range(2))
+    got = flashattn_cuda.prefill(q, k, v, True, 0.0883883)
+    want = reference(q, k, v, True, 0.0883883)
+    assert (got.float() - want).abs().max().item() <= 2e-3
+
+
+@pytest.mark.parametrize("scale,tol", [(0.0, 2e-3), (-0.09, 2e-3), (0.5, 4e-3)])
+def test_prefill_d128_scales(scale, tol):
+    """The 2e-3 bound is stated for scale = 1/sqrt(d); at 0.5 the logits are
+    5.7x wider, the softmax is peakier and the fp16 rounding of P and of the
+    output weighs more, so that case gets twice the bound."""
+    torch.manual_seed(12)
+    q, k, v = (torch.randn(1, 3, 300, 128, device="cuda").half() for _ in range(3))
+    for causal in (True, False):
+        got = flashattn_cuda.prefill(q, k, v, causal, scale)
+        want = reference(q, k, v, causal, scale)
+        assert (got.float() - want).abs().max().item() <= tol, (scale, causal)
+
+
+def test_prefill_d128_single_key_rows_are_exact():
+    """Causal row 0 attends one key: its output is that value row."""
+    torch.manual_seed(13)
+    q, k, v = (torch.randn(2, 2, 200, 128, device="cuda").half() for _ in range(3))
+    got = flashattn_cuda.prefill(q, k, v, True, 0.088)
+    assert torch.equal(got[:, :, 0], v[:, :, 0])
+
+
+def test_decode_still_requires_head_dim_64():
+    q = torch.randn(1, 2, 1, 128, device="cuda").half()
+    k = torch.randn(1, 2, 16, 128, device="cuda").half()
+    with pytest.raises(RuntimeError, match="head_dim"):
+        flashattn_cuda.decode(q, k, k, torch.tensor([4], dtype=torch.int32,
+                                                    device="cuda"), 0.1)
