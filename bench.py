@@ -337,6 +337,20 @@ def run_ours(args, rank, world, local_rank):
                     "two index_put copies + decode"}
         del qd, kc, vc, kn, vn
 
+        # config 4 at head_dim 128 (rank-local batch shard, same lengths)
+        qd = randn(bm, C4["H"], 1, 128, seed=45 + rank)
+        kc = randn(bm, C4["H"], C4["cap"], 128, seed=46 + rank)
+        vc = randn(bm, C4["H"], C4["cap"], 128, seed=47 + rank)
+        t = timer.run(lambda: fa.decode(qd, kc, vc, lens, SCALE), args.steps,
+                      args.warmup) / args.steps
+        launches += args.steps
+        b128 = bytes_rank * 2
+        secondary["c4_decode_d128"] = {
+            "ms": round(t, 5), "gbs_per_gpu_rank0": round(b128 / (t * 1e-3) / 1e9, 1),
+            "frac_of_measured_hbm": round(b128 / (t * 1e-3) / 1e9 / hbm, 4),
+            "note": "config 4 at head_dim 128 (the reference's named next size)"}
+        del qd, kc, vc
+
         # ---------------- secondary: C5 long decode, sequence-sharded ----
         S = C5["S"]
         c0, c1 = shard_range(S, world, rank)

@@ -43,8 +43,8 @@ void check_bhnd(const at::Tensor &t, const char *name) {
               kHeadDim, ", got ", t.size(3));
 }
 
-// Prefill also takes head_dim 128 (a kernel of its own).
-void check_bhnd_prefill(const at::Tensor &t, const char *name) {
+// Prefill and per-head decode also take head_dim 128 (kernels of their own).
+void check_bhnd_any(const at::Tensor &t, const char *name) {
   check_cuda(t, name);
   check_half(t, name);
   check_contiguous(t, name);
@@ -103,9 +103,12 @@ DecodeScratch &decode_scratch(const at::Tensor &like, size_t partial_bytes,
 void check_decode_inputs(const at::Tensor &q, const at::Tensor &k_cache,
                          const at::Tensor &v_cache, const at::Tensor &seq_lens,
                          double scale) {
-  check_bhnd(q, "q");
-  check_bhnd(k_cache, "k_cache");
-  check_bhnd(v_cache, "v_cache");
+  check_bhnd_any(q, "q");
+  check_bhnd_any(k_cache, "k_cache");
+  check_bhnd_any(v_cache, "v_cache");
+  TORCH_CHECK(q.size(3) == k_cache.size(3),
+              "q and the caches must have the same head_dim, got ", q.size(3),
+              " and ", k_cache.size(3));
   TORCH_CHECK(q.size(2) == 1, "decode expects exactly one query row, got ",
               q.size(2));
   TORCH_CHECK(k_cache.sizes() == v_cache.sizes(),
@@ -135,9 +138,9 @@ void check_decode_inputs(const at::Tensor &q, const at::Tensor &k_cache,
 // prefill(q, k, v, causal, scale): reference csrc/bindings.cpp:10-27.
 at::Tensor prefill(const at::Tensor &q, const at::Tensor &k,
                    const at::Tensor &v, bool causal, double scale) {
-  check_bhnd_prefill(q, "q");
-  check_bhnd_prefill(k, "k");
-  check_bhnd_prefill(v, "v");
+  check_bhnd_any(q, "q");
+  check_bhnd_any(k, "k");
+  check_bhnd_any(v, "v");
   // Identical shapes as in the reference; additionally k and v may have
   // fewer heads than q when they divide it (grouped-query attention).
   const bool same = q.sizes() == k.sizes() && q.sizes() == v.sizes();
@@ -182,19 +185,22 @@ at::Tensor decode_impl(const at::Tensor &q, const at::Tensor &k_cache,
   const int split = split_size > 0 ? to_int(split_size, "split_size") : 0;
   at::Tensor o = at::empty_like(q);
   const int H_kv = to_int(k_cache.size(1), "kv heads");
+  const int D = to_int(q.size(3), "head_dim");
+  TORCH_CHECK(D == kHeadDim || H_kv == H,
+              "grouped K/V heads need head_dim == ", kHeadDim);
   const size_t bytes =
-      H_kv == H ? fa_decode_workspace_bytes(B, H, S, split, q.get_device())
-                : fa_decode_gqa_workspace_bytes(B, H, H_kv, S, q.get_device());
+      H_kv != H ? fa_decode_gqa_workspace_bytes(B, H, H_kv, S, q.get_device())
+                : fa_decode_hd_workspace_bytes(B, H, S, D, split, q.get_device());
   TORCH_CHECK(bytes > 0, "fa_decode_workspace_bytes failed");
   DecodeScratch &ws = decode_scratch(q, bytes, static_cast<size_t>(B) * H);
   uint32_t *ctr = reinterpret_cast<uint32_t *>(ws.counters.data_ptr<int32_t>());
   if (H_kv == H) {
     check_status(
-        fa_decode(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
-                  seq_lens.data_ptr<int32_t>(), o.data_ptr(), B, H, S,
-                  static_cast<float>(scale), split, ws.partials.data_ptr(),
-                  static_cast<size_t>(ws.partials.numel()), ctr,
-                  static_cast<size_t>(ws.counters.numel()), current_stream()),
+        fa_decode_hd(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                     seq_lens.data_ptr<int32_t>(), o.data_ptr(), B, H, S, D,
+                     static_cast<float>(scale), split, ws.partials.data_ptr(),
+                     static_cast<size_t>(ws.partials.numel()), ctr,
+                     static_cast<size_t>(ws.counters.numel()), current_stream()),
         "fa_decode");
   } else {
     TORCH_CHECK(split == 0, "a forced split size needs one K/V head per query head");
@@ -221,6 +227,8 @@ at::Tensor decode_partial(const at::Tensor &q, const at::Tensor &k_cache,
                           const at::Tensor &v_cache,
                           const at::Tensor &seq_lens, double scale) {
   check_decode_inputs(q, k_cache, v_cache, seq_lens, scale);
+  TORCH_CHECK(q.size(3) == kHeadDim, "decode_partial needs head_dim == ",
+              kHeadDim);
   TORCH_CHECK(k_cache.size(1) == q.size(1),
               "decode_partial needs one K/V head per query head");
   const c10::cuda::CUDAGuard guard(q.device());
@@ -252,6 +260,8 @@ at::Tensor decode_append(const at::Tensor &q, const at::Tensor &k_new,
                          at::Tensor v_cache, const at::Tensor &seq_lens,
                          double scale) {
   check_decode_inputs(q, k_cache, v_cache, seq_lens, scale);
+  TORCH_CHECK(q.size(3) == kHeadDim, "decode_append needs head_dim == ",
+              kHeadDim);
   check_bhnd(k_new, "k_new");
   check_bhnd(v_new, "v_new");
   TORCH_CHECK(k_new.sizes() == v_new.sizes() && k_new.size(0) == k_cache.size(0) &&

@@ -76,6 +76,12 @@ int ensure_device(int *device_out) {
       cudaFuncSetAttribute(decode_kernel_ptr(),
                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                            decode_smem_bytes()) != cudaSuccess ||
+      cudaFuncSetAttribute(decode_d128_kernel_ptr(),
+                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           decode_d128_smem_bytes()) != cudaSuccess ||
+      cudaFuncSetAttribute(decode_d128_kernel_ptr(),
+                           cudaFuncAttributePreferredSharedMemoryCarveout,
+                           cudaSharedmemCarveoutMaxShared) != cudaSuccess ||
       cudaFuncSetAttribute(prefill_d128_kernel_ptr(),
                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                            prefill_d128_smem_bytes()) != cudaSuccess ||
@@ -347,6 +353,73 @@ size_t fa_decode_workspace_bytes(int B, int H, int S_max, int split_size,
       cudaSuccess)
     return 0;
   return workspace_bytes_for(B, H, decode_grid(sms, B, H, S_max, split_size));
+}
+
+size_t fa_decode_hd_workspace_bytes(int B, int H, int S_max, int head_dim,
+                                    int split_size, int device) {
+  if (head_dim == FA_HEAD_DIM)
+    return fa_decode_workspace_bytes(B, H, S_max, split_size, device);
+  if (head_dim != 128 || B <= 0 || H <= 0 || S_max <= 0) return 0;
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) !=
+      cudaSuccess)
+    return 0;
+  const int grid = decode_grid(sms, B, H, S_max, split_size);
+  return (static_cast<size_t>(B) * H + grid) * decode_d128_partial_floats() *
+         sizeof(float);
+}
+
+int fa_decode_hd(const void *q, const void *k_cache, const void *v_cache,
+                 const int32_t *seq_lens, void *o, int B, int H, int S_max,
+                 int head_dim, float scale, int split_size, void *workspace,
+                 size_t workspace_bytes, uint32_t *counters,
+                 size_t counter_count, void *stream) {
+  if (head_dim == FA_HEAD_DIM)
+    return fa_decode(q, k_cache, v_cache, seq_lens, o, B, H, S_max, scale,
+                     split_size, workspace, workspace_bytes, counters,
+                     counter_count, stream);
+  if (head_dim != 128) return FA_EINVAL;
+  if (!decode_shape_ok(B, H, S_max, scale)) return FA_EINVAL;
+  if (split_size > 0 && split_size % 4 != 0) return FA_EINVAL;
+  if (!q || !k_cache || !v_cache || !seq_lens || !o || !workspace || !counters)
+    return FA_EINVAL;
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) ||
+      !aligned16(o) || !aligned16(workspace) ||
+      (reinterpret_cast<uintptr_t>(seq_lens) & 3u) ||
+      (reinterpret_cast<uintptr_t>(counters) & 3u))
+    return FA_EALIGN;
+  int dev = 0;
+  int rc = ensure_device(&dev);
+  if (rc != FA_OK) return rc;
+  const int grid = decode_grid(g_devices[dev].sms, B, H, S_max, split_size);
+  if (workspace_bytes < (static_cast<size_t>(B) * H + grid) *
+                            decode_d128_partial_floats() * sizeof(float) ||
+      counter_count < static_cast<size_t>(B) * H)
+    return FA_ENOSPACE;
+  DecodeArgs a;
+  a.k_new = nullptr;
+  a.v_new = nullptr;
+  a.k_cache_w = nullptr;
+  a.v_cache_w = nullptr;
+  a.q = static_cast<const __half *>(q);
+  a.k = static_cast<const __half *>(k_cache);
+  a.v = static_cast<const __half *>(v_cache);
+  a.seq_lens = seq_lens;
+  a.out = static_cast<__half *>(o);
+  a.partial_out = nullptr;
+  a.ws_counters = counters;
+  a.ws_partials = static_cast<float *>(workspace);
+  a.B = B;
+  a.H = H;
+  a.S_max = S_max;
+  a.H_kv = H;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.rows_per_cta = split_size > 0 ? split_size : 0;
+  a.grid = grid;
+  return launch_decode_d128_kernel(a, static_cast<cudaStream_t>(stream)) ==
+                 cudaSuccess
+             ? FA_OK
+             : FA_ECUDA;
 }
 
 size_t fa_decode_gqa_workspace_bytes(int B, int H, int H_kv, int S_max,

@@ -269,7 +269,9 @@ __device__ void merger(const DecodeArgs &a, uint8_t *red_base,
 // reads cache plane b * H_kv + s / seg_per_plane. kTiled: 128-row TMA boxes
 // with the 128-byte swizzle (for ldmatrix consumers); otherwise contiguous
 // bulk copies of exactly the rows of the stage.
-template <bool kTiled, int kNumStages>
+// kD: head dim of the cache rows; kRowsPerStage x 2 kD bytes = one stage.
+template <bool kTiled, int kNumStages, int kD = kHeadDim,
+          int kRowsPerStage = kStageRows>
 __device__ void produce(const DecodeArgs &a, int nseg, int seg_per_plane,
                         uint8_t *smem, uint32_t k_off, uint32_t v_off,
                         uint64_t *full, uint64_t *empty, StageHeader *hdr,
@@ -282,7 +284,7 @@ __device__ void produce(const DecodeArgs &a, int nseg, int seg_per_plane,
       sum_len += len;
       if (len == 0 && (b % static_cast<int>(gridDim.x)) ==
                           static_cast<int>(blockIdx.x)) {
-        write_empty_sequence(a, b);
+        if (kD == kHeadDim) write_empty_sequence(a, b);  // other widths: caller
       }
     }
     const long long total = warp_sum_ll(sum_len) * nseg;
@@ -350,9 +352,9 @@ __device__ void produce(const DecodeArgs &a, int nseg, int seg_per_plane,
         // cache plane (K/V head) of this segment
         const int g_kv = b * a.H_kv + h / seg_per_plane;
         const size_t row0 = static_cast<size_t>(g_kv) * a.S_max + r;
-        for (long long r0 = cur; r0 < piece_end; r0 += kStageRows) {
+        for (long long r0 = cur; r0 < piece_end; r0 += kRowsPerStage) {
           const int n = static_cast<int>(
-              piece_end - r0 < kStageRows ? piece_end - r0 : kStageRows);
+              piece_end - r0 < kRowsPerStage ? piece_end - r0 : kRowsPerStage);
           const int slot = it % kNumStages;
           const int use = it / kNumStages;
           if (use > 0 && !mbar_wait(&empty[slot], (use - 1) & 1)) {
@@ -376,9 +378,8 @@ __device__ void produce(const DecodeArgs &a, int nseg, int seg_per_plane,
             tma_load_3d(smem + v_off + slot * kStageBytes, tm_v, &full[slot], 0,
                         row_in_plane, g_kv);
           } else {
-            const size_t elem =
-                (row0 + static_cast<size_t>(r0 - cur)) * kHeadDim;
-            const uint32_t bytes = static_cast<uint32_t>(n) * kRowBytes;
+            const size_t elem = (row0 + static_cast<size_t>(r0 - cur)) * kD;
+            const uint32_t bytes = static_cast<uint32_t>(n) * 2 * kD;
             mbar_arrive_expect_tx(&full[slot], 2 * bytes);
             bulk_load(smem + k_off + slot * kStageBytes, a.k + elem, bytes,
                       &full[slot], policy);

@@ -3,6 +3,7 @@
 // defined in the same unit that uses it.
 #include "capi.cu"
 #include "decode_sm100.cu"
+#include "decode_d128_sm100.cu"
 #include "prefill_sm100.cu"
 #include "prefill_d128_sm100.cu"
 #include "legacy_sm100.cu"

@@ -72,6 +72,14 @@ cudaError_t launch_decode_gqa_kernel(const DecodeArgs &args,
                                      const CUtensorMap &tm_v,
                                      cudaStream_t stream);
 
+// head_dim 128 per-head decode (decode_d128_sm100.cu); partials are
+// decode_d128_partial_floats() = 132 floats, grid as decode_kernel's.
+const void *decode_d128_kernel_ptr();
+int decode_d128_smem_bytes();
+int decode_d128_partial_floats();
+cudaError_t launch_decode_d128_kernel(const DecodeArgs &args,
+                                      cudaStream_t stream);
+
 const void *merge_kernel_ptr();
 int merge_threads();
 cudaError_t launch_merge_kernel(const float *partials, int G, __half *out,

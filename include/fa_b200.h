@@ -114,6 +114,21 @@ size_t fa_decode_gqa_workspace_bytes(int B, int H, int H_kv, int S_max,
                                      int device);
 
 /*
+ * Decode for head_dim 64 (same as fa_decode) or 128: q, o (B, H, 1,
+ * head_dim), caches (B, H, S_max, head_dim), same schedule, rules and
+ * counters as fa_decode; workspace of fa_decode_hd_workspace_bytes() bytes.
+ * The reference is specialised to 64 and names 128 as its next size; no
+ * reference counterpart.
+ */
+size_t fa_decode_hd_workspace_bytes(int B, int H, int S_max, int head_dim,
+                                    int split_size, int device);
+int fa_decode_hd(const void *q, const void *k_cache, const void *v_cache,
+                 const int32_t *seq_lens, void *o, int B, int H, int S_max,
+                 int head_dim, float scale, int split_size, void *workspace,
+                 size_t workspace_bytes, uint32_t *counters,
+                 size_t counter_count, void *stream);
+
+/*
  * Decode with the KV-cache append fused in: for every sequence b the new
  * token's k_new / v_new rows (B, H_kv, 1, 64) fp16 are stored at row
  * p = max(seq_lens[b], 0) of k_cache / v_cache (B, H_kv, S_max, 64) and the

@@ -67,9 +67,70 @@ def test_prefill_d128_single_key_rows_are_exact():
     assert torch.equal(got[:, :, 0], v[:, :, 0])
 
 
-def test_decode_still_requires_head_dim_64():
-    q = torch.randn(1, 2, 1, 128, device="cuda").half()
+def decode_reference(q, k, v, lens, scale):
+    b, h = q.shape[:2]
+    out = torch.zeros(q.shape, dtype=torch.float32, device=q.device)
+    for i in range(b):
+        n = max(0, min(int(lens[i]), k.shape[2]))
+        if n == 0:
+            continue
+        s = (q[i].float() @ k[i, :, :n].float().transpose(1, 2)) * scale
+        out[i] = torch.softmax(s, dim=-1) @ v[i, :, :n].float()
+    return out
+
+
+@pytest.mark.parametrize("b,h,s,lens", [
+    (5, 8, 3000, [3000, 1, 0, 1777, 64]),
+    (1, 14, 65536, [65533]),
+    (64, 4, 700, None),
+])
+def test_decode_d128_matches_fp32(b, h, s, lens):
+    torch.manual_seed(b + h)
+    q = torch.randn(b, h, 1, 128, device="cuda").half()
+    k, v = (torch.randn(b, h, s, 128, device="cuda").half() for _ in range(2))
+    if lens is None:
+        g = torch.Generator().manual_seed(2)
+        lens = torch.randint(0, s + 20, (b,), generator=g, dtype=torch.int32)
+    lens = torch.as_tensor(lens, dtype=torch.int32).cuda()
+    scale = 128 ** -0.5
+    for _ in range(2):  # counters are clean for the next call
+        got = flashattn_cuda.decode(q, k, v, lens, scale)
+        want = decode_reference(q, k, v, lens, scale)
+        assert (got.float() - want).abs().max().item() <= 2e-3
+    empty = (lens <= 0).nonzero().flatten()
+    assert torch.all(got[empty] == 0)
+    assert flashattn_cuda.take_device_error() == 0
+
+
+def test_decode_d128_equals_prefill_row():
+    """decode of token t == causal prefill row t, at head_dim 128."""
+    torch.manual_seed(21)
+    b, h, n = 2, 3, 900
+    q, k, v = (torch.randn(b, h, n, 128, device="cuda").half() for _ in range(3))
+    scale = 128 ** -0.5
+    pre = flashattn_cuda.prefill(q, k, v, True, scale)
+    for t in (0, 1, 127, 128, 899):
+        lens = torch.full((b,), t + 1, dtype=torch.int32, device="cuda")
+        dec = flashattn_cuda.decode(q[:, :, t:t + 1].contiguous(), k, v, lens, scale)
+        assert (dec.float() - pre[:, :, t:t + 1].float()).abs().max().item() <= 2e-3
+
+
+@pytest.mark.parametrize("split", [128, 256, 1024])
+def test_decode_d128_split_invariance(split):
+    torch.manual_seed(22)
+    q = torch.randn(2, 4, 1, 128, device="cuda").half()
+    k, v = (torch.randn(2, 4, 5000, 128, device="cuda").half() for _ in range(2))
+    lens = torch.tensor([5000, 2501], dtype=torch.int32, device="cuda")
+    auto = flashattn_cuda.decode(q, k, v, lens, 0.088)
+    forced = flashattn_cuda._decode_with_split(q, k, v, lens, 0.088, split)
+    assert (auto.float() - forced.float()).abs().max().item() <= 1e-3
+
+
+def test_decode_d128_limits():
+    q = torch.randn(1, 4, 1, 128, device="cuda").half()
     k = torch.randn(1, 2, 16, 128, device="cuda").half()
+    lens = torch.tensor([4], dtype=torch.int32, device="cuda")
     with pytest.raises(RuntimeError, match="head_dim"):
-        flashattn_cuda.decode(q, k, k, torch.tensor([4], dtype=torch.int32,
-                                                    device="cuda"), 0.1)
+        flashattn_cuda.decode(q, k, k, lens, 0.1)
+    with pytest.raises(RuntimeError, match="head_dim"):
+        flashattn_cuda.decode(q[..., :64].contiguous(), k, k, lens, 0.1)
