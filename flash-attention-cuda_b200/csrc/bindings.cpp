@@ -292,6 +292,81 @@ at::Tensor decode_append(const at::Tensor &q, const at::Tensor &k_new,
   return o;
 }
 
+// ---- sequence-sharded decode with the cross-GPU combine in the kernel ----
+size_t exchange_bytes(int64_t B, int64_t H, int64_t world) {
+  const size_t n = fa_exchange_bytes(to_int(B, "batch"), to_int(H, "heads"),
+                                     to_int(world, "world"));
+  TORCH_CHECK(n > 0, "invalid exchange shape");
+  return n;
+}
+
+py::tuple exchange_alloc(size_t bytes, int64_t device) {
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  void *p = nullptr;
+  char handle[64];
+  check_status(fa_exchange_alloc(bytes, &p, handle), "fa_exchange_alloc");
+  return py::make_tuple(reinterpret_cast<uintptr_t>(p),
+                        py::bytes(handle, sizeof(handle)));
+}
+
+uintptr_t exchange_open(py::bytes handle, int64_t device) {
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  const std::string h = handle;
+  TORCH_CHECK(h.size() == 64, "an exchange handle is 64 bytes");
+  void *p = nullptr;
+  check_status(fa_exchange_open(h.data(), &p), "fa_exchange_open");
+  return reinterpret_cast<uintptr_t>(p);
+}
+
+void exchange_close(uintptr_t ptr, int64_t device) {
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  check_status(fa_exchange_close(reinterpret_cast<void *>(ptr)),
+               "fa_exchange_close");
+}
+
+void exchange_free(uintptr_t ptr, int64_t device) {
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  check_status(fa_exchange_free(reinterpret_cast<void *>(ptr)),
+               "fa_exchange_free");
+}
+
+at::Tensor decode_exchange(const at::Tensor &q, const at::Tensor &k_cache,
+                           const at::Tensor &v_cache,
+                           const at::Tensor &seq_lens, double scale,
+                           const at::Tensor &peers, int64_t rank,
+                           int64_t world, int64_t epoch) {
+  check_decode_inputs(q, k_cache, v_cache, seq_lens, scale);
+  TORCH_CHECK(q.size(3) == kHeadDim && k_cache.size(1) == q.size(1),
+              "sharded decode needs head_dim == ", kHeadDim,
+              " and one K/V head per query head");
+  check_cuda(peers, "peers");
+  TORCH_CHECK(peers.scalar_type() == at::kLong && peers.dim() == 1 &&
+                  peers.size(0) == world && peers.device() == q.device(),
+              "peers must be an int64 CUDA tensor of world buffer pointers");
+  TORCH_CHECK(epoch > 0 && epoch <= UINT32_MAX, "epoch out of range");
+  const c10::cuda::CUDAGuard guard(q.device());
+  const int B = to_int(q.size(0), "batch");
+  const int H = to_int(q.size(1), "heads");
+  const int S = to_int(k_cache.size(2), "cache length");
+  at::Tensor o = at::empty_like(q);
+  const size_t bytes = fa_decode_workspace_bytes(B, H, S, 0, q.get_device());
+  TORCH_CHECK(bytes > 0, "fa_decode_workspace_bytes failed");
+  DecodeScratch &ws = decode_scratch(q, bytes, static_cast<size_t>(B) * H);
+  check_status(
+      fa_decode_exchange(
+          q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+          seq_lens.data_ptr<int32_t>(), o.data_ptr(), B, H, S,
+          static_cast<float>(scale), ws.partials.data_ptr(),
+          static_cast<size_t>(ws.partials.numel()),
+          reinterpret_cast<uint32_t *>(ws.counters.data_ptr<int32_t>()),
+          static_cast<size_t>(ws.counters.numel()),
+          reinterpret_cast<float *const *>(peers.data_ptr<int64_t>()),
+          to_int(rank, "rank"), to_int(world, "world"),
+          static_cast<uint32_t>(epoch), current_stream()),
+      "fa_decode_exchange");
+  return o;
+}
+
 // Merges (G, B, H, 68) partials into the fp16 (B, H, 1, 64) output.
 at::Tensor merge_partials(const at::Tensor &partials) {
   check_cuda(partials, "partials");
@@ -400,6 +475,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "Decode with the new token's K/V row stored into the cache in the same launch",
         py::arg("q"), py::arg("k_new"), py::arg("v_new"), py::arg("k_cache"),
         py::arg("v_cache"), py::arg("seq_lens"), py::arg("scale"));
+  m.def("_exchange_bytes", &exchange_bytes);
+  m.def("_exchange_alloc", &exchange_alloc);
+  m.def("_exchange_open", &exchange_open);
+  m.def("_exchange_close", &exchange_close);
+  m.def("_exchange_free", &exchange_free);
+  m.def("decode_exchange", &decode_exchange,
+        "Sequence-sharded decode, cross-GPU combine inside the kernel",
+        py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
+        py::arg("seq_lens"), py::arg("scale"), py::arg("peers"),
+        py::arg("rank"), py::arg("world"), py::arg("epoch"));
   m.def("merge_partials", &merge_partials,
         "Merge (G, B, H, 68) decode partials into the fp16 output",
         py::arg("partials"));

@@ -206,7 +206,9 @@ int run_decode_gqa(const void *q, const void *k_cache, const void *v_cache,
                    int H, int H_kv, int S_max, float scale, int split_size,
                    void *workspace, size_t workspace_bytes, uint32_t *counters,
                    size_t counter_count, void *stream,
-                   const void *k_new = nullptr, const void *v_new = nullptr) {
+                   const void *k_new = nullptr, const void *v_new = nullptr,
+                   float *const *x_peers = nullptr, int x_rank = 0,
+                   int x_world = 1, uint32_t x_epoch = 0) {
   if (!decode_shape_ok(B, H, S_max, scale)) return FA_EINVAL;
   if (H_kv <= 0 || H % H_kv != 0) return FA_EINVAL;
   if (split_size > 0 && split_size % 4 != 0) return FA_EINVAL;
@@ -232,7 +234,14 @@ int run_decode_gqa(const void *q, const void *k_cache, const void *v_cache,
     return FA_ENOSPACE;
   if ((k_new == nullptr) != (v_new == nullptr)) return FA_EINVAL;
   if (k_new && (!aligned16(k_new) || !aligned16(v_new))) return FA_EALIGN;
-  DecodeArgs a;
+  if (x_peers && (H_kv != H || partial_out || k_new || x_world < 1 ||
+                  x_world > 32 || x_rank < 0 || x_rank >= x_world))
+    return FA_EINVAL;
+  DecodeArgs a{};
+  a.x_peers = x_peers;
+  a.x_rank = x_rank;
+  a.x_world = x_world;
+  a.x_epoch = x_epoch;
   a.k_new = static_cast<const __half *>(k_new);
   a.v_new = static_cast<const __half *>(v_new);
   a.k_cache_w = k_new ? static_cast<__half *>(const_cast<void *>(k_cache)) : nullptr;
@@ -355,6 +364,60 @@ size_t fa_decode_workspace_bytes(int B, int H, int S_max, int split_size,
   return workspace_bytes_for(B, H, decode_grid(sms, B, H, S_max, split_size));
 }
 
+size_t fa_exchange_bytes(int B, int H, int world) {
+  if (B <= 0 || H <= 0 || world <= 0 || world > 32) return 0;
+  const size_t bh = static_cast<size_t>(B) * H;
+  return align_up(bh * world * kPartialFloats * sizeof(float) +
+                      bh * sizeof(uint32_t),
+                  256);
+}
+
+int fa_exchange_alloc(size_t bytes, void **buffer, void *ipc_handle) {
+  if (!buffer || !ipc_handle || bytes == 0) return FA_EINVAL;
+  void *p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return FA_ECUDA;
+  cudaIpcMemHandle_t h;
+  if (cudaMemset(p, 0, bytes) != cudaSuccess ||
+      cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaFree(p);
+    return FA_ECUDA;
+  }
+  memcpy(ipc_handle, &h, sizeof(h));
+  *buffer = p;
+  return FA_OK;
+}
+
+int fa_exchange_open(const void *ipc_handle, void **peer_buffer) {
+  if (!ipc_handle || !peer_buffer) return FA_EINVAL;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  return cudaIpcOpenMemHandle(peer_buffer, h, cudaIpcMemLazyEnablePeerAccess) ==
+                 cudaSuccess
+             ? FA_OK
+             : FA_ECUDA;
+}
+
+int fa_exchange_close(void *peer_buffer) {
+  return cudaIpcCloseMemHandle(peer_buffer) == cudaSuccess ? FA_OK : FA_ECUDA;
+}
+
+int fa_exchange_free(void *buffer) {
+  return cudaFree(buffer) == cudaSuccess ? FA_OK : FA_ECUDA;
+}
+
+int fa_decode_exchange(const void *q, const void *k_cache, const void *v_cache,
+                       const int32_t *seq_lens, void *o, int B, int H,
+                       int S_max, float scale, void *workspace,
+                       size_t workspace_bytes, uint32_t *counters,
+                       size_t counter_count, float *const *peer_buffers,
+                       int rank, int world, uint32_t epoch, void *stream) {
+  if (!o || !peer_buffers || epoch == 0) return FA_EINVAL;
+  return run_decode_gqa(q, k_cache, v_cache, seq_lens, o, nullptr, B, H, H,
+                        S_max, scale, 0, workspace, workspace_bytes, counters,
+                        counter_count, stream, nullptr, nullptr, peer_buffers,
+                        rank, world, epoch);
+}
+
 size_t fa_decode_hd_workspace_bytes(int B, int H, int S_max, int head_dim,
                                     int split_size, int device) {
   if (head_dim == FA_HEAD_DIM)
@@ -396,7 +459,7 @@ int fa_decode_hd(const void *q, const void *k_cache, const void *v_cache,
                             decode_d128_partial_floats() * sizeof(float) ||
       counter_count < static_cast<size_t>(B) * H)
     return FA_ENOSPACE;
-  DecodeArgs a;
+  DecodeArgs a{};
   a.k_new = nullptr;
   a.v_new = nullptr;
   a.k_cache_w = nullptr;

@@ -162,11 +162,98 @@ __device__ void write_empty_sequence(const DecodeArgs &a, int b) {
   }
 }
 
+// ---- cross-GPU exchange of finished segments (sequence-sharded decode) ----
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];"
+               : "=r"(v)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint32_t *x_counters(const DecodeArgs &a, int r) {
+  return reinterpret_cast<uint32_t *>(
+      a.x_peers[r] + static_cast<size_t>(a.x_world) * a.B * a.H * kPartialFloats);
+}
+
+// Whole warp: stores this rank's (m, l, acc) of segment g into slot
+// [x_rank][g] of every rank's buffer (peer memory over NVLink, plain
+// stores), then raises each rank's counter of g. Lane l holds dims l, l+32.
+__device__ void x_send(const DecodeArgs &a, size_t g, float M, float L,
+                       float A0, float A1, int lane) {
+  const size_t BH = static_cast<size_t>(a.B) * a.H;
+  for (int r = 0; r < a.x_world; ++r) {
+    float *dst = a.x_peers[r] + (static_cast<size_t>(a.x_rank) * BH + g) * kPartialFloats;
+    dst[4 + lane] = A0;
+    dst[4 + 32 + lane] = A1;
+    if (lane == 0) {
+      dst[0] = M;
+      dst[1] = L;
+    }
+  }
+  __threadfence_system();
+  __syncwarp();
+  if (lane < a.x_world) atomicAdd_system(x_counters(a, lane) + g, 1u);
+  __syncwarp();
+}
+
+// Whole warp: waits (bounded) until all x_world partials of segment g are
+// in this rank's buffer, merges them (log-sum-exp, empty partials skipped,
+// rank order) and writes the fp16 output row.
+__device__ void x_finish(const DecodeArgs &a, size_t g, int lane) {
+  const size_t BH = static_cast<size_t>(a.B) * a.H;
+  const uint32_t *ctr = x_counters(a, a.x_rank) + g;
+  const uint32_t target = a.x_epoch * static_cast<uint32_t>(a.x_world);
+  int ok = 1;
+  if (lane == 0) {
+    unsigned long long t0 = 0;
+    while (static_cast<int>(ld_acquire_sys(ctr) - target) < 0) {
+      const unsigned long long now = global_timer_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > kWaitLimitNs) {
+        record_error(FA_ERR_TIMEOUT);
+        ok = 0;
+        break;
+      }
+    }
+  }
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (!ok) return;
+  (void)ld_acquire_sys(ctr);  // order this lane's reads after the arrivals
+  const float *base = a.x_peers[a.x_rank];
+  float M = kNegBig;
+  for (int r = 0; r < a.x_world; ++r) {
+    const float *p = base + (static_cast<size_t>(r) * BH + g) * kPartialFloats;
+    if (__ldcg(p + 1) > 0.f) M = fmaxf(M, __ldcg(p));
+  }
+  float L = 0.f, B0 = 0.f, B1 = 0.f;
+  for (int r = 0; r < a.x_world; ++r) {
+    const float *p = base + (static_cast<size_t>(r) * BH + g) * kPartialFloats;
+    const float l = __ldcg(p + 1);
+    if (l <= 0.f) continue;
+    const float f = fast_exp2(__ldcg(p) - M);
+    L = fmaf(l, f, L);
+    B0 = fmaf(__ldcg(p + 4 + lane), f, B0);
+    B1 = fmaf(__ldcg(p + 4 + 32 + lane), f, B1);
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  a.out[g * kHeadDim + lane] = __float2half_rn(B0 * inv);
+  a.out[g * kHeadDim + 32 + lane] = __float2half_rn(B1 * inv);
+}
+
 // Writes a finished (m, l, acc) for segment g: the fp16 output, or the
-// partial in partial mode. Lane l holds dims l and l + 32.
+// partial in partial mode, or (sharded) sends it to every rank and writes
+// the merge of all ranks. Lane l holds dims l and l + 32.
 __device__ __forceinline__ void finish_segment(const DecodeArgs &a, size_t g,
                                                float M, float L, float A0,
                                                float A1, int lane) {
+  if (a.x_peers) {
+    x_send(a, g, M, L, A0, A1, lane);
+    x_finish(a, g, lane);
+    return;
+  }
   if (a.partial_out) {
     float *p = a.partial_out + g * kPartialFloats;
     p[4 + lane] = A0;
@@ -279,12 +366,26 @@ __device__ void produce(const DecodeArgs &a, int nseg, int seg_per_plane,
   const int lane = threadIdx.x & 31;
     // ------------------------------------------------------------ planning
     long long sum_len = 0;
-    for (int b = lane; b < a.B; b += 32) {
-      const int len = seq_rows(a, b);
-      sum_len += len;
-      if (len == 0 && (b % static_cast<int>(gridDim.x)) ==
-                          static_cast<int>(blockIdx.x)) {
-        if (kD == kHeadDim) write_empty_sequence(a, b);  // other widths: caller
+    for (int chunk = 0; chunk < a.B; chunk += 32) {
+      const int b = chunk + lane;
+      const int len = b < a.B ? seq_rows(a, b) : 1;
+      if (b < a.B) sum_len += len;
+      // sequences without rows (other widths: written by the caller)
+      unsigned todo = __ballot_sync(
+          0xffffffffu, b < a.B && len == 0 &&
+                           (b % static_cast<int>(gridDim.x)) ==
+                               static_cast<int>(blockIdx.x));
+      while (kD == kHeadDim && todo) {
+        const int i = __ffs(todo) - 1;
+        todo &= todo - 1;
+        if (a.x_peers) {
+          // an empty partial for every rank now; merged after streaming
+          for (int h = 0; h < a.H; ++h)
+            x_send(a, static_cast<size_t>(chunk + i) * a.H + h, kNegBig, 0.f,
+                   0.f, 0.f, lane);
+        } else if (lane == 0) {
+          write_empty_sequence(a, chunk + i);
+        }
       }
     }
     const long long total = warp_sum_ll(sum_len) * nseg;
@@ -405,6 +506,24 @@ __device__ void produce(const DecodeArgs &a, int nseg, int seg_per_plane,
         // Consumers stopped early: let our copies land before the CTA exits.
         for (int j = (it > kNumStages ? it - kNumStages : 0); j < it; ++j)
           mbar_wait(&full[j % kNumStages], (j / kNumStages) & 1);
+      }
+    }
+    // Sharded: the rows of this CTA's empty sequences come from other
+    // ranks; merge them now that this CTA's own stream is issued.
+    if (kD == kHeadDim && a.x_peers) {
+      __syncwarp();
+      for (int chunk = 0; chunk < a.B; chunk += 32) {
+        const int b = chunk + lane;
+        unsigned todo = __ballot_sync(
+            0xffffffffu, b < a.B && seq_rows(a, b) == 0 &&
+                             (b % static_cast<int>(gridDim.x)) ==
+                                 static_cast<int>(blockIdx.x));
+        while (todo) {
+          const int i = __ffs(todo) - 1;
+          todo &= todo - 1;
+          for (int h = 0; h < a.H; ++h)
+            x_finish(a, static_cast<size_t>(chunk + i) * a.H + h, lane);
+        }
       }
     }
 }

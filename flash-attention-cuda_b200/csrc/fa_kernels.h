@@ -45,6 +45,14 @@ struct DecodeArgs {
   const __half *v_new;
   __half *k_cache_w;
   __half *v_cache_w;
+  // cross-GPU exchange (null when not sharded): x_peers[r] is rank r's
+  // exchange buffer, (x_world, B*H, 68) fp32 partials then B*H uint32
+  // arrival counters; each finished segment is sent to every rank and the
+  // merged output written once all x_world partials of it are present
+  // (counters reach x_epoch * x_world)
+  float *const *x_peers;
+  int x_rank, x_world;
+  uint32_t x_epoch;
   int B, H, S_max;
   int H_kv;  // K/V heads; H / H_kv query heads share each
   float scale_log2;

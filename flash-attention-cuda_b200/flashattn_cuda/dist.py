@@ -126,3 +126,74 @@ def sharded_decode(q, k_local, v_local, seq_lens_local, scale, group=None):
                            device=part.device)
     dist.all_gather_into_tensor(gathered, part, group=group)
     return merge_partials(gathered)
+
+
+class PeerExchange:
+    """Exchange buffers for sharded_decode_fused on one process group.
+
+    Each rank allocates one device buffer (fa_exchange_alloc), the 64-byte
+    IPC handles are all-gathered on the host, and every rank maps the
+    others' buffers; the kernel then stores its finished partials straight
+    into every rank's buffer over NVLink. One instance serves any number of
+    calls with this (B, H); all ranks must call in the same order."""
+
+    def __init__(self, batch, heads, group=None, device=None):
+        import torch
+        import torch.distributed as dist
+
+        from . import _C
+
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.device = torch.cuda.current_device() if device is None else device
+        self.shape = (batch, heads)
+        nbytes = _C._exchange_bytes(batch, heads, self.world)
+        self._own, handle = _C._exchange_alloc(nbytes, self.device)
+        handles = [handle]
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, handle, group=group)
+        self._opened = []
+        ptrs = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                ptrs.append(self._own)
+            else:
+                p = _C._exchange_open(h, self.device)
+                self._opened.append(p)
+                ptrs.append(p)
+        self.peers = torch.tensor(ptrs, dtype=torch.int64,
+                                  device=torch.device("cuda", self.device))
+        self.epoch = 0
+
+    def close(self):
+        """Unmaps the peers' buffers and frees this rank's (after a barrier
+        so no peer still writes into it)."""
+        import torch
+        import torch.distributed as dist
+
+        from . import _C
+
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        for p in self._opened:
+            _C._exchange_close(p, self.device)
+        self._opened = []
+        if self._own:
+            _C._exchange_free(self._own, self.device)
+            self._own = 0
+
+
+def sharded_decode_fused(q, k_local, v_local, seq_lens_local, scale, xchg):
+    """sharded_decode with the combine inside the decode kernel: every rank
+    passes the full q and its own KV chunk (lengths clamped to the chunk, see
+    local_seq_lens) and gets the full fp16 output from one launch."""
+    from . import _C
+
+    if tuple(q.shape[:2]) != xchg.shape:
+        raise ValueError(f"exchange was sized for {xchg.shape}, got {tuple(q.shape[:2])}")
+    xchg.epoch += 1
+    return _C.decode_exchange(q, k_local, v_local, seq_lens_local, scale,
+                              xchg.peers, xchg.rank, xchg.world, xchg.epoch)

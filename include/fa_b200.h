@@ -129,6 +129,35 @@ int fa_decode_hd(const void *q, const void *k_cache, const void *v_cache,
                  size_t counter_count, void *stream);
 
 /*
+ * Sequence-sharded decode with the cross-GPU combine inside the kernel.
+ * Rank r of `world` (one GPU each, world <= 32) holds a contiguous chunk of
+ * every sequence's KV cache (caches (B, H, S_max, 64) of its chunk,
+ * seq_lens = rows of the chunk). Each rank allocates one exchange buffer of
+ * fa_exchange_bytes(B, H, world) bytes with fa_exchange_alloc (zeroed, with
+ * a 64-byte IPC handle), sends the handle to the others and maps theirs
+ * with fa_exchange_open; peer_buffers is a device array of the world
+ * buffer pointers, index = rank. Every call passes the same epoch on all
+ * ranks, starting at 1 and increasing by one per call. Each finished
+ * (b, h) partial (m, l, acc[64]) is stored into every rank's buffer over
+ * NVLink and counted; each rank then merges all ranks' partials (waits are
+ * bounded) and writes the full (B, H, 1, 64) output. Replaces the
+ * reference-named exchange (decode_partial + NCCL all-gather + merge, the
+ * (m, l, o) combine of csrc/decode.cu:143-175 across GPUs). After a
+ * device error the buffers and epochs must be re-created.
+ */
+size_t fa_exchange_bytes(int B, int H, int world);
+int fa_exchange_alloc(size_t bytes, void **buffer, void *ipc_handle);
+int fa_exchange_open(const void *ipc_handle, void **peer_buffer);
+int fa_exchange_close(void *peer_buffer);
+int fa_exchange_free(void *buffer);
+int fa_decode_exchange(const void *q, const void *k_cache, const void *v_cache,
+                       const int32_t *seq_lens, void *o, int B, int H,
+                       int S_max, float scale, void *workspace,
+                       size_t workspace_bytes, uint32_t *counters,
+                       size_t counter_count, float *const *peer_buffers,
+                       int rank, int world, uint32_t epoch, void *stream);
+
+/*
  * Decode with the KV-cache append fused in: for every sequence b the new
  * token's k_new / v_new rows (B, H_kv, 1, 64) fp16 are stored at row
  * p = max(seq_lens[b], 0) of k_cache / v_cache (B, H_kv, S_max, 64) and the
