@@ -132,3 +132,46 @@ def test_python_package_exports_the_reference_surface():
         assert hasattr(flashattn_cuda, name)
     assert flashattn_cuda.head_dim == 64
     assert flashattn_cuda.choose_decode_split(512, 1, 12, 296) == 128
+
+
+def test_new_entry_points_reject_bad_arguments_without_a_device(lib):
+    """head_dim, append and exchange entry points validate on the host
+    before touching a device (status codes only, no GPU here)."""
+    vp = ctypes.c_void_p
+    p = ctypes.c_void_p(4096)
+    lib.fa_prefill_hd.argtypes = [vp] * 4 + [ctypes.c_int] * 6 + [ctypes.c_float, vp]
+    # head_dim 96 is not built; 0 heads; non-dividing K/V heads
+    assert lib.fa_prefill_hd(p, p, p, p, 1, 2, 2, 16, 96, 1, 0.1, None) == FA_EINVAL
+    assert lib.fa_prefill_hd(p, p, p, p, 1, 0, 1, 16, 128, 1, 0.1, None) == FA_EINVAL
+    assert lib.fa_prefill_hd(p, p, p, p, 1, 6, 4, 16, 128, 1, 0.1, None) == FA_EINVAL
+    assert lib.fa_prefill_hd(p, p, p, p, 1, 2, 2, 16, 128, 1, math.nan, None) == FA_EINVAL
+    odd = ctypes.c_void_p(4096 + 8)
+    assert lib.fa_prefill_hd(p, odd, p, p, 1, 2, 2, 16, 128, 1, 0.1, None) == FA_EALIGN
+    lib.fa_decode_hd.argtypes = [vp] * 5 + [ctypes.c_int] * 4 + [
+        ctypes.c_float, ctypes.c_int, vp, ctypes.c_size_t, vp, ctypes.c_size_t, vp]
+    assert lib.fa_decode_hd(p, p, p, p, p, 1, 1, 8, 96, 0.1, 0, p, 1 << 20, p, 1,
+                            None) == FA_EINVAL
+    assert lib.fa_decode_hd(p, p, p, p, p, 1, 1, 8, 128, 0.1, 6, p, 1 << 20, p, 1,
+                            None) == FA_EINVAL
+    lib.fa_decode_append.argtypes = [vp] * 7 + [ctypes.c_int] * 4 + [
+        ctypes.c_float, vp, ctypes.c_size_t, vp, ctypes.c_size_t, vp]
+    # the new-token rows are required
+    assert lib.fa_decode_append(p, None, p, p, p, p, p, 1, 2, 2, 8, 0.1, p,
+                                1 << 20, p, 2, None) == FA_EINVAL
+    lib.fa_decode_exchange.argtypes = [vp] * 5 + [ctypes.c_int] * 3 + [
+        ctypes.c_float, vp, ctypes.c_size_t, vp, ctypes.c_size_t, vp,
+        ctypes.c_int, ctypes.c_int, ctypes.c_uint32, vp]
+    # epoch 0 is reserved (counters start at zero)
+    assert lib.fa_decode_exchange(p, p, p, p, p, 1, 2, 8, 0.1, p, 1 << 20, p, 2,
+                                  p, 0, 1, 0, None) == FA_EINVAL
+
+
+def test_exchange_buffer_size(lib):
+    lib.fa_exchange_bytes.restype = ctypes.c_size_t
+    lib.fa_exchange_bytes.argtypes = [ctypes.c_int] * 3
+    for b, h, w in [(1, 14, 8), (64, 12, 2), (3, 5, 1)]:
+        n = lib.fa_exchange_bytes(b, h, w)
+        need = b * h * w * 68 * 4 + b * h * 4
+        assert need <= n < need + 256 and n % 256 == 0
+    assert lib.fa_exchange_bytes(1, 14, 0) == 0
+    assert lib.fa_exchange_bytes(1, 14, 33) == 0
