@@ -314,7 +314,8 @@ int fa_prefill_hd(const void *q, const void *k, const void *v, void *o, int B,
   if (!q || !k || !v || !o) return FA_EINVAL;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
     return FA_EALIGN;
-  int rc = ensure_device(nullptr);
+  int dev = 0;
+  int rc = ensure_device(&dev);
   if (rc != FA_OK) return rc;
   CUtensorMap tq, tk, tv;
   if (make_bhnd_map(&tq, q, B * H, N, 128, 128) != FA_OK ||
@@ -323,6 +324,7 @@ int fa_prefill_hd(const void *q, const void *k, const void *v, void *o, int B,
     return FA_EINVAL;
   return launch_prefill_d128_kernel(tq, tk, tv, static_cast<__half *>(o), B,
                                     H, N, causal != 0, scale, H_kv,
+                                    g_devices[dev].sms,
                                     static_cast<cudaStream_t>(stream)) ==
                  cudaSuccess
              ? FA_OK
@@ -340,7 +342,8 @@ int fa_prefill_gqa(const void *q, const void *k, const void *v, void *o, int B,
   if (!q || !k || !v || !o) return FA_EINVAL;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
     return FA_EALIGN;
-  int rc = ensure_device(nullptr);
+  int dev = 0;
+  int rc = ensure_device(&dev);
   if (rc != FA_OK) return rc;
   CUtensorMap tq, tk, tv;
   if (make_bhn64_map(&tq, q, B * H, N) != FA_OK ||
@@ -348,7 +351,7 @@ int fa_prefill_gqa(const void *q, const void *k, const void *v, void *o, int B,
       make_bhn64_map(&tv, v, B * H_kv, N) != FA_OK)
     return FA_EINVAL;
   return launch_prefill_kernel(tq, tk, tv, static_cast<__half *>(o), B, H, N,
-                               causal != 0, scale, H_kv,
+                               causal != 0, scale, H_kv, g_devices[dev].sms,
                                static_cast<cudaStream_t>(stream)) == cudaSuccess
              ? FA_OK
              : FA_ECUDA;

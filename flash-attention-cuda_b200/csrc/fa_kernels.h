@@ -16,7 +16,7 @@ cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
                                   const CUtensorMap &tm_k,
                                   const CUtensorMap &tm_v, __half *out, int B,
                                   int H, int N, bool causal, float scale,
-                                  int H_kv, cudaStream_t stream);
+                                  int H_kv, int sms, cudaStream_t stream);
 
 // ---- prefill, head_dim 128 (prefill_d128_sm100.cu) -------------------------
 const void *prefill_d128_kernel_ptr();
@@ -25,7 +25,7 @@ cudaError_t launch_prefill_d128_kernel(const CUtensorMap &tm_q,
                                        const CUtensorMap &tm_k,
                                        const CUtensorMap &tm_v, __half *out,
                                        int B, int H, int N, bool causal,
-                                       float scale, int H_kv,
+                                       float scale, int H_kv, int sms,
                                        cudaStream_t stream);
 
 // ---- decode (decode_sm100.cu) ---------------------------------------------

@@ -120,11 +120,13 @@ struct TileInfo {
 };
 
 __device__ __forceinline__ TileInfo tile_info(int pair, int t, int N,
-                                              int causal) {
+                                              int causal, int zigzag) {
   TileInfo ti;
-  ti.qt = kTilesPerCta * pair + t;
   const int n_qt = (N + kBlockM - 1) / kBlockM;
-  if (ti.qt >= n_qt) {
+  // zig-zag: tile p with tile n_qt - 1 - p, so every causal pair attends
+  // the same number of keys (one-wave grids)
+  ti.qt = zigzag ? (t == 0 ? pair : n_qt - 1 - pair) : kTilesPerCta * pair + t;
+  if (ti.qt >= n_qt || (t == 1 && zigzag && ti.qt == pair)) {
     ti.n_kv = 0;
   } else {
     const int keys = causal ? min((ti.qt + 1) * kBlockM, N) : N;
@@ -143,6 +145,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
+  // bit 0: causal; bit 1: zig-zag query-tile pairing
+  const int zigzag = causal >> 1;
+  causal &= 1;
   if (device_failed()) return;
   if (smem_u32(smem) & 1023u) {
     if (threadIdx.x == 0) record_error(FA_ERR_SMEM_ALIGN);
@@ -155,8 +160,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int pair = n_pairs - 1 - static_cast<int>(blockIdx.x / BH);
   const int bh = static_cast<int>(blockIdx.x % BH);
   const int kv_bh = (bh / H) * (H / group) + (bh % H) / group;
-  const TileInfo t0 = tile_info(pair, 0, N, causal);
-  const TileInfo t1 = tile_info(pair, 1, N, causal);
+  const TileInfo t0 = tile_info(pair, 0, N, causal, zigzag);
+  const TileInfo t1 = tile_info(pair, 1, N, causal, zigzag);
   const int n_kv = t0.n_kv > t1.n_kv ? t0.n_kv : t1.n_kv;
 
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kBarOff);
@@ -201,7 +206,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool two = t1.n_kv > 0;
         mbar_arrive_expect_tx(&bars[kBarQFull], (two ? 2 : 1) * kQTile);
         for (int t = 0; t < (two ? 2 : 1); ++t) {
-          const int row0 = (kTilesPerCta * pair + t) * kBlockM;
+          const int row0 = (t == 0 ? t0.qt : t1.qt) * kBlockM;
           for (int h = 0; h < 2; ++h)
             tma_load_3d(smem + kQOff + t * kQTile + h * kQHalf, &tm_q,
                         &bars[kBarQFull], 64 * h, row0, bh);
@@ -475,7 +480,7 @@ cudaError_t launch_prefill_d128_kernel(const CUtensorMap &tm_q,
                                        const CUtensorMap &tm_k,
                                        const CUtensorMap &tm_v, __half *out,
                                        int B, int H, int N, bool causal,
-                                       float scale, int H_kv,
+                                       float scale, int H_kv, int sms,
                                        cudaStream_t stream) {
   const int BH = B * H;
   const int n_qt = (N + prefill128::kBlockM - 1) / prefill128::kBlockM;
@@ -484,9 +489,13 @@ cudaError_t launch_prefill_d128_kernel(const CUtensorMap &tm_q,
   const unsigned grid =
       static_cast<unsigned>(n_pairs) * static_cast<unsigned>(BH);
   const float scale_log2 = scale * 1.4426950408889634f;
+  // One wave of CTAs: zig-zag pairs of equal causal work, so the kernel
+  // does not wait on the heaviest pair. Several waves: heaviest first.
+  const int zigzag = causal && grid <= static_cast<unsigned>(sms) ? 2 : 0;
   prefill128::prefill_d128_kernel<<<grid, prefill128::kThreads,
                                     prefill128::kSmemBytes, stream>>>(
-      tm_q, tm_k, tm_v, out, N, BH, causal ? 1 : 0, scale_log2, H, H / H_kv);
+      tm_q, tm_k, tm_v, out, N, BH, (causal ? 1 : 0) | zigzag, scale_log2, H,
+      H / H_kv);
   return cudaGetLastError();
 }
 

@@ -117,11 +117,13 @@ struct TileInfo {
 };
 
 __device__ __forceinline__ TileInfo tile_info(int pair, int t, int N,
-                                              int causal) {
+                                              int causal, int zigzag) {
   TileInfo ti;
-  ti.qt = 2 * pair + t;
   const int n_qt = (N + kBlockM - 1) / kBlockM;
-  if (ti.qt >= n_qt) {
+  // zig-zag: tile p with tile n_qt - 1 - p, so every causal pair attends
+  // the same number of keys (one-wave grids)
+  ti.qt = zigzag ? (t == 0 ? pair : n_qt - 1 - pair) : 2 * pair + t;
+  if (ti.qt >= n_qt || (t == 1 && zigzag && ti.qt == pair)) {
     ti.n_kv = 0;
   } else {
     ti.n_kv = causal ? ti.qt + 1 : (N + kBlockN - 1) / kBlockN;
@@ -139,6 +141,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
+  // bit 0: causal; bit 1: zig-zag query-tile pairing
+  const int zigzag = causal >> 1;
+  causal &= 1;
   if (device_failed()) return;
   if (smem_u32(smem) & 1023u) {
     if (threadIdx.x == 0) record_error(FA_ERR_SMEM_ALIGN);
@@ -154,8 +159,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   // K/V head of this query head: `group` query heads share one K/V head
   // (group == 1 without grouped-query attention).
   const int kv_bh = (bh / H) * (H / group) + (bh % H) / group;
-  const TileInfo t0 = tile_info(pair, 0, N, causal);
-  const TileInfo t1 = tile_info(pair, 1, N, causal);
+  const TileInfo t0 = tile_info(pair, 0, N, causal, zigzag);
+  const TileInfo t1 = tile_info(pair, 1, N, causal, zigzag);
   const int n_kv = t0.n_kv > t1.n_kv ? t0.n_kv : t1.n_kv;
 
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kBarOff);
@@ -510,7 +515,7 @@ cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
                                   const CUtensorMap &tm_k,
                                   const CUtensorMap &tm_v, __half *out, int B,
                                   int H, int N, bool causal, float scale,
-                                  int H_kv, cudaStream_t stream) {
+                                  int H_kv, int sms, cudaStream_t stream) {
   static_assert(prefill::kBlockM == prefill::kBlockN,
                 "causal tile skipping assumes square tiles");
   const int BH = B * H;
@@ -519,9 +524,13 @@ cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
   const unsigned grid =
       static_cast<unsigned>(n_pairs) * static_cast<unsigned>(BH);
   const float scale_log2 = scale * 1.4426950408889634f;
+  // One wave of CTAs: zig-zag pairs of equal causal work, so the kernel
+  // does not wait on the heaviest pair. Several waves: heaviest first.
+  const int zigzag = causal && grid <= static_cast<unsigned>(sms) ? 2 : 0;
   prefill::prefill_kernel<<<grid, prefill::kThreads, prefill::kSmemBytes,
                             stream>>>(tm_q, tm_k, tm_v, out, N, BH,
-                                      causal ? 1 : 0, scale_log2, H, H / H_kv);
+                                      (causal ? 1 : 0) | zigzag, scale_log2, H,
+                                      H / H_kv);
   return cudaGetLastError();
 }
 
