@@ -432,6 +432,20 @@ def run_ours(args, rank, world, local_rank):
                           args.warmup) / args.steps
             launches += args.steps
             kv_bytes = C5["S"] * 2 * HEAD_DIM * 2 * 2
+            # grouped decode at head_dim 128 (32 query heads on 8 K/V heads)
+            qd8 = randn(8, 32, 1, 128, seed=99)
+            kc8 = randn(8, 8, 32768, 128, seed=100)
+            vc8 = randn(8, 8, 32768, 128, seed=101)
+            lens8 = torch.full((8,), 32768, dtype=torch.int32, device="cuda")
+            t8 = timer.run(lambda: fa.decode(qd8, kc8, vc8, lens8, 128 ** -0.5),
+                           args.steps, args.warmup) / args.steps
+            launches += args.steps
+            b8 = 8 * 8 * 32768 * 128 * 2 * 2
+            secondary["decode_gqa_d128_b8_h32_kv8"] = {
+                "ms": round(t8, 5), "kv_gbs": round(b8 / (t8 * 1e-3) / 1e9, 1),
+                "frac_of_measured_hbm": round(b8 / (t8 * 1e-3) / 1e9 / hbm, 4),
+                "note": "B=8, 32 query heads on 8 K/V heads, S=32768, head_dim 128"}
+            del qd8, kc8, vc8
             secondary["c5_decode_gqa_kv2"] = {
                 "ms": round(t, 5),
                 "kv_gbs": round(kv_bytes / (t * 1e-3) / 1e9, 1),

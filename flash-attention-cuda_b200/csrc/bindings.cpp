@@ -186,11 +186,10 @@ at::Tensor decode_impl(const at::Tensor &q, const at::Tensor &k_cache,
   at::Tensor o = at::empty_like(q);
   const int H_kv = to_int(k_cache.size(1), "kv heads");
   const int D = to_int(q.size(3), "head_dim");
-  TORCH_CHECK(D == kHeadDim || H_kv == H,
-              "grouped K/V heads need head_dim == ", kHeadDim);
   const size_t bytes =
-      H_kv != H ? fa_decode_gqa_workspace_bytes(B, H, H_kv, S, q.get_device())
-                : fa_decode_hd_workspace_bytes(B, H, S, D, split, q.get_device());
+      H_kv != H
+          ? fa_decode_gqa_hd_workspace_bytes(B, H, H_kv, S, D, q.get_device())
+          : fa_decode_hd_workspace_bytes(B, H, S, D, split, q.get_device());
   TORCH_CHECK(bytes > 0, "fa_decode_workspace_bytes failed");
   DecodeScratch &ws = decode_scratch(q, bytes, static_cast<size_t>(B) * H);
   uint32_t *ctr = reinterpret_cast<uint32_t *>(ws.counters.data_ptr<int32_t>());
@@ -205,11 +204,12 @@ at::Tensor decode_impl(const at::Tensor &q, const at::Tensor &k_cache,
   } else {
     TORCH_CHECK(split == 0, "a forced split size needs one K/V head per query head");
     check_status(
-        fa_decode_gqa(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
-                      seq_lens.data_ptr<int32_t>(), o.data_ptr(), B, H, H_kv, S,
-                      static_cast<float>(scale), ws.partials.data_ptr(),
-                      static_cast<size_t>(ws.partials.numel()), ctr,
-                      static_cast<size_t>(ws.counters.numel()), current_stream()),
+        fa_decode_gqa_hd(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                         seq_lens.data_ptr<int32_t>(), o.data_ptr(), B, H, H_kv,
+                         S, D, static_cast<float>(scale), ws.partials.data_ptr(),
+                         static_cast<size_t>(ws.partials.numel()), ctr,
+                         static_cast<size_t>(ws.counters.numel()),
+                         current_stream()),
         "fa_decode_gqa");
   }
   return o;

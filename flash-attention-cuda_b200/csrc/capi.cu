@@ -85,9 +85,12 @@ int ensure_device(int *device_out) {
       cudaFuncSetAttribute(prefill_d128_kernel_ptr(),
                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                            prefill_d128_smem_bytes()) != cudaSuccess ||
-      cudaFuncSetAttribute(decode_gqa_kernel_ptr(),
+      cudaFuncSetAttribute(decode_gqa_kernel_ptr(64),
                            cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           decode_gqa_smem_bytes()) != cudaSuccess ||
+                           decode_gqa_smem_bytes(64)) != cudaSuccess ||
+      cudaFuncSetAttribute(decode_gqa_kernel_ptr(128),
+                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           decode_gqa_smem_bytes(128)) != cudaSuccess ||
       // Both kernels are sized for two CTAs per SM, which needs the whole
       // unified L1/shared array configured as shared memory.
       cudaFuncSetAttribute(prefill_kernel_ptr(),
@@ -190,9 +193,10 @@ int decode_gqa_grid(int sms, int B, const GqaPlan &p, int S_max,
   return static_cast<int>(g < 1 ? 1 : g);
 }
 
-size_t gqa_workspace_bytes_for(int B, const GqaPlan &p, int grid) {
+size_t gqa_workspace_bytes_for(int B, const GqaPlan &p, int grid,
+                               int head_dim = FA_HEAD_DIM) {
   return (static_cast<size_t>(B) * p.n_seg_per_b + grid) * p.heads_per_seg *
-         kPartialFloats * sizeof(float);
+         (4 + head_dim) * sizeof(float);
 }
 
 bool decode_shape_ok(int B, int H, int S_max, float scale) {
@@ -208,7 +212,11 @@ int run_decode_gqa(const void *q, const void *k_cache, const void *v_cache,
                    size_t counter_count, void *stream,
                    const void *k_new = nullptr, const void *v_new = nullptr,
                    float *const *x_peers = nullptr, int x_rank = 0,
-                   int x_world = 1, uint32_t x_epoch = 0) {
+                   int x_world = 1, uint32_t x_epoch = 0,
+                   int head_dim = FA_HEAD_DIM) {
+  if (head_dim != FA_HEAD_DIM && (head_dim != 128 || H_kv == H || k_new ||
+                                  x_peers || partial_out || split_size > 0))
+    return FA_EINVAL;
   if (!decode_shape_ok(B, H, S_max, scale)) return FA_EINVAL;
   if (H_kv <= 0 || H % H_kv != 0) return FA_EINVAL;
   if (split_size > 0 && split_size % 4 != 0) return FA_EINVAL;
@@ -228,7 +236,7 @@ int run_decode_gqa(const void *q, const void *k_cache, const void *v_cache,
   const int grid =
       grouped ? decode_gqa_grid(g_devices[dev].sms, B, plan, S_max, split_size)
               : decode_grid(g_devices[dev].sms, B, H, S_max, split_size);
-  const size_t need = grouped ? gqa_workspace_bytes_for(B, plan, grid)
+  const size_t need = grouped ? gqa_workspace_bytes_for(B, plan, grid, head_dim)
                               : workspace_bytes_for(B, H, grid);
   if (workspace_bytes < need || counter_count < static_cast<size_t>(B) * H)
     return FA_ENOSPACE;
@@ -263,10 +271,11 @@ int run_decode_gqa(const void *q, const void *k_cache, const void *v_cache,
   a.grid = grid;
   if (grouped) {
     CUtensorMap tk, tv;
-    if (make_bhn64_map(&tk, k_cache, B * H_kv, S_max) != FA_OK ||
-        make_bhn64_map(&tv, v_cache, B * H_kv, S_max) != FA_OK)
+    const int rows = decode_gqa_box_rows(head_dim);
+    if (make_bhnd_map(&tk, k_cache, B * H_kv, S_max, head_dim, rows) != FA_OK ||
+        make_bhnd_map(&tv, v_cache, B * H_kv, S_max, head_dim, rows) != FA_OK)
       return FA_EINVAL;
-    return launch_decode_gqa_kernel(a, tk, tv,
+    return launch_decode_gqa_kernel(a, tk, tv, head_dim,
                                     static_cast<cudaStream_t>(stream)) ==
                    cudaSuccess
                ? FA_OK
@@ -486,6 +495,38 @@ int fa_decode_hd(const void *q, const void *k_cache, const void *v_cache,
                  cudaSuccess
              ? FA_OK
              : FA_ECUDA;
+}
+
+size_t fa_decode_gqa_hd_workspace_bytes(int B, int H, int H_kv, int S_max,
+                                        int head_dim, int device) {
+  if (head_dim == FA_HEAD_DIM)
+    return fa_decode_gqa_workspace_bytes(B, H, H_kv, S_max, device);
+  if (head_dim != 128 || B <= 0 || H <= 0 || S_max <= 0 || H_kv <= 0 ||
+      H % H_kv != 0)
+    return 0;
+  if (H_kv == H) return fa_decode_hd_workspace_bytes(B, H, S_max, 128, 0, device);
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) !=
+      cudaSuccess)
+    return 0;
+  const GqaPlan p = gqa_plan(H, H_kv);
+  return gqa_workspace_bytes_for(B, p, decode_gqa_grid(sms, B, p, S_max, 0), 128);
+}
+
+int fa_decode_gqa_hd(const void *q, const void *k_cache, const void *v_cache,
+                     const int32_t *seq_lens, void *o, int B, int H, int H_kv,
+                     int S_max, int head_dim, float scale, void *workspace,
+                     size_t workspace_bytes, uint32_t *counters,
+                     size_t counter_count, void *stream) {
+  if (head_dim == 128 && H_kv == H)
+    return fa_decode_hd(q, k_cache, v_cache, seq_lens, o, B, H, S_max, 128,
+                        scale, 0, workspace, workspace_bytes, counters,
+                        counter_count, stream);
+  if (!o) return FA_EINVAL;
+  return run_decode_gqa(q, k_cache, v_cache, seq_lens, o, nullptr, B, H, H_kv,
+                        S_max, scale, 0, workspace, workspace_bytes, counters,
+                        counter_count, stream, nullptr, nullptr, nullptr, 0, 1,
+                        0, head_dim);
 }
 
 size_t fa_decode_gqa_workspace_bytes(int B, int H, int H_kv, int S_max,

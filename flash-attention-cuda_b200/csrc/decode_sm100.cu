@@ -359,6 +359,7 @@ __device__ void merger(const DecodeArgs &a, uint8_t *red_base,
 // kD: head dim of the cache rows; kRowsPerStage x 2 kD bytes = one stage.
 template <bool kTiled, int kNumStages, int kD = kHeadDim,
           int kRowsPerStage = kStageRows>
+// (every stage is kStageBytes: kRowsPerStage * 2 * kD == kStageBytes)
 __device__ void produce(const DecodeArgs &a, int nseg, int seg_per_plane,
                         uint8_t *smem, uint32_t k_off, uint32_t v_off,
                         uint64_t *full, uint64_t *empty, StageHeader *hdr,
@@ -470,14 +471,18 @@ __device__ void produce(const DecodeArgs &a, int nseg, int seg_per_plane,
           hd.c1 = c1;
           hd.r0 = r + static_cast<int>(r0 - cur);
           if (kTiled) {
-            // whole 128-row boxes, 128-byte swizzled; rows past the piece
-            // are loaded but masked by the consumers
+            // whole boxes of kRowsPerStage rows, 128-byte swizzled, one box
+            // per 64 head dims (blocks of kRowsPerStage x 128 B); rows past
+            // the piece are loaded but masked by the consumers
             const int row_in_plane = r + static_cast<int>(r0 - cur);
             mbar_arrive_expect_tx(&full[slot], 2 * kStageBytes);
-            tma_load_3d(smem + k_off + slot * kStageBytes, tm_k, &full[slot], 0,
-                        row_in_plane, g_kv);
-            tma_load_3d(smem + v_off + slot * kStageBytes, tm_v, &full[slot], 0,
-                        row_in_plane, g_kv);
+#pragma unroll
+            for (int hb = 0; hb < kD / 64; ++hb) {
+              tma_load_3d(smem + k_off + slot * kStageBytes + hb * kRowsPerStage * 128,
+                          tm_k, &full[slot], 64 * hb, row_in_plane, g_kv);
+              tma_load_3d(smem + v_off + slot * kStageBytes + hb * kRowsPerStage * 128,
+                          tm_v, &full[slot], 64 * hb, row_in_plane, g_kv);
+            }
           } else {
             const size_t elem = (row0 + static_cast<size_t>(r0 - cur)) * kD;
             const uint32_t bytes = static_cast<uint32_t>(n) * 2 * kD;
@@ -762,569 +767,6 @@ __global__ void __launch_bounds__(kHeadDim)
 }
 
 
-// ===========================================================================
-// Grouped-query decode: every K/V row is read once for all the query heads
-// that share its K/V head.
-//
-// A segment is (b, K/V head, chunk of up to 16 of its query heads). The
-// producer (produce<true>) streams 128-row boxes of the K and V planes by
-// TMA with the 128-byte swizzle. Consumer warp w takes keys [16w, 16w + 16)
-// of a stage and works on the tensor cores with warp-level MMAs
-// (m16n8k16, fp16 in, fp32 accumulate): S (16 heads x 16 keys) = Q K^T with
-// the group's queries as the M dimension, an online softmax per head row,
-// then O (16 heads x 64) += P V with P taken straight from the S registers.
-// K is read with ldmatrix, V with its transposed form, both conflict-free
-// on the swizzled rows. At the end of a piece the warps' per-head partials
-// go to the merger warp as in the per-head kernel.
-// ===========================================================================
-constexpr int kGqaMaxHeads = 16;  // query heads per segment (MMA M)
-constexpr int kGqaStages = 4;
-constexpr int kGqaConsumerWarps = kStageRows / 16;  // 16 keys per warp
-constexpr int kGqaThreads = (kGqaConsumerWarps + 2) * 32;
-constexpr uint32_t kGqaKOff = 0;
-constexpr uint32_t kGqaVOff = kGqaStages * kStageBytes;
-constexpr uint32_t kGqaHdrOff = 2 * kGqaStages * kStageBytes;
-constexpr uint32_t kGqaRedOff = kGqaHdrOff + kGqaStages * sizeof(StageHeader);
-constexpr uint32_t kGqaRedWarpFloats = kGqaMaxHeads * kPartialFloats;
-constexpr uint32_t kGqaRedBufBytes =
-    kGqaConsumerWarps * kGqaRedWarpFloats * 4 + 32;
-constexpr uint32_t kGqaBarOff = kGqaRedOff + kRedBufs * kGqaRedBufBytes;
-// bars: full[], empty[], red_full[], red_empty[], gather
-constexpr uint32_t kGqaPendOff = kGqaBarOff + (2 * kGqaStages + 2 * kRedBufs + 1) * 8;
-constexpr uint32_t kGqaSmemBytes = kGqaPendOff + 64;
-
-struct GqaSegment {
-  int b, h0, hv;  // batch entry, first query head, query heads in the chunk
-};
-
-__device__ __forceinline__ GqaSegment gqa_segment(const DecodeArgs &a, int g,
-                                                  int nseg, int n_hc,
-                                                  int group) {
-  GqaSegment sg;
-  sg.b = g / nseg;
-  const int s = g - sg.b * nseg;
-  const int kvh = s / n_hc;
-  const int hc = s - kvh * n_hc;
-  sg.h0 = kvh * group + hc * kGqaMaxHeads;
-  const int left = group - hc * kGqaMaxHeads;
-  sg.hv = left < kGqaMaxHeads ? left : kGqaMaxHeads;
-  return sg;
-}
-
-// Merger warp of the grouped kernel: per query head of the finished piece,
-// combines the consumer warps' partials; whole segments are written out,
-// split ones published to workspace slot (g + cta) * hs + head (hs = query
-// heads per segment, at most 16) and merged by the last CTA to arrive.
-// Segments whose cross-CTA merge this CTA owns are queued here and merged
-// by all consumer warps together once streaming is over.
-constexpr int kGqaMaxPending = 4;
-struct GqaPending {
-  int count;
-  int g[kGqaMaxPending], c0[kGqaMaxPending], c1[kGqaMaxPending];
-};
-// Partials a queued merge may span (its scratch lives in the stage buffers).
-constexpr int kGqaMergeCap = 1 << 20;
-static_assert(kGqaMaxHeads * (kHeadDim / 4) <= (kGqaConsumerWarps + 2) * 32,
-              "one merge thread per output float4");
-static_assert(sizeof(GqaPending) <= 64, "pending list slot");
-
-__device__ void merger_gqa(const DecodeArgs &a, int nseg, int n_hc, int group,
-                           uint8_t *red_base, uint64_t *red_full,
-                           uint64_t *red_empty, GqaPending *pend) {
-  const int lane = threadIdx.x & 31;
-  const int hs = group < kGqaMaxHeads ? group : kGqaMaxHeads;
-  for (int piece = 0;; ++piece) {
-    const int buf = piece & 1;
-    if (!mbar_wait(&red_full[buf], (piece >> 1) & 1)) return;
-    const float *red =
-        reinterpret_cast<const float *>(red_base + buf * kGqaRedBufBytes);
-    const int *hdr_in = reinterpret_cast<const int *>(
-        red + kGqaConsumerWarps * kGqaRedWarpFloats);
-    const int flags = hdr_in[1];
-    if (flags & kDone) return;
-    const int g = hdr_in[0];
-    const int c0 = hdr_in[2];
-    const int c1 = hdr_in[3];
-    const GqaSegment sg = gqa_segment(a, g, nseg, n_hc, group);
-    for (int i = 0; i < sg.hv; ++i) {
-      float M = kNegBig;
-#pragma unroll
-      for (int w = 0; w < kGqaConsumerWarps; ++w)
-        M = fmaxf(M, red[w * kGqaRedWarpFloats + i * kPartialFloats]);
-      float L = 0.f, A0 = 0.f, A1 = 0.f;
-#pragma unroll
-      for (int w = 0; w < kGqaConsumerWarps; ++w) {
-        const float *pw = red + w * kGqaRedWarpFloats + i * kPartialFloats;
-        const float fw = fast_exp2(pw[0] - M);
-        L = fmaf(pw[1], fw, L);
-        A0 = fmaf(pw[4 + lane], fw, A0);
-        A1 = fmaf(pw[4 + 32 + lane], fw, A1);
-      }
-      const size_t gq = static_cast<size_t>(sg.b) * a.H + sg.h0 + i;
-      if (flags & kWhole) {
-        finish_segment(a, gq, M, L, A0, A1, lane);
-      } else {
-        float *ws = a.ws_partials +
-                    ((static_cast<size_t>(g) + blockIdx.x) * hs + i) * kPartialFloats;
-        ws[4 + lane] = A0;
-        ws[4 + 32 + lane] = A1;
-        if (lane == 0) {
-          ws[0] = M;
-          ws[1] = L;
-        }
-      }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&red_empty[buf]);  // buffer consumed
-    if (flags & kWhole) continue;
-
-    __threadfence();
-    __syncwarp();
-    unsigned last = 0;
-    if (lane == 0) {
-      const unsigned n_parts = static_cast<unsigned>(c1 - c0);
-      last = atomicInc(&a.ws_counters[g], n_parts) == n_parts;
-    }
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (!last) continue;
-    __threadfence();
-    if (pend->count < kGqaMaxPending && c1 - c0 + 1 <= kGqaMergeCap) {
-      if (lane == 0) {
-        const int k = pend->count;
-        pend->g[k] = g;
-        pend->c0[k] = c0;
-        pend->c1[k] = c1;
-        pend->count = k + 1;
-      }
-      __syncwarp();
-      continue;
-    }
-    for (int i = 0; i < sg.hv; ++i) {
-      float M2 = kNegBig;
-      for (int c = c0 + lane; c <= c1; c += 32) {
-        const float *pp = a.ws_partials +
-                          ((static_cast<size_t>(g) + c) * hs + i) * kPartialFloats;
-        if (__ldcg(pp + 1) > 0.f) M2 = fmaxf(M2, __ldcg(pp));
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1)
-        M2 = fmaxf(M2, __shfl_xor_sync(0xffffffffu, M2, o));
-      float L2 = 0.f, B0 = 0.f, B1 = 0.f;
-#pragma unroll 4
-      for (int c = c0; c <= c1; ++c) {
-        const float *pp = a.ws_partials +
-                          ((static_cast<size_t>(g) + c) * hs + i) * kPartialFloats;
-        const float lc = __ldcg(pp + 1);
-        const float mc = __ldcg(pp);
-        const float x0 = __ldcg(pp + 4 + lane);
-        const float x1 = __ldcg(pp + 4 + 32 + lane);
-        const float fc = lc > 0.f ? fast_exp2(mc - M2) : 0.f;
-        L2 = fmaf(lc, fc, L2);
-        B0 = fmaf(x0, fc, B0);
-        B1 = fmaf(x1, fc, B1);
-      }
-      finish_segment(a, static_cast<size_t>(sg.b) * a.H + sg.h0 + i, M2, L2,
-                     B0, B1, lane);
-    }
-  }
-}
-
-// Cooperative last-arrival merge of segment g over CTAs c0..c1 by all the
-// threads of the CTA (every thread calls it). The partials are gathered into
-// shared memory with bulk async copies (one copy of hv records per CTA,
-// as many CTAs per round as `gather_bytes` holds), so each round costs one
-// L2 round trip, then combined there: per head a running (M, L), and each
-// thread owns one float4 of one head's output.
-__device__ void coop_merge(const DecodeArgs &a, int g, int c0, int c1,
-                           const GqaSegment &sg, int hs, uint8_t *gather,
-                           uint32_t gather_bytes, float *stats,
-                           uint64_t *gbar, uint32_t &gphase) {
-  const int tid = static_cast<int>(threadIdx.x);
-  const int nthreads = static_cast<int>(blockDim.x);
-  const int lane = tid & 31;
-  const int warp = tid >> 5;
-  const int nwarps = nthreads >> 5;
-  const int nc = c1 - c0 + 1;
-  const uint32_t rec_bytes = static_cast<uint32_t>(sg.hv) * kPartialFloats * 4;
-  const int per_round = static_cast<int>(gather_bytes / rec_bytes);
-  const float *recs = reinterpret_cast<const float *>(gather);
-  // stats: per head M, L (running) and the previous M of the round
-  const int i_own = tid / (kHeadDim / 4);
-  const int dq = tid % (kHeadDim / 4);
-  const bool owner = i_own < sg.hv;
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int i = tid; i < sg.hv; i += nthreads) {
-    stats[3 * i] = kNegBig;
-    stats[3 * i + 1] = 0.f;
-  }
-  for (int cb = 0; cb < nc; cb += per_round) {
-    const int n = nc - cb < per_round ? nc - cb : per_round;
-    if (warp == 0) {
-      // generic-proxy writes of the partials (other CTAs, ordered by the
-      // counter) and earlier shared-memory use come before the async copies
-      asm volatile("fence.proxy.async.global;" ::: "memory");
-      fence_proxy_async_smem();
-      if (lane == 0) mbar_arrive_expect_tx(gbar, rec_bytes * n);
-      __syncwarp();
-      for (int c = lane; c < n; c += 32) {
-        const float *src = a.ws_partials +
-                           (static_cast<size_t>(g) + c0 + cb + c) * hs * kPartialFloats;
-        asm volatile(
-            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes "
-            "[%0], [%1], %2, [%3];" ::"r"(smem_u32(gather + c * rec_bytes)),
-            "l"(src), "r"(rec_bytes), "r"(smem_u32(gbar))
-            : "memory");
-      }
-    }
-    const bool ok = mbar_wait(gbar, gphase);
-    gphase ^= 1u;
-    if (!__syncthreads_and(ok)) break;  // uniform: every thread leaves
-    // per head: the round's max and the rescaled running sum
-    for (int i = warp; i < sg.hv; i += nwarps) {
-      float mx = kNegBig;
-      for (int c = lane; c < n; c += 32) {
-        const float *r = recs + (c * sg.hv + i) * kPartialFloats;
-        if (r[1] > 0.f) mx = fmaxf(mx, r[0]);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1)
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      const float m_old = stats[3 * i];
-      const float m_new = fmaxf(m_old, mx);
-      float l = 0.f;
-      for (int c = lane; c < n; c += 32) {
-        const float *r = recs + (c * sg.hv + i) * kPartialFloats;
-        if (r[1] > 0.f) l = fmaf(r[1], fast_exp2(r[0] - m_new), l);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-      __syncwarp();
-      if (lane == 0) {
-        stats[3 * i + 1] = fmaf(stats[3 * i + 1], fast_exp2(m_old - m_new), l);
-        stats[3 * i] = m_new;
-        stats[3 * i + 2] = m_old;
-      }
-    }
-    __syncthreads();
-    if (owner) {
-      const float m_new = stats[3 * i_own];
-      const float f = fast_exp2(stats[3 * i_own + 2] - m_new);
-      acc.x *= f;
-      acc.y *= f;
-      acc.z *= f;
-      acc.w *= f;
-      for (int c = 0; c < n; ++c) {
-        const float *r = recs + (c * sg.hv + i_own) * kPartialFloats;
-        const float w = r[1] > 0.f ? fast_exp2(r[0] - m_new) : 0.f;
-        const float4 x = *reinterpret_cast<const float4 *>(r + 4 + 4 * dq);
-        acc.x = fmaf(w, x.x, acc.x);
-        acc.y = fmaf(w, x.y, acc.y);
-        acc.z = fmaf(w, x.z, acc.z);
-        acc.w = fmaf(w, x.w, acc.w);
-      }
-    }
-    __syncthreads();  // the buffer is free for the next round
-  }
-  if (owner) {
-    const size_t gq = static_cast<size_t>(sg.b) * a.H + sg.h0 + i_own;
-    const float M = stats[3 * i_own], L = stats[3 * i_own + 1];
-    if (a.partial_out) {
-      float *p = a.partial_out + gq * kPartialFloats;
-      *reinterpret_cast<float4 *>(p + 4 + 4 * dq) = acc;
-      if (dq == 0) {
-        p[0] = M;
-        p[1] = L;
-        p[2] = 0.f;
-        p[3] = 0.f;
-      }
-    } else {
-      const float inv = L > 0.f ? 1.f / L : 0.f;
-      __half2 h01 = __floats2half2_rn(acc.x * inv, acc.y * inv);
-      __half2 h23 = __floats2half2_rn(acc.z * inv, acc.w * inv);
-      uint2 v;
-      v.x = *reinterpret_cast<uint32_t *>(&h01);
-      v.y = *reinterpret_cast<uint32_t *>(&h23);
-      *reinterpret_cast<uint2 *>(a.out + gq * kHeadDim + 4 * dq) = v;
-    }
-  }
-  __syncthreads();
-}
-
-// Consumer warps of the grouped kernel.
-__device__ __forceinline__ void gqa_consume(
-    const DecodeArgs &a, int nseg, int n_hc, int group, uint8_t *smem,
-    uint64_t *full, uint64_t *empty, uint64_t *red_full, uint64_t *red_empty,
-    const StageHeader *hdr) {
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-
-  const int quad = lane >> 2;  // MMA row (query head) quad and quad + 8
-  const int qid = lane & 3;    // MMA column pair
-  const int key0 = warp * 16;  // this warp's keys within a stage
-  uint32_t qa[4][4];           // Q as the A operand, head dims 16kk..16kk+16
-  float o[8][4];               // O: dims 8dt + 2qid (+1), rows quad / quad+8
-  float m_r[2], l_r[2];
-  int cur_g = -1;
-  int app_row = -1;  // segment row of the appended token, -1 for none
-  uint4 app_val = make_uint4(0, 0, 0, 0);
-  int piece = 0;
-  auto reset = [&]() {
-    m_r[0] = m_r[1] = kNegBig;
-    l_r[0] = l_r[1] = 0.f;
-#pragma unroll
-    for (int dt = 0; dt < 8; ++dt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) o[dt][e] = 0.f;
-  };
-  reset();
-
-  for (int it = 0;; ++it) {
-    const int slot = it % kGqaStages;
-    if (!mbar_wait(&full[slot], (it / kGqaStages) & 1)) break;
-    const StageHeader hd = hdr[slot];
-    if (hd.flags & kDone) {
-      const int buf = piece & 1;
-      if (piece >= kRedBufs &&
-          !mbar_wait(&red_empty[buf], ((piece >> 1) - 1) & 1))
-        break;
-      if (warp == 0 && lane == 0) {
-        int *hdr_out = reinterpret_cast<int *>(
-            smem + kGqaRedOff + buf * kGqaRedBufBytes +
-            kGqaConsumerWarps * kGqaRedWarpFloats * 4);
-        hdr_out[1] = kDone;
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&red_full[buf]);
-      break;
-    }
-    if (hd.g != cur_g) {
-      cur_g = hd.g;
-      const GqaSegment sg = gqa_segment(a, cur_g, nseg, n_hc, group);
-      app_row = a.k_new ? appended_row(a, sg.b) : -1;
-      if (app_row >= 0)
-        app_val = load_new_row(a, sg.b * a.H_kv + (cur_g - sg.b * nseg) / n_hc);
-      const uint32_t *q0 =
-          quad < sg.hv
-              ? reinterpret_cast<const uint32_t *>(
-                    a.q + (static_cast<size_t>(sg.b) * a.H + sg.h0 + quad) * kHeadDim)
-              : nullptr;
-      const uint32_t *q1 =
-          quad + 8 < sg.hv
-              ? reinterpret_cast<const uint32_t *>(
-                    a.q + (static_cast<size_t>(sg.b) * a.H + sg.h0 + quad + 8) * kHeadDim)
-              : nullptr;
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        qa[kk][0] = q0 ? q0[8 * kk + qid] : 0u;
-        qa[kk][1] = q1 ? q1[8 * kk + qid] : 0u;
-        qa[kk][2] = q0 ? q0[8 * kk + 4 + qid] : 0u;
-        qa[kk][3] = q1 ? q1[8 * kk + 4 + qid] : 0u;
-      }
-    }
-
-    if (app_row >= 0) {
-      const int local = app_row - hd.r0;
-      if (local >= key0 && local < key0 + 16 && local < hd.n) {
-        const int b = hd.g / nseg;
-        const int s_in_b = hd.g - b * nseg;
-        patch_new_row<true>(a, b * a.H_kv + s_in_b / n_hc, app_row, local,
-                            smem + kGqaKOff + slot * kStageBytes,
-                            smem + kGqaVOff + slot * kStageBytes,
-                            s_in_b % n_hc == 0, app_val);
-      }
-    }
-    if (key0 < hd.n) {  // warp-uniform
-      const uint32_t kb = smem_u32(smem + kGqaKOff + slot * kStageBytes);
-      const uint32_t vb = smem_u32(smem + kGqaVOff + slot * kStageBytes);
-      // S = Q K^T for keys key0 + 8j + [0, 8)
-      float sc[2][4];
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) sc[j][e] = 0.f;
-        const int row = key0 + 8 * j + (lane & 7);
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          const int chunk = 4 * half + (lane >> 3);
-          uint32_t kf[4];
-          ldsm_x4(kb + row * kRowBytes + ((chunk ^ (row & 7)) << 4), kf);
-          mma_16816(sc[j], qa[2 * half], kf[0], kf[1]);
-          mma_16816(sc[j], qa[2 * half + 1], kf[2], kf[3]);
-        }
-      }
-      // online softmax per head row (rows quad and quad + 8)
-      const int n_here = hd.n - key0;
-      float x[2][4];
-#pragma unroll
-      for (int j = 0; j < 2; ++j)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int key = 8 * j + 2 * qid + (e & 1);
-          x[j][e] = key < n_here ? sc[j][e] * a.scale_log2 : -INFINITY;
-        }
-      float mx0 = fmaxf(fmaxf(x[0][0], x[0][1]), fmaxf(x[1][0], x[1][1]));
-      float mx1 = fmaxf(fmaxf(x[0][2], x[0][3]), fmaxf(x[1][2], x[1][3]));
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-      const float mn0 = fmaxf(m_r[0], mx0);
-      const float mn1 = fmaxf(m_r[1], mx1);
-      const float corr0 = fast_exp2(m_r[0] - mn0);
-      const float corr1 = fast_exp2(m_r[1] - mn1);
-      m_r[0] = mn0;
-      m_r[1] = mn1;
-      float p[2][4];
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        p[j][0] = fast_exp2(x[j][0] - mn0);
-        p[j][1] = fast_exp2(x[j][1] - mn0);
-        p[j][2] = fast_exp2(x[j][2] - mn1);
-        p[j][3] = fast_exp2(x[j][3] - mn1);
-      }
-      l_r[0] = fmaf(l_r[0], corr0, (p[0][0] + p[0][1]) + (p[1][0] + p[1][1]));
-      l_r[1] = fmaf(l_r[1], corr1, (p[0][2] + p[0][3]) + (p[1][2] + p[1][3]));
-#pragma unroll
-      for (int dt = 0; dt < 8; ++dt) {
-        o[dt][0] *= corr0;
-        o[dt][1] *= corr0;
-        o[dt][2] *= corr1;
-        o[dt][3] *= corr1;
-      }
-      // P as the A operand: k index = key within the 16 (C -> A layout)
-      const uint32_t pa[4] = {pack_half2(p[0][0], p[0][1]),
-                              pack_half2(p[0][2], p[0][3]),
-                              pack_half2(p[1][0], p[1][1]),
-                              pack_half2(p[1][2], p[1][3])};
-      // O += P V over dims 8dt..8dt+8, V read transposed
-      const int vrow = key0 + 8 * ((lane >> 3) & 1) + (lane & 7);
-#pragma unroll
-      for (int dp = 0; dp < 4; ++dp) {
-        const int chunk = 2 * dp + (lane >> 4);
-        uint32_t vf[4];
-        ldsm_x4_trans(vb + vrow * kRowBytes + ((chunk ^ (vrow & 7)) << 4), vf);
-        mma_16816(o[2 * dp], pa, vf[0], vf[1]);
-        mma_16816(o[2 * dp + 1], pa, vf[2], vf[3]);
-      }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[slot]);
-
-    if (!(hd.flags & kLast)) continue;
-
-    // ---- piece complete: per head row (m, l, O) of this warp to the merger
-    float l0 = l_r[0], l1 = l_r[1];
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-    const int buf = piece & 1;
-    if (piece >= kRedBufs &&
-        !mbar_wait(&red_empty[buf], ((piece >> 1) - 1) & 1))
-      break;
-    float *red = reinterpret_cast<float *>(smem + kGqaRedOff + buf * kGqaRedBufBytes);
-    float *r0p = red + warp * kGqaRedWarpFloats + quad * kPartialFloats;
-    float *r1p = r0p + 8 * kPartialFloats;
-#pragma unroll
-    for (int dt = 0; dt < 8; ++dt) {
-      *reinterpret_cast<float2 *>(r0p + 4 + 8 * dt + 2 * qid) =
-          make_float2(o[dt][0], o[dt][1]);
-      *reinterpret_cast<float2 *>(r1p + 4 + 8 * dt + 2 * qid) =
-          make_float2(o[dt][2], o[dt][3]);
-    }
-    if (qid == 0) {
-      r0p[0] = m_r[0];
-      r0p[1] = l0;
-      r1p[0] = m_r[1];
-      r1p[1] = l1;
-    }
-    if (warp == 0 && lane == 0) {
-      int *hdr_out = reinterpret_cast<int *>(red + kGqaConsumerWarps * kGqaRedWarpFloats);
-      hdr_out[0] = hd.g;
-      hdr_out[1] = hd.flags;
-      hdr_out[2] = hd.c0;
-      hdr_out[3] = hd.c1;
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&red_full[buf]);
-    ++piece;
-    reset();
-  }
-}
-
-__global__ void __launch_bounds__(kGqaThreads, 1)
-    decode_gqa_kernel(const DecodeArgs a,
-                      const __grid_constant__ CUtensorMap tm_k,
-                      const __grid_constant__ CUtensorMap tm_v) {
-  extern __shared__ __align__(1024) uint8_t smem[];
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + kGqaBarOff);
-  uint64_t *empty = full + kGqaStages;
-  uint64_t *red_full = empty + kGqaStages;
-  uint64_t *red_empty = red_full + kRedBufs;
-  StageHeader *hdr = reinterpret_cast<StageHeader *>(smem + kGqaHdrOff);
-  if (device_failed()) return;
-  if (smem_u32(smem) & 1023u) {  // the swizzled stages need 1 KiB alignment
-    if (threadIdx.x == 0) record_error(FA_ERR_SMEM_ALIGN);
-    return;
-  }
-  const int group = a.H / a.H_kv;
-  const int n_hc = (group + kGqaMaxHeads - 1) / kGqaMaxHeads;
-  const int nseg = a.H_kv * n_hc;
-
-  GqaPending *pend = reinterpret_cast<GqaPending *>(smem + kGqaPendOff);
-  if (threadIdx.x == 0) {
-    pend->count = 0;
-    for (int s = 0; s < kGqaStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kGqaConsumerWarps);
-    }
-    for (int r = 0; r < kRedBufs; ++r) {
-      mbar_init(&red_full[r], kGqaConsumerWarps);
-      mbar_init(&red_empty[r], 1);
-    }
-    fence_barrier_init();
-  }
-  __syncthreads();
-
-  if (warp == kGqaConsumerWarps) {
-    if (lane == 0) {
-      prefetch_tensormap(&tm_k);
-      prefetch_tensormap(&tm_v);
-    }
-    produce<true, kGqaStages>(a, nseg, n_hc, smem, kGqaKOff, kGqaVOff, full,
-                              empty, hdr, &tm_k, &tm_v);
-  } else if (warp == kGqaConsumerWarps + 1) {
-    merger_gqa(a, nseg, n_hc, group, smem + kGqaRedOff, red_full, red_empty,
-               pend);
-  } else {
-    gqa_consume(a, nseg, n_hc, group, smem, full, empty, red_full, red_empty,
-                hdr);
-  }
-  // Streaming is over for every warp (the stage and hand-off buffers are
-  // free): the whole CTA merges the segments it arrived on last.
-  __syncthreads();
-  const int hs = group < kGqaMaxHeads ? group : kGqaMaxHeads;
-  // everything below the barriers is free now: gather area + stats
-  float *stats = reinterpret_cast<float *>(smem + kGqaBarOff) - 3 * kGqaMaxHeads;
-  uint8_t *gather = smem;
-  const uint32_t gather_bytes = kGqaBarOff - 3 * kGqaMaxHeads * 4;
-  uint64_t *gbar = red_empty + kRedBufs;
-  if (threadIdx.x == 0) {
-    mbar_init(gbar, 1);
-    fence_barrier_init();
-  }
-  __syncthreads();
-  uint32_t gphase = 0;
-  for (int k = 0; k < pend->count; ++k) {
-    const GqaSegment sg = gqa_segment(a, pend->g[k], nseg, n_hc, group);
-    coop_merge(a, pend->g[k], pend->c0[k], pend->c1[k], sg, hs, gather,
-               gather_bytes, stats, gbar, gphase);
-  }
-}
-
-
 }  // namespace decode
 
 const void *decode_kernel_ptr() {
@@ -1338,21 +780,6 @@ int decode_min_rows_per_cta() { return decode::kMinRowsPerCta; }
 cudaError_t launch_decode_kernel(const DecodeArgs &args, cudaStream_t stream) {
   decode::decode_kernel<<<args.grid, decode::kThreads, decode::kSmemBytes,
                           stream>>>(args);
-  return cudaGetLastError();
-}
-
-const void *decode_gqa_kernel_ptr() {
-  return reinterpret_cast<const void *>(decode::decode_gqa_kernel);
-}
-int decode_gqa_smem_bytes() { return static_cast<int>(decode::kGqaSmemBytes); }
-int decode_gqa_max_heads() { return decode::kGqaMaxHeads; }
-
-cudaError_t launch_decode_gqa_kernel(const DecodeArgs &args,
-                                     const CUtensorMap &tm_k,
-                                     const CUtensorMap &tm_v,
-                                     cudaStream_t stream) {
-  decode::decode_gqa_kernel<<<args.grid, decode::kGqaThreads,
-                              decode::kGqaSmemBytes, stream>>>(args, tm_k, tm_v);
   return cudaGetLastError();
 }
 

@@ -4,6 +4,7 @@
 #include "capi.cu"
 #include "decode_sm100.cu"
 #include "decode_d128_sm100.cu"
+#include "decode_gqa_sm100.cu"
 #include "prefill_sm100.cu"
 #include "prefill_d128_sm100.cu"
 #include "legacy_sm100.cu"

@@ -72,12 +72,15 @@ cudaError_t launch_decode_kernel(const DecodeArgs &args, cudaStream_t stream);
 // Grouped-query decode: K/V read once per group of query heads. The grid is
 // one CTA per SM at most; segments are (b, K/V head, chunk of up to
 // decode_gqa_max_heads() query heads).
-const void *decode_gqa_kernel_ptr();
-int decode_gqa_smem_bytes();
+// (decode_gqa_sm100.cu) head_dim 64 or 128; K/V TMA boxes of
+// decode_gqa_box_rows(head_dim) rows; partials of 4 + head_dim floats.
+const void *decode_gqa_kernel_ptr(int head_dim);
+int decode_gqa_smem_bytes(int head_dim);
 int decode_gqa_max_heads();
+int decode_gqa_box_rows(int head_dim);
 cudaError_t launch_decode_gqa_kernel(const DecodeArgs &args,
                                      const CUtensorMap &tm_k,
-                                     const CUtensorMap &tm_v,
+                                     const CUtensorMap &tm_v, int head_dim,
                                      cudaStream_t stream);
 
 // head_dim 128 per-head decode (decode_d128_sm100.cu); partials are

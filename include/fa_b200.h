@@ -158,6 +158,21 @@ int fa_decode_exchange(const void *q, const void *k_cache, const void *v_cache,
                        int rank, int world, uint32_t epoch, void *stream);
 
 /*
+ * Grouped-query decode for head_dim 64 or 128 (64: as fa_decode_gqa); K/V
+ * heads dividing the query heads, every K/V row read once per group;
+ * workspace of fa_decode_gqa_hd_workspace_bytes() bytes. No reference
+ * counterpart (kernel-side GQA and d = 128 are both the reference's named
+ * next steps).
+ */
+size_t fa_decode_gqa_hd_workspace_bytes(int B, int H, int H_kv, int S_max,
+                                        int head_dim, int device);
+int fa_decode_gqa_hd(const void *q, const void *k_cache, const void *v_cache,
+                     const int32_t *seq_lens, void *o, int B, int H, int H_kv,
+                     int S_max, int head_dim, float scale, void *workspace,
+                     size_t workspace_bytes, uint32_t *counters,
+                     size_t counter_count, void *stream);
+
+/*
  * Decode with the KV-cache append fused in: for every sequence b the new
  * token's k_new / v_new rows (B, H_kv, 1, 64) fp16 are stored at row
  * p = max(seq_lens[b], 0) of k_cache / v_cache (B, H_kv, S_max, 64) and the

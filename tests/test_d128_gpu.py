@@ -126,11 +126,43 @@ def test_decode_d128_split_invariance(split):
     assert (auto.float() - forced.float()).abs().max().item() <= 1e-3
 
 
+@pytest.mark.parametrize("h,h_kv", [(32, 8), (14, 2), (40, 2), (8, 1)])
+def test_decode_d128_grouped_matches_fp32(h, h_kv):
+    """Grouped decode at head_dim 128 (e.g. 32 query heads on 8 K/V heads):
+    every K/V row read once per group, groups above 16 in two passes."""
+    torch.manual_seed(h + h_kv)
+    b, s = 5, 2500
+    q = torch.randn(b, h, 1, 128, device="cuda").half()
+    k, v = (torch.randn(b, h_kv, s, 128, device="cuda").half() for _ in range(2))
+    lens = torch.tensor([2500, 1, 0, 1311, 9999], dtype=torch.int32, device="cuda")
+    scale = 128 ** -0.5
+    for _ in range(2):
+        got = flashattn_cuda.decode(q, k, v, lens, scale)
+        kk = k.repeat_interleave(h // h_kv, dim=1)
+        vv = v.repeat_interleave(h // h_kv, dim=1)
+        want = decode_reference(q, kk, vv, lens, scale)
+        assert (got.float() - want).abs().max().item() <= 2e-3
+    assert torch.all(got[2] == 0)
+    assert flashattn_cuda.take_device_error() == 0
+
+
+def test_decode_d128_grouped_long_sequence():
+    torch.manual_seed(23)
+    q = torch.randn(1, 32, 1, 128, device="cuda").half()
+    k, v = (torch.randn(1, 8, 50000, 128, device="cuda").half() for _ in range(2))
+    lens = torch.tensor([49999], dtype=torch.int32, device="cuda")
+    got = flashattn_cuda.decode(q, k, v, lens, 0.088)
+    want = decode_reference(q, k.repeat_interleave(4, 1), v.repeat_interleave(4, 1),
+                            lens, 0.088)
+    assert (got.float() - want).abs().max().item() <= 2e-3
+
+
 def test_decode_d128_limits():
     q = torch.randn(1, 4, 1, 128, device="cuda").half()
     k = torch.randn(1, 2, 16, 128, device="cuda").half()
     lens = torch.tensor([4], dtype=torch.int32, device="cuda")
     with pytest.raises(RuntimeError, match="head_dim"):
-        flashattn_cuda.decode(q, k, k, lens, 0.1)
-    with pytest.raises(RuntimeError, match="head_dim"):
         flashattn_cuda.decode(q[..., :64].contiguous(), k, k, lens, 0.1)
+    with pytest.raises(RuntimeError, match="head_dim"):
+        flashattn_cuda.decode_append(q, k[:, :, :1].contiguous(),
+                                     k[:, :, :1].contiguous(), k, k.clone(), lens, 0.1)
