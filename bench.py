@@ -588,9 +588,9 @@ def cpu_baseline(budget_s):
     flops = prefill_flops(1, heads, C3["N"], True)
     return {"value": round(flops / secs / 1e12, 5), "unit": "TFLOP/s",
             "cores": cpu_threads(), "kind": "port",
-            "sample": f"{heads} of the 56 (batch, head) causal N=4096 heads of "
-                      f"config 3 through the numpy restatement of "
-                      f"src/attention_cpu.py ({secs:.1f} s)"}
+            "sample": f"{heads} causal N=4096 (batch, head) evaluations, cycling "
+                      f"over config 3's 56 heads, through the numpy restatement "
+                      f"of src/attention_cpu.py ({secs:.1f} s)"}
 
 
 def run_reference(args, rank, world):
