@@ -260,12 +260,11 @@ at::Tensor decode_append(const at::Tensor &q, const at::Tensor &k_new,
                          at::Tensor v_cache, const at::Tensor &seq_lens,
                          double scale) {
   check_decode_inputs(q, k_cache, v_cache, seq_lens, scale);
-  TORCH_CHECK(q.size(3) == kHeadDim, "decode_append needs head_dim == ",
-              kHeadDim);
-  check_bhnd(k_new, "k_new");
-  check_bhnd(v_new, "v_new");
+  check_bhnd_any(k_new, "k_new");
+  check_bhnd_any(v_new, "v_new");
   TORCH_CHECK(k_new.sizes() == v_new.sizes() && k_new.size(0) == k_cache.size(0) &&
-                  k_new.size(1) == k_cache.size(1) && k_new.size(2) == 1,
+                  k_new.size(1) == k_cache.size(1) && k_new.size(2) == 1 &&
+                  k_new.size(3) == k_cache.size(3),
               "k_new and v_new must be (B, H_kv, 1, 64) matching the caches, got ",
               k_new.sizes(), " and ", v_new.sizes());
   TORCH_CHECK(k_new.device() == q.device() && v_new.device() == q.device(),
@@ -276,15 +275,16 @@ at::Tensor decode_append(const at::Tensor &q, const at::Tensor &k_new,
   const int H_kv = to_int(k_cache.size(1), "kv heads");
   const int S = to_int(k_cache.size(2), "cache length");
   at::Tensor o = at::empty_like(q);
+  const int D = to_int(q.size(3), "head_dim");
   const size_t bytes =
-      fa_decode_gqa_workspace_bytes(B, H, H_kv, S, q.get_device());
+      fa_decode_gqa_hd_workspace_bytes(B, H, H_kv, S, D, q.get_device());
   TORCH_CHECK(bytes > 0, "fa_decode_gqa_workspace_bytes failed");
   DecodeScratch &ws = decode_scratch(q, bytes, static_cast<size_t>(B) * H);
   check_status(
-      fa_decode_append(q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(),
+      fa_decode_append_hd(q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(),
                        k_cache.data_ptr(), v_cache.data_ptr(),
                        seq_lens.data_ptr<int32_t>(), o.data_ptr(), B, H, H_kv,
-                       S, static_cast<float>(scale), ws.partials.data_ptr(),
+                       S, D, static_cast<float>(scale), ws.partials.data_ptr(),
                        static_cast<size_t>(ws.partials.numel()),
                        reinterpret_cast<uint32_t *>(ws.counters.data_ptr<int32_t>()),
                        static_cast<size_t>(ws.counters.numel()), current_stream()),

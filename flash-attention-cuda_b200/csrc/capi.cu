@@ -214,8 +214,8 @@ int run_decode_gqa(const void *q, const void *k_cache, const void *v_cache,
                    float *const *x_peers = nullptr, int x_rank = 0,
                    int x_world = 1, uint32_t x_epoch = 0,
                    int head_dim = FA_HEAD_DIM) {
-  if (head_dim != FA_HEAD_DIM && (head_dim != 128 || H_kv == H || k_new ||
-                                  x_peers || partial_out || split_size > 0))
+  if (head_dim != FA_HEAD_DIM && (head_dim != 128 || H_kv == H || x_peers ||
+                                  partial_out || split_size > 0))
     return FA_EINVAL;
   if (!decode_shape_ok(B, H, S_max, scale)) return FA_EINVAL;
   if (H_kv <= 0 || H % H_kv != 0) return FA_EINVAL;
@@ -444,16 +444,15 @@ size_t fa_decode_hd_workspace_bytes(int B, int H, int S_max, int head_dim,
          sizeof(float);
 }
 
-int fa_decode_hd(const void *q, const void *k_cache, const void *v_cache,
-                 const int32_t *seq_lens, void *o, int B, int H, int S_max,
-                 int head_dim, float scale, int split_size, void *workspace,
-                 size_t workspace_bytes, uint32_t *counters,
-                 size_t counter_count, void *stream) {
-  if (head_dim == FA_HEAD_DIM)
-    return fa_decode(q, k_cache, v_cache, seq_lens, o, B, H, S_max, scale,
-                     split_size, workspace, workspace_bytes, counters,
-                     counter_count, stream);
-  if (head_dim != 128) return FA_EINVAL;
+namespace fa {
+namespace {
+// head_dim 128, one K/V head per query head (optionally with the append).
+int run_decode_d128(const void *q, const void *k_cache, const void *v_cache,
+                    const int32_t *seq_lens, void *o, int B, int H, int S_max,
+                    float scale, int split_size, void *workspace,
+                    size_t workspace_bytes, uint32_t *counters,
+                    size_t counter_count, void *stream, const void *k_new,
+                    const void *v_new) {
   if (!decode_shape_ok(B, H, S_max, scale)) return FA_EINVAL;
   if (split_size > 0 && split_size % 4 != 0) return FA_EINVAL;
   if (!q || !k_cache || !v_cache || !seq_lens || !o || !workspace || !counters)
@@ -471,11 +470,13 @@ int fa_decode_hd(const void *q, const void *k_cache, const void *v_cache,
                             decode_d128_partial_floats() * sizeof(float) ||
       counter_count < static_cast<size_t>(B) * H)
     return FA_ENOSPACE;
+  if ((k_new == nullptr) != (v_new == nullptr)) return FA_EINVAL;
+  if (k_new && (!aligned16(k_new) || !aligned16(v_new))) return FA_EALIGN;
   DecodeArgs a{};
-  a.k_new = nullptr;
-  a.v_new = nullptr;
-  a.k_cache_w = nullptr;
-  a.v_cache_w = nullptr;
+  a.k_new = static_cast<const __half *>(k_new);
+  a.v_new = static_cast<const __half *>(v_new);
+  a.k_cache_w = k_new ? static_cast<__half *>(const_cast<void *>(k_cache)) : nullptr;
+  a.v_cache_w = k_new ? static_cast<__half *>(const_cast<void *>(v_cache)) : nullptr;
   a.q = static_cast<const __half *>(q);
   a.k = static_cast<const __half *>(k_cache);
   a.v = static_cast<const __half *>(v_cache);
@@ -495,6 +496,45 @@ int fa_decode_hd(const void *q, const void *k_cache, const void *v_cache,
                  cudaSuccess
              ? FA_OK
              : FA_ECUDA;
+}
+}  // namespace
+}  // namespace fa
+
+int fa_decode_hd(const void *q, const void *k_cache, const void *v_cache,
+                 const int32_t *seq_lens, void *o, int B, int H, int S_max,
+                 int head_dim, float scale, int split_size, void *workspace,
+                 size_t workspace_bytes, uint32_t *counters,
+                 size_t counter_count, void *stream) {
+  if (head_dim == FA_HEAD_DIM)
+    return fa_decode(q, k_cache, v_cache, seq_lens, o, B, H, S_max, scale,
+                     split_size, workspace, workspace_bytes, counters,
+                     counter_count, stream);
+  if (head_dim != 128) return FA_EINVAL;
+  return run_decode_d128(q, k_cache, v_cache, seq_lens, o, B, H, S_max, scale,
+                         split_size, workspace, workspace_bytes, counters,
+                         counter_count, stream, nullptr, nullptr);
+}
+
+int fa_decode_append_hd(const void *q, const void *k_new, const void *v_new,
+                        void *k_cache, void *v_cache, const int32_t *seq_lens,
+                        void *o, int B, int H, int H_kv, int S_max,
+                        int head_dim, float scale, void *workspace,
+                        size_t workspace_bytes, uint32_t *counters,
+                        size_t counter_count, void *stream) {
+  if (!o || !k_new || !v_new) return FA_EINVAL;
+  if (head_dim == FA_HEAD_DIM)
+    return fa_decode_append(q, k_new, v_new, k_cache, v_cache, seq_lens, o, B,
+                            H, H_kv, S_max, scale, workspace, workspace_bytes,
+                            counters, counter_count, stream);
+  if (head_dim != 128) return FA_EINVAL;
+  if (H_kv == H)
+    return run_decode_d128(q, k_cache, v_cache, seq_lens, o, B, H, S_max,
+                           scale, 0, workspace, workspace_bytes, counters,
+                           counter_count, stream, k_new, v_new);
+  return run_decode_gqa(q, k_cache, v_cache, seq_lens, o, nullptr, B, H, H_kv,
+                        S_max, scale, 0, workspace, workspace_bytes, counters,
+                        counter_count, stream, k_new, v_new, nullptr, 0, 1, 0,
+                        128);
 }
 
 size_t fa_decode_gqa_hd_workspace_bytes(int B, int H, int H_kv, int S_max,

@@ -216,6 +216,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   const int sub = lane % kLanesPerRow;  // head dims [8*sub, 8*sub + 8)
   float qf[8];
   int cur_g = -1;
+  int app_row = -1;  // segment row of the appended token, -1 for none
+  uint4 app_val = make_uint4(0, 0, 0, 0);
   float m_run = kNegBig, l_run = 0.f;
   int piece = 0;
   float acc[8];
@@ -242,6 +244,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     }
     if (hd.g != cur_g) {
       cur_g = hd.g;
+      if (a.k_new) {
+        app_row = decode::appended_row(a, cur_g / a.H);
+        if (app_row >= 0) app_val = decode::load_new_row<kD>(a, cur_g);
+      }
       const uint4 qv = *reinterpret_cast<const uint4 *>(
           a.q + static_cast<size_t>(cur_g) * kD + sub * 8);
       const __half2 *qh = reinterpret_cast<const __half2 *>(&qv);
@@ -253,6 +259,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       }
     }
 
+    if (app_row >= 0) {  // fused append: the owner warp patches and stores
+      const int local = app_row - hd.r0;
+      if (local >= 0 && local < hd.n && warp == local / kRowsPerWarp)
+        decode::patch_new_row<false, kD, kStageRows>(
+            a, hd.g, app_row, local, smem + kKOff + slot * kStageBytes,
+            smem + kVOff + slot * kStageBytes, true, app_val);
+    }
     const uint32_t kb = smem_u32(smem + kKOff + slot * kStageBytes);
     const uint32_t vb = smem_u32(smem + kVOff + slot * kStageBytes);
     const int row_base = warp * kRowsPerWarp + grp;

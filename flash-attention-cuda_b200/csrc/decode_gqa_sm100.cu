@@ -406,11 +406,9 @@ __device__ __forceinline__ void gqa_consume(
     if (hd.g != cur_g) {
       cur_g = hd.g;
       const GqaSegment sg = gqa_segment(cur_g, nseg, n_hc, group);
-      if (D == kHeadDim) {
-        app_row = a.k_new ? appended_row(a, sg.b) : -1;
-        if (app_row >= 0)
-          app_val = load_new_row(a, sg.b * a.H_kv + (cur_g - sg.b * nseg) / n_hc);
-      }
+      app_row = a.k_new ? appended_row(a, sg.b) : -1;
+      if (app_row >= 0)
+        app_val = load_new_row<D>(a, sg.b * a.H_kv + (cur_g - sg.b * nseg) / n_hc);
       const uint32_t *q0 =
           quad < sg.hv
               ? reinterpret_cast<const uint32_t *>(
@@ -430,12 +428,12 @@ __device__ __forceinline__ void gqa_consume(
       }
     }
 
-    if (D == kHeadDim && app_row >= 0) {
+    if (app_row >= 0) {
       const int local = app_row - hd.r0;
       if (local >= key0 && local < key0 + 16 && local < hd.n) {
         const int b = hd.g / nseg;
         const int s_in_b = hd.g - b * nseg;
-        patch_new_row<true>(a, b * a.H_kv + s_in_b / n_hc, app_row, local,
+        patch_new_row<true, D, C::kRows>(a, b * a.H_kv + s_in_b / n_hc, app_row, local,
                             smem + C::kKOff + slot * kStageBytes,
                             smem + C::kVOff + slot * kStageBytes,
                             s_in_b % n_hc == 0, app_val);

@@ -104,34 +104,41 @@ __device__ __forceinline__ int appended_row(const DecodeArgs &a, int b) {
 // The appended token's 16-byte chunk held by this lane (lanes 0-7: K,
 // 8-15: V; other lanes get zeros), loaded when a segment starts so the load
 // overlaps the query load.
+template <int D = kHeadDim>
 __device__ __forceinline__ uint4 load_new_row(const DecodeArgs &a, int g_kv) {
+  constexpr int kChunks = D / 8;  // 16-byte chunks per row
   const int lane = threadIdx.x & 31;
-  if (lane >= 16) return make_uint4(0, 0, 0, 0);
+  if (lane >= 2 * kChunks) return make_uint4(0, 0, 0, 0);
   const __half *src =
-      (lane >= 8 ? a.v_new : a.k_new) + static_cast<size_t>(g_kv) * kHeadDim;
-  return reinterpret_cast<const uint4 *>(src)[lane & 7];
+      (lane >= kChunks ? a.v_new : a.k_new) + static_cast<size_t>(g_kv) * D;
+  return reinterpret_cast<const uint4 *>(src)[lane % kChunks];
 }
 
 // Fused append, run by the warp that owns stage row `local` of plane g_kv:
 // the new K/V row (val from load_new_row) replaces the stale cache row in
-// shared memory (16-byte chunk c of a row sits at chunk c ^ (row & 7) when
-// the stage is swizzled) and, when `store` is set, is written to the cache.
-template <bool kSwizzled>
+// shared memory and, when `store` is set, is written to the cache. Swizzled
+// stages hold 64-dim blocks of kRows x 128 B with 16-byte chunk c of a row
+// at chunk c ^ (row & 7); plain stages hold rows of 2 D bytes.
+template <bool kSwizzled, int D = kHeadDim, int kRows = kStageRows>
 __device__ __forceinline__ void patch_new_row(const DecodeArgs &a, int g_kv,
                                               int row_in_plane, int local,
                                               uint8_t *k_stage,
                                               uint8_t *v_stage, bool store,
                                               uint4 val) {
+  constexpr int kChunks = D / 8;
   const int lane = threadIdx.x & 31;
-  if (lane < 16) {
-    const int c = lane & 7;
-    const bool is_v = lane >= 8;
-    const int pc = kSwizzled ? (c ^ (local & 7)) : c;
+  if (lane < 2 * kChunks) {
+    const int c = lane % kChunks;
+    const bool is_v = lane >= kChunks;
+    const int off =
+        kSwizzled ? (c >> 3) * kRows * 128 + local * 128 +
+                        (((c & 7) ^ (local & 7)) << 4)
+                  : local * 2 * D + c * 16;
     uint8_t *stage = is_v ? v_stage : k_stage;
-    *reinterpret_cast<uint4 *>(stage + local * kRowBytes + pc * 16) = val;
+    *reinterpret_cast<uint4 *>(stage + off) = val;
     if (store) {
       __half *dst = (is_v ? a.v_cache_w : a.k_cache_w) +
-                    (static_cast<size_t>(g_kv) * a.S_max + row_in_plane) * kHeadDim;
+                    (static_cast<size_t>(g_kv) * a.S_max + row_in_plane) * D;
       reinterpret_cast<uint4 *>(dst)[c] = val;
     }
   }

@@ -191,6 +191,18 @@ int fa_decode_append(const void *q, const void *k_new, const void *v_new,
                      uint32_t *counters, size_t counter_count, void *stream);
 
 /*
+ * fa_decode_append for head_dim 64 (same as fa_decode_append) or 128 (k_new,
+ * v_new (B, H_kv, 1, 128), caches (B, H_kv, S_max, 128)); workspace of
+ * fa_decode_gqa_hd_workspace_bytes(B, H, H_kv, S_max, head_dim) bytes.
+ */
+int fa_decode_append_hd(const void *q, const void *k_new, const void *v_new,
+                        void *k_cache, void *v_cache, const int32_t *seq_lens,
+                        void *o, int B, int H, int H_kv, int S_max,
+                        int head_dim, float scale, void *workspace,
+                        size_t workspace_bytes, uint32_t *counters,
+                        size_t counter_count, void *stream);
+
+/*
  * Grouped-query decode: q, o (B, H, 1, 64); caches (B, H_kv, S_max, 64) with
  * H % H_kv == 0 (query head h reads K/V head h / (H / H_kv)); automatic
  * schedule; workspace of fa_decode_gqa_workspace_bytes() bytes; counters as

@@ -16,7 +16,7 @@ pytestmark = [pytest.mark.gpu, requires_gpu]
 SCALE = 1.0 / math.sqrt(64)
 
 
-def append_reference(q, k_new, v_new, k, v, lens):
+def append_reference(q, k_new, v_new, k, v, lens, scale=SCALE):
     """Cache update and fp32 attention done separately."""
     k, v = k.clone(), v.clone()
     s_max = k.shape[2]
@@ -32,7 +32,7 @@ def append_reference(q, k_new, v_new, k, v, lens):
     for b, n in enumerate(new_lens):
         kk = k[b, :, :n].float().repeat_interleave(group, dim=0)
         vv = v[b, :, :n].float().repeat_interleave(group, dim=0)
-        out[b] = torch.softmax(q[b].float() @ kk.transpose(1, 2) * SCALE, -1) @ vv
+        out[b] = torch.softmax(q[b].float() @ kk.transpose(1, 2) * scale, -1) @ vv
     return out, k, v, torch.tensor(new_lens, dtype=torch.int32, device=q.device)
 
 
@@ -95,3 +95,24 @@ def test_decode_append_rejects_bad_shapes():
     with pytest.raises(RuntimeError, match="k_new and v_new"):
         flashattn_cuda.decode_append(q, k[:, :, :2].contiguous(), k[:, :, :2].contiguous(),
                                      k, k.clone(), lens, SCALE)
+
+
+@pytest.mark.parametrize("h,h_kv", [(8, 8), (32, 8), (20, 1)])
+def test_decode_append_head_dim_128(h, h_kv):
+    torch.manual_seed(31 + h)
+    b, s = 5, 900
+    scale = 128 ** -0.5
+    q = torch.randn(b, h, 1, 128, device="cuda").half()
+    k = torch.randn(b, h_kv, s, 128, device="cuda").half()
+    v = torch.randn(b, h_kv, s, 128, device="cuda").half()
+    k_new = torch.randn(b, h_kv, 1, 128, device="cuda").half()
+    v_new = torch.randn(b, h_kv, 1, 128, device="cuda").half()
+    lens = torch.tensor([0, 899, 900, 77, 450], dtype=torch.int32, device="cuda")
+    want, k_want, v_want, lens_after = append_reference(q, k_new, v_new, k, v,
+                                                        lens, scale)
+    k_c, v_c = k.clone(), v.clone()
+    got = flashattn_cuda.decode_append(q, k_new, v_new, k_c, v_c, lens, scale)
+    assert torch.equal(k_c, k_want) and torch.equal(v_c, v_want)
+    assert (got.float() - want).abs().max().item() <= 2e-3
+    assert torch.equal(got, flashattn_cuda.decode(q, k_c, v_c, lens_after, scale))
+    assert flashattn_cuda.take_device_error() == 0

@@ -163,6 +163,3 @@ def test_decode_d128_limits():
     lens = torch.tensor([4], dtype=torch.int32, device="cuda")
     with pytest.raises(RuntimeError, match="head_dim"):
         flashattn_cuda.decode(q[..., :64].contiguous(), k, k, lens, 0.1)
-    with pytest.raises(RuntimeError, match="head_dim"):
-        flashattn_cuda.decode_append(q, k[:, :, :1].contiguous(),
-                                     k[:, :, :1].contiguous(), k, k.clone(), lens, 0.1)
