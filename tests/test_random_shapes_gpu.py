@@ -1,0 +1,95 @@
+"""Seeded random configurations across the whole surface (prefill and
+decode, head_dim 64 and 128, grouped K/V heads, ragged lengths, fused
+append) against fp32 PyTorch attention at the north star's 2e-3 bound."""
+
+import random
+
+import pytest
+import torch
+
+from conftest import requires_gpu
+
+import flashattn_cuda
+
+pytestmark = [pytest.mark.gpu, requires_gpu]
+
+
+def sdpa(q, k, v, causal, scale):
+    group = q.shape[1] // k.shape[1]
+    return torch.nn.functional.scaled_dot_product_attention(
+        q.float(), k.float().repeat_interleave(group, 1),
+        v.float().repeat_interleave(group, 1), is_causal=causal, scale=scale)
+
+
+def decode_ref(q, k, v, lens, scale):
+    group = q.shape[1] // k.shape[1]
+    out = torch.zeros(q.shape, dtype=torch.float32, device=q.device)
+    for b, n in enumerate(lens.tolist()):
+        n = max(0, min(n, k.shape[2]))
+        if n:
+            kk = k[b, :, :n].float().repeat_interleave(group, 0)
+            vv = v[b, :, :n].float().repeat_interleave(group, 0)
+            out[b] = torch.softmax(q[b].float() @ kk.transpose(1, 2) * scale, -1) @ vv
+    return out
+
+
+def pick_heads(rng):
+    h_kv = rng.choice([1, 2, 3, 4, 8])
+    return h_kv * rng.choice([1, 1, 2, 3, 7, 17]), h_kv
+
+
+@pytest.mark.parametrize("seed", range(24))
+def test_random_prefill(seed):
+    rng = random.Random(seed)
+    d = rng.choice([64, 128])
+    b = rng.randint(1, 3)
+    h, h_kv = pick_heads(rng)
+    n = rng.choice([1, 2, 63, 64, 65, 127, 128, 129, 255, 300, 511, 700, 1024, 1500])
+    causal = rng.random() < 0.6
+    scale = d ** -0.5
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    q = torch.randn(b, h, n, d, device="cuda", generator=g).half()
+    k = torch.randn(b, h_kv, n, d, device="cuda", generator=g).half()
+    v = torch.randn(b, h_kv, n, d, device="cuda", generator=g).half()
+    got = flashattn_cuda.prefill(q, k, v, causal, scale)
+    err = (got.float() - sdpa(q, k, v, causal, scale)).abs().max().item()
+    assert err <= 2e-3, (d, b, h, h_kv, n, causal, err)
+    assert flashattn_cuda.take_device_error() == 0
+
+
+@pytest.mark.parametrize("seed", range(24))
+def test_random_decode(seed):
+    rng = random.Random(1000 + seed)
+    d = rng.choice([64, 128])
+    b = rng.randint(1, 9)
+    h, h_kv = pick_heads(rng)
+    s = rng.choice([1, 17, 128, 129, 1000, 4096, 9000])
+    scale = d ** -0.5
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    q = torch.randn(b, h, 1, d, device="cuda", generator=g).half()
+    k = torch.randn(b, h_kv, s, d, device="cuda", generator=g).half()
+    v = torch.randn(b, h_kv, s, d, device="cuda", generator=g).half()
+    lens = torch.tensor([rng.choice([0, 1, s, s + 5, rng.randint(0, s)])
+                         for _ in range(b)], dtype=torch.int32, device="cuda")
+    append = rng.random() < 0.4
+    if append:
+        kn = torch.randn(b, h_kv, 1, d, device="cuda", generator=g).half()
+        vn = torch.randn(b, h_kv, 1, d, device="cuda", generator=g).half()
+        k_ref, v_ref = k.clone(), v.clone()
+        lens_after = []
+        for i, n in enumerate(lens.tolist()):
+            p = max(n, 0)
+            if p < s:
+                k_ref[i, :, p] = kn[i, :, 0]
+                v_ref[i, :, p] = vn[i, :, 0]
+            lens_after.append(min(p + 1, s))
+        got = flashattn_cuda.decode_append(q, kn, vn, k, v, lens, scale)
+        assert torch.equal(k, k_ref) and torch.equal(v, v_ref)
+        want = decode_ref(q, k_ref, v_ref,
+                          torch.tensor(lens_after, dtype=torch.int32), scale)
+    else:
+        got = flashattn_cuda.decode(q, k, v, lens, scale)
+        want = decode_ref(q, k, v, lens.cpu(), scale)
+    err = (got.float() - want).abs().max().item()
+    assert err <= 2e-3, (d, b, h, h_kv, s, lens.tolist(), append, err)
+    assert flashattn_cuda.take_device_error() == 0
