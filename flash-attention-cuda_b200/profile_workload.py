@@ -35,6 +35,9 @@ CASES = {
     "decode_gqa_c5": ("decode", (1, 14, 131072), None, 2),
     "decode_gqa_b8": ("decode", (8, 32, 32768), None, 8),
     "decode_append_c4": ("decode_append", (64, 12, 8192), None, None),
+    # head_dim 128: config 4 per head, and 32 query heads on 8 K/V heads
+    "decode_d128_c4": ("decode_d128", (64, 12, 8192), None, None),
+    "decode_gqa_d128_b8": ("decode_d128", (8, 32, 32768), None, 8),
 }
 
 
@@ -52,8 +55,9 @@ def main():
                                dtype=torch.float16) for _ in range(3))
         fn = lambda: fa.prefill(q, k, v, causal, d ** -0.5)
     else:
-        q = torch.randn(b, h, 1, 64, generator=g, device="cuda", dtype=torch.float16)
-        k, v = (torch.randn(b, h_kv, n, 64, generator=g, device="cuda",
+        d = 128 if kind == "decode_d128" else 64
+        q = torch.randn(b, h, 1, d, generator=g, device="cuda", dtype=torch.float16)
+        k, v = (torch.randn(b, h_kv, n, d, generator=g, device="cuda",
                             dtype=torch.float16) for _ in range(2))
         cpu_gen = torch.Generator().manual_seed(0)
         if b > 1:
@@ -67,7 +71,7 @@ def main():
             lens = (lens - 1).contiguous()
             fn = lambda: fa.decode_append(q, kn, vn, k, v, lens, SCALE)
         else:
-            fn = lambda: fa.decode(q, k, v, lens, SCALE)
+            fn = lambda: fa.decode(q, k, v, lens, d ** -0.5)
     for _ in range(args.iters):
         fn()
     torch.cuda.synchronize()
