@@ -144,7 +144,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   // bit 0: causal; bit 1: zig-zag query-tile pairing
   const int zigzag = causal >> 1;
   causal &= 1;
-  if (device_failed()) return;
   if (smem_u32(smem) & 1023u) {
     if (threadIdx.x == 0) record_error(FA_ERR_SMEM_ALIGN);
     return;
@@ -168,7 +167,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile uint32_t *abort_flag =
       reinterpret_cast<volatile uint32_t *>(smem + kAbortOff);
 
-  if (threadIdx.x == 0) {
+  // The producer lane sets up the barriers and issues the Q tiles and the
+  // first kStages K/V tiles before the CTA-wide barrier, so their latency
+  // overlaps the TMEM allocation; the device error word (a global read) is
+  // checked after that and turns into the abort flag.
+  int preissued = 0;
+  if (warp == kProducerWarp && lane == 0) {
     mbar_init(&bars[kBarQFull], 1);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&bars[kBarKFull + s], 1);
@@ -181,8 +185,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars[kBarODone + t], 1);
     }
     mbar_init(&bars[kBarDrain], 1);
-    *abort_flag = 0;
     fence_barrier_init();
+    prefetch_tensormap(&tm_q);
+    prefetch_tensormap(&tm_k);
+    prefetch_tensormap(&tm_v);
+    const bool two = t1.n_kv > 0;
+    mbar_arrive_expect_tx(&bars[kBarQFull], (two ? 2 : 1) * kTileBytes);
+    tma_load_3d(smem + kQOff, &tm_q, &bars[kBarQFull], 0, t0.qt * kBlockM, bh);
+    if (two)
+      tma_load_3d(smem + kQOff + kTileBytes, &tm_q, &bars[kBarQFull], 0,
+                  t1.qt * kBlockM, bh);
+    for (; preissued < n_kv && preissued < kStages; ++preissued) {
+      const int s = preissued;
+      mbar_arrive_expect_tx(&bars[kBarKFull + s], 2 * kTileBytes);
+      tma_load_3d(smem + kKOff + s * kTileBytes, &tm_k, &bars[kBarKFull + s],
+                  0, preissued * kBlockN, kv_bh);
+      tma_load_3d(smem + kVOff + s * kTileBytes, &tm_v, &bars[kBarKFull + s],
+                  0, preissued * kBlockN, kv_bh);
+    }
+    *abort_flag = device_failed() ? 1u : 0u;
   }
   if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, kTmemCols);
@@ -204,18 +225,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------------ TMA
     if (lane == 0) {
-      prefetch_tensormap(&tm_q);
-      prefetch_tensormap(&tm_k);
-      prefetch_tensormap(&tm_v);
-      const bool two = t1.n_kv > 0;
-      mbar_arrive_expect_tx(&bars[kBarQFull], (two ? 2 : 1) * kTileBytes);
-      tma_load_3d(smem + kQOff, &tm_q, &bars[kBarQFull], 0, t0.qt * kBlockM,
-                  bh);
-      if (two)
-        tma_load_3d(smem + kQOff + kTileBytes, &tm_q, &bars[kBarQFull], 0,
-                    t1.qt * kBlockM, bh);
-      int issued = 0;
-      for (int j = 0; j < n_kv; ++j) {
+      int issued = preissued;
+      for (int j = preissued; j < n_kv; ++j) {
         if (*abort_flag) break;
         const int s = j % kStages;
         const int use = j / kStages;
