@@ -27,7 +27,7 @@ LIB_NAME = "libfa_b200.so"
 LIB_SOURCES = ["fa_all.cu", "capi.cu", "prefill_sm100.cu", "decode_sm100.cu",
                "prefill_d128_sm100.cu", "decode_d128_sm100.cu",
                "decode_gqa_sm100.cu",
-               "noalloc.cu", "legacy_sm100.cu", "fa_sm100.cuh", "fa_kernels.h"]
+               "noalloc.cu", "legacy_sm100.cu", "host_stage.cu", "fa_sm100.cuh", "fa_kernels.h"]
 
 
 def _nvcc():

@@ -168,6 +168,77 @@ at::Tensor prefill(const at::Tensor &q, const at::Tensor &k,
   return o;
 }
 
+// prefill_host(q, k, v, causal, scale, out=None, non_blocking=False): the
+// prefill() contract with q/k/v (and the result) in host memory, streamed
+// through the current CUDA device by fa_prefill_host. Page-locked inputs
+// let the copies overlap the kernels. The result is a page-locked CPU
+// tensor (or `out`); unless non_blocking, the call returns after the
+// current stream has finished it, like Tensor.cpu().
+at::Tensor prefill_host(const at::Tensor &q, const at::Tensor &k,
+                        const at::Tensor &v, bool causal, double scale,
+                        c10::optional<at::Tensor> out, bool non_blocking) {
+  for (const auto *t : {&q, &k, &v}) {
+    TORCH_CHECK(t->device().is_cpu(), "prefill_host expects CPU tensors");
+    check_half(*t, "q/k/v");
+    check_contiguous(*t, "q/k/v");
+    TORCH_CHECK(t->dim() == 4 && (t->size(3) == kHeadDim || t->size(3) == 128),
+                "q/k/v must be 4-D (B, H, N, 64 or 128), got ", t->sizes());
+  }
+  const bool same = q.sizes() == k.sizes() && q.sizes() == v.sizes();
+  const bool grouped = k.sizes() == v.sizes() && q.size(0) == k.size(0) &&
+                       q.size(2) == k.size(2) && q.size(3) == k.size(3) &&
+                       k.size(1) > 0 && q.size(1) % k.size(1) == 0;
+  TORCH_CHECK(same || grouped,
+              "prefill expects q, k and v to have identical shapes, got q=",
+              q.sizes(), " k=", k.sizes(), " v=", v.sizes());
+  TORCH_CHECK(q.size(2) > 0, "sequence length must be > 0");
+  TORCH_CHECK(std::isfinite(scale), "scale must be finite");
+  at::Tensor o;
+  if (out.has_value()) {
+    o = *out;
+    TORCH_CHECK(o.device().is_cpu() && o.scalar_type() == at::kHalf &&
+                    o.is_contiguous() && o.sizes() == q.sizes(),
+                "out must be a contiguous fp16 CPU tensor shaped like q");
+  } else {
+    o = at::empty(q.sizes(), q.options().pinned_memory(true));
+  }
+  const int B = to_int(q.size(0), "batch"), H = to_int(q.size(1), "heads");
+  const int H_kv = to_int(k.size(1), "kv heads");
+  const int N = to_int(q.size(2), "sequence length");
+  const int D = to_int(q.size(3), "head_dim");
+  int chunks = 0;
+  size_t ws_bytes = 0;
+  check_status(fa_prefill_host_plan(B, H, H_kv, N, D, &chunks, &ws_bytes),
+               "fa_prefill_host_plan");
+  const auto dev_opts = at::TensorOptions()
+                            .device(at::kCUDA, at::cuda::current_device())
+                            .dtype(at::kByte);
+  at::Tensor ws = at::empty({static_cast<int64_t>(ws_bytes)}, dev_opts);
+  check_status(fa_prefill_host(q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                               o.data_ptr(), B, H, H_kv, N, D, causal ? 1 : 0,
+                               static_cast<float>(scale), ws.data_ptr(),
+                               ws_bytes, current_stream()),
+               "fa_prefill_host");
+  if (!non_blocking) {
+    TORCH_CHECK(cudaStreamSynchronize(at::cuda::getCurrentCUDAStream()
+                                          .stream()) == cudaSuccess,
+                "prefill_host: stream synchronisation failed");
+  }
+  return o;
+}
+
+int64_t prefill_host_launches(int64_t B, int64_t H, int64_t H_kv, int64_t N,
+                              int64_t head_dim) {
+  int chunks = 0;
+  check_status(fa_prefill_host_plan(to_int(B, "batch"), to_int(H, "heads"),
+                                    to_int(H_kv, "kv heads"),
+                                    to_int(N, "sequence length"),
+                                    to_int(head_dim, "head_dim"), &chunks,
+                                    nullptr),
+               "fa_prefill_host_plan");
+  return chunks;
+}
+
 // decode / _decode_with_split: reference csrc/bindings.cpp:36-76,127-129.
 at::Tensor decode_impl(const at::Tensor &q, const at::Tensor &k_cache,
                        const at::Tensor &v_cache, const at::Tensor &seq_lens,
@@ -455,6 +526,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("prefill", &prefill,
         "Full-sequence attention (fp16 in/out, fp32 accum)", py::arg("q"),
         py::arg("k"), py::arg("v"), py::arg("causal"), py::arg("scale"));
+  m.def("prefill_host", &prefill_host,
+        "prefill() with host-memory q/k/v/out, copies overlapped with compute",
+        py::arg("q"), py::arg("k"), py::arg("v"), py::arg("causal"),
+        py::arg("scale"), py::arg("out") = py::none(),
+        py::arg("non_blocking") = false);
+  m.def("_prefill_host_launches", &prefill_host_launches);
   m.def("decode", &decode, "Single-query attention against a KV cache",
         py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
         py::arg("seq_lens"), py::arg("scale"));

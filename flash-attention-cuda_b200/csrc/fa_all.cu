@@ -9,3 +9,4 @@
 #include "prefill_d128_sm100.cu"
 #include "legacy_sm100.cu"
 #include "noalloc.cu"
+#include "host_stage.cu"

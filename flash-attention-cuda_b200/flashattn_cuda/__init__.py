@@ -24,11 +24,13 @@ from ._C import (  # noqa: F401
     merge_partials,
     occupancy_report,
     prefill,
+    prefill_host,
     take_device_error,
 )
 
 __all__ = [
     "prefill",
+    "prefill_host",
     "decode",
     "head_dim",
     "occupancy_report",

@@ -1,8 +1,9 @@
 /*
  * fa_b200.h — C ABI of the B200 (sm_100a) head_dim-64 fp16 attention forward.
  *
- * Every entry point takes plain device pointers, sizes and a cudaStream_t
- * passed as void*. No entry point allocates memory, synchronises the stream
+ * Every entry point takes plain device pointers (fa_prefill_host: host
+ * pointers for q/k/v/o), sizes and a cudaStream_t passed as void*. No entry
+ * point allocates memory, synchronises the stream
  * or touches a framework type; the Python package (flashattn_cuda._C) and any
  * other host language bind these symbols directly.
  *
@@ -71,6 +72,34 @@ int fa_prefill_gqa(const void *q, const void *k, const void *v, void *o, int B,
 int fa_prefill_hd(const void *q, const void *k, const void *v, void *o, int B,
                   int H, int H_kv, int N, int head_dim, int causal,
                   float scale, void *stream);
+
+/*
+ * Prefill with q, k, v and o in HOST memory (page-locked for the copies to
+ * overlap; pageable memory works but serialises them). Same shapes and
+ * result as fa_prefill_hd: every output element is bit-identical. The heads
+ * are streamed through device staging slots in chunks of whole
+ * (batch, K/V head) groups: the upload of chunk i+1, the kernel of chunk i
+ * and the download of chunk i-1 run at the same time on two internal copy
+ * streams and the caller's stream. The call only enqueues; o is complete
+ * once `stream` reaches the point of the call (synchronise it before reading
+ * o). workspace: device memory of at least fa_prefill_host_plan's
+ * workspace_bytes, 256-byte aligned, owned by the caller. The two copy
+ * streams and their events are created once per device on first use.
+ * Replaces the reference's host-to-device round trip around prefill()
+ * (tensors moved with .cuda() before csrc/bindings.cpp:10-27 and .cpu()
+ * after); no single reference entry point.
+ */
+int fa_prefill_host(const void *q, const void *k, const void *v, void *o,
+                    int B, int H, int H_kv, int N, int head_dim, int causal,
+                    float scale, void *workspace, size_t workspace_bytes,
+                    void *stream);
+
+/*
+ * Plan of fa_prefill_host for this shape: the number of chunks (one kernel
+ * launch each) and the device workspace it needs. Host-only.
+ */
+int fa_prefill_host_plan(int B, int H, int H_kv, int N, int head_dim,
+                         int *chunks, size_t *workspace_bytes);
 
 /*
  * Bytes of scratch memory fa_decode / fa_decode_partial need for this shape

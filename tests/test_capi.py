@@ -175,3 +175,51 @@ def test_exchange_buffer_size(lib):
         assert need <= n < need + 256 and n % 256 == 0
     assert lib.fa_exchange_bytes(1, 14, 0) == 0
     assert lib.fa_exchange_bytes(1, 14, 33) == 0
+
+
+def test_prefill_host_plan_and_validation(lib):
+    """fa_prefill_host_plan chunks whole (batch, K/V head) groups and sizes
+    the staging ring; fa_prefill_host rejects bad arguments before touching
+    a device."""
+    vp, ci = ctypes.c_void_p, ctypes.c_int
+    lib.fa_prefill_host_plan.argtypes = [ci] * 5 + [vp, vp]
+    lib.fa_prefill_host.argtypes = [vp] * 4 + [ci] * 6 + [
+        ctypes.c_float, vp, ctypes.c_size_t, vp]
+
+    def plan(B, H, H_kv, N, D):
+        c, w = ctypes.c_int(), ctypes.c_size_t()
+        rc = lib.fa_prefill_host_plan(B, H, H_kv, N, D, ctypes.byref(c),
+                                      ctypes.byref(w))
+        return rc, c.value, w.value
+
+    # config 3: 56 single-head groups, 3 chunks of 14 and the last 14 split
+    # in two; 3 staging slots of 14 * 4 * 512 KiB
+    assert plan(4, 14, 14, 4096, 64) == (FA_OK, 5, 3 * 14 * 4 * (512 << 10))
+    # grouped: 8 groups of 7 query heads + 1 K/V head, chunks of 2 groups
+    rc, chunks, ws = plan(4, 14, 2, 4096, 64)
+    assert (rc, chunks) == (FA_OK, 5) and ws == 3 * 2 * (7 * 2 + 2) * (512 << 10)
+    # tiny: a single chunk, a single slot
+    rc, chunks, ws = plan(1, 1, 1, 128, 64)
+    assert (rc, chunks) == (FA_OK, 1) and ws == 4 * 128 * 64 * 2
+    # ragged: 5 heads of 768 KiB input each at head_dim 128 make chunks of
+    # 3 heads (>= 2 MiB), the remaining 2 split in two
+    rc, chunks, _ = plan(1, 5, 5, 1024, 128)
+    assert (rc, chunks) == (FA_OK, 3)
+    # large: chunks are capped at 64 MiB of input (21 heads of 3 MiB here),
+    # so 12 chunks of 21 heads + the last 4 split in two, and the workspace
+    # stays bounded
+    rc, chunks, ws = plan(8, 32, 32, 8192, 64)
+    assert rc == FA_OK and chunks == 14 and ws == 3 * 21 * 4 * (1 << 20)
+    for bad in [(1, 2, 2, 16, 96), (0, 2, 2, 16, 64), (1, 6, 4, 16, 64),
+                (1, 2, 2, 0, 64)]:
+        assert plan(*bad)[0] == FA_EINVAL
+    p = ctypes.c_void_p(4096)
+    rc, _, ws = plan(1, 2, 2, 256, 64)
+    assert lib.fa_prefill_host(p, p, p, p, 1, 2, 2, 256, 64, 1, 0.1, p,
+                               ws - 1, None) == 4  # FA_ENOSPACE
+    assert lib.fa_prefill_host(p, p, p, p, 1, 2, 2, 256, 64, 1, 0.1,
+                               ctypes.c_void_p(4096 + 16), ws, None) == FA_EALIGN
+    assert lib.fa_prefill_host(p, None, p, p, 1, 2, 2, 256, 64, 1, 0.1, p,
+                               ws, None) == FA_EINVAL
+    assert lib.fa_prefill_host(p, p, p, p, 1, 2, 2, 256, 64, 1, math.inf, p,
+                               ws, None) == FA_EINVAL
