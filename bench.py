@@ -468,6 +468,13 @@ def run_ours(args, rank, world, local_rank):
                         "once for its 7 query heads; L2 flushed between steps"}
             del qd, kc, vc
 
+        # ------- NVIDIA's library attention on the headline shape (context) --
+        # cuDNN's fused attention through torch SDPA: a library kernel, timed
+        # beside ours for reference only; nothing of it is on our path.
+        if world == 1 and not args.no_library:
+            secondary["cudnn_sdpa_c3"] = cudnn_measure(
+                timer, randn, args.steps, args.warmup, value)
+
         # ------- the reference's own CUDA kernels on this B200 (baseline) ----
         if world == 1 and not args.no_ref_cuda:
             secondary["reference_cuda_kernels"] = ref_cuda_measure(
@@ -611,6 +618,31 @@ def cpu_baseline(budget_s):
                       f"of src/attention_cpu.py ({secs:.1f} s)"}
 
 
+def cudnn_measure(timer, randn, steps, warmup, ours_tflops):
+    """Config 3 through torch SDPA restricted to the cuDNN backend, with the
+    same inputs shape, L2 flush and timing as the headline line."""
+    import torch
+    try:
+        from torch.nn.attention import SDPBackend, sdpa_kernel
+        q = randn(C3["B"], C3["H"], C3["N"], HEAD_DIM, seed=1000)
+        k = randn(C3["B"], C3["H"], C3["N"], HEAD_DIM, seed=2000)
+        v = randn(C3["B"], C3["H"], C3["N"], HEAD_DIM, seed=3000)
+
+        def step():
+            with sdpa_kernel(SDPBackend.CUDNN_ATTENTION):
+                torch.nn.functional.scaled_dot_product_attention(
+                    q, k, v, is_causal=True, scale=SCALE)
+
+        ms = timer.run(step, steps, warmup) / steps
+        tf = prefill_flops(C3["B"], C3["H"], C3["N"], True) / (ms * 1e-3) / 1e12
+        return {"ms": round(ms, 5), "tflops": round(tf, 2),
+                "ours_over_cudnn": round(ours_tflops / tf, 3),
+                "note": "cuDNN fused attention (torch SDPA, CUDNN_ATTENTION "
+                        "backend) on config 3: library kernel, context only"}
+    except Exception as exc:  # library missing or backend refused the shape
+        return {"unavailable": f"{type(exc).__name__}: {str(exc)[:120]}"}
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return
@@ -657,6 +689,8 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=12.0,
                     help="seconds of CPU work for the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-library", action="store_true",
+                    help="skip the cuDNN (torch SDPA) comparison line")
     ap.add_argument("--no-ref-cuda", action="store_true",
                     help="skip timing the reference's own CUDA kernels")
     args = ap.parse_args()
