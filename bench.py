@@ -432,6 +432,34 @@ def run_ours(args, rank, world, local_rank):
                 "note": "config 3 shape at head_dim 128 (the reference's named "
                         "next size), causal"}
             del qh, kh, vh
+            # bf16 (the reference's other named next variant): config 3
+            # prefill and the config-5 decode with bf16 tensors
+            qb, kb, vb = (randn(C3["B"], C3["H"], C3["N"], HEAD_DIM,
+                                seed=110 + i).to(torch.bfloat16)
+                          for i in range(3))
+            tb = timer.run(lambda: fa.prefill(qb, kb, vb, True, SCALE),
+                           args.steps, args.warmup) / args.steps
+            launches += args.steps
+            fb = prefill_flops(C3["B"], C3["H"], C3["N"], True)
+            secondary["c3_prefill_bf16"] = {
+                "ms": round(tb, 5),
+                "tflops": round(fb / (tb * 1e-3) / 1e12, 2),
+                "frac_of_measured_bf16_peak": round(
+                    fb / (tb * 1e-3) / 1e12 / peak, 4)}
+            del qb, kb, vb
+            qdb = randn(1, C5["H"], 1, HEAD_DIM, seed=113).to(torch.bfloat16)
+            kcb = randn(1, C5["H"], C5["S"], HEAD_DIM, seed=114).to(torch.bfloat16)
+            vcb = randn(1, C5["H"], C5["S"], HEAD_DIM, seed=115).to(torch.bfloat16)
+            lensb = torch.tensor([C5["S"]], dtype=torch.int32, device="cuda")
+            tdb = timer.run(lambda: fa.decode(qdb, kcb, vcb, lensb, SCALE),
+                            args.steps, args.warmup) / args.steps
+            launches += args.steps
+            bb = C5["S"] * C5["H"] * HEAD_DIM * 2 * 2
+            secondary["c5_decode_bf16"] = {
+                "ms": round(tdb, 5),
+                "gbs": round(bb / (tdb * 1e-3) / 1e9, 1),
+                "frac_of_measured_hbm": round(bb / (tdb * 1e-3) / 1e9 / hbm, 4)}
+            del qdb, kcb, vcb
             secondary["c3_prefill_gqa_kv2"] = {
                 "ms": round(t, 5),
                 "tflops": round(prefill_flops(C3["B"], C3["H"], C3["N"], True)

@@ -43,10 +43,20 @@ void check_bhnd(const at::Tensor &t, const char *name) {
               kHeadDim, ", got ", t.size(3));
 }
 
-// Prefill and per-head decode also take head_dim 128 (kernels of their own).
+// fp16, or bf16 where a kernel exists for it (prefill and decode).
+void check_16bit(const at::Tensor &t, const char *name) {
+  TORCH_CHECK(t.scalar_type() == at::kHalf || t.scalar_type() == at::kBFloat16,
+              name, " must be fp16 or bf16 (got ", t.scalar_type(), ")");
+}
+int dtype_code(const at::Tensor &t) {
+  return t.scalar_type() == at::kBFloat16 ? FA_DTYPE_BF16 : FA_DTYPE_F16;
+}
+
+// Prefill and per-head decode also take head_dim 128 (kernels of their own)
+// and bf16 tensors.
 void check_bhnd_any(const at::Tensor &t, const char *name) {
   check_cuda(t, name);
-  check_half(t, name);
+  check_16bit(t, name);
   check_contiguous(t, name);
   TORCH_CHECK(t.dim() == 4, name, " must be 4-D (B, H, N, ", kHeadDim,
               "), got ", t.dim(), "-D");
@@ -106,6 +116,11 @@ void check_decode_inputs(const at::Tensor &q, const at::Tensor &k_cache,
   check_bhnd_any(q, "q");
   check_bhnd_any(k_cache, "k_cache");
   check_bhnd_any(v_cache, "v_cache");
+  TORCH_CHECK(q.scalar_type() == k_cache.scalar_type() &&
+                  q.scalar_type() == v_cache.scalar_type(),
+              "q and the caches must have the same dtype, got ",
+              q.scalar_type(), ", ", k_cache.scalar_type(), " and ",
+              v_cache.scalar_type());
   TORCH_CHECK(q.size(3) == k_cache.size(3),
               "q and the caches must have the same head_dim, got ", q.size(3),
               " and ", k_cache.size(3));
@@ -141,6 +156,10 @@ at::Tensor prefill(const at::Tensor &q, const at::Tensor &k,
   check_bhnd_any(q, "q");
   check_bhnd_any(k, "k");
   check_bhnd_any(v, "v");
+  TORCH_CHECK(q.scalar_type() == k.scalar_type() &&
+                  q.scalar_type() == v.scalar_type(),
+              "q, k and v must have the same dtype, got ", q.scalar_type(),
+              ", ", k.scalar_type(), " and ", v.scalar_type());
   // Identical shapes as in the reference; additionally k and v may have
   // fewer heads than q when they divide it (grouped-query attention).
   const bool same = q.sizes() == k.sizes() && q.sizes() == v.sizes();
@@ -157,13 +176,14 @@ at::Tensor prefill(const at::Tensor &q, const at::Tensor &k,
 
   const c10::cuda::CUDAGuard guard(q.device());
   at::Tensor o = at::empty_like(q);
-  check_status(fa_prefill_hd(q.data_ptr(), k.data_ptr(), v.data_ptr(),
+  check_status(fa_prefill_ex(q.data_ptr(), k.data_ptr(), v.data_ptr(),
                              o.data_ptr(), to_int(q.size(0), "batch"),
                              to_int(q.size(1), "heads"),
                              to_int(k.size(1), "kv heads"),
                              to_int(q.size(2), "sequence length"),
-                             to_int(q.size(3), "head_dim"), causal ? 1 : 0,
-                             static_cast<float>(scale), current_stream()),
+                             to_int(q.size(3), "head_dim"), dtype_code(q),
+                             causal ? 1 : 0, static_cast<float>(scale),
+                             current_stream()),
                "fa_prefill");
   return o;
 }
@@ -257,6 +277,8 @@ at::Tensor decode_impl(const at::Tensor &q, const at::Tensor &k_cache,
   at::Tensor o = at::empty_like(q);
   const int H_kv = to_int(k_cache.size(1), "kv heads");
   const int D = to_int(q.size(3), "head_dim");
+  const bool bf16 = q.scalar_type() == at::kBFloat16;
+  TORCH_CHECK(!bf16 || split == 0, "a forced split size needs fp16 tensors");
   const size_t bytes =
       H_kv != H
           ? fa_decode_gqa_hd_workspace_bytes(B, H, H_kv, S, D, q.get_device())
@@ -264,7 +286,17 @@ at::Tensor decode_impl(const at::Tensor &q, const at::Tensor &k_cache,
   TORCH_CHECK(bytes > 0, "fa_decode_workspace_bytes failed");
   DecodeScratch &ws = decode_scratch(q, bytes, static_cast<size_t>(B) * H);
   uint32_t *ctr = reinterpret_cast<uint32_t *>(ws.counters.data_ptr<int32_t>());
-  if (H_kv == H) {
+  if (bf16) {
+    check_status(
+        fa_decode_ex(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                     seq_lens.data_ptr<int32_t>(), o.data_ptr(), B, H, H_kv,
+                     S, D, FA_DTYPE_BF16, static_cast<float>(scale),
+                     ws.partials.data_ptr(),
+                     static_cast<size_t>(ws.partials.numel()), ctr,
+                     static_cast<size_t>(ws.counters.numel()),
+                     current_stream()),
+        "fa_decode");
+  } else if (H_kv == H) {
     check_status(
         fa_decode_hd(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
                      seq_lens.data_ptr<int32_t>(), o.data_ptr(), B, H, S, D,
@@ -298,6 +330,7 @@ at::Tensor decode_partial(const at::Tensor &q, const at::Tensor &k_cache,
                           const at::Tensor &v_cache,
                           const at::Tensor &seq_lens, double scale) {
   check_decode_inputs(q, k_cache, v_cache, seq_lens, scale);
+  TORCH_CHECK(q.scalar_type() == at::kHalf, "decode_partial needs fp16 tensors");
   TORCH_CHECK(q.size(3) == kHeadDim, "decode_partial needs head_dim == ",
               kHeadDim);
   TORCH_CHECK(k_cache.size(1) == q.size(1),
@@ -331,6 +364,7 @@ at::Tensor decode_append(const at::Tensor &q, const at::Tensor &k_new,
                          at::Tensor v_cache, const at::Tensor &seq_lens,
                          double scale) {
   check_decode_inputs(q, k_cache, v_cache, seq_lens, scale);
+  TORCH_CHECK(q.scalar_type() == at::kHalf, "decode_append needs fp16 tensors");
   check_bhnd_any(k_new, "k_new");
   check_bhnd_any(v_new, "v_new");
   TORCH_CHECK(k_new.sizes() == v_new.sizes() && k_new.size(0) == k_cache.size(0) &&
@@ -407,6 +441,7 @@ at::Tensor decode_exchange(const at::Tensor &q, const at::Tensor &k_cache,
                            const at::Tensor &peers, int64_t rank,
                            int64_t world, int64_t epoch) {
   check_decode_inputs(q, k_cache, v_cache, seq_lens, scale);
+  TORCH_CHECK(q.scalar_type() == at::kHalf, "decode_exchange needs fp16 tensors");
   TORCH_CHECK(q.size(3) == kHeadDim && k_cache.size(1) == q.size(1),
               "sharded decode needs head_dim == ", kHeadDim,
               " and one K/V head per query head");

@@ -70,37 +70,28 @@ int ensure_device(int *device_out) {
     return st.status;
   }
   st.sms = sms;
-  if (cudaFuncSetAttribute(prefill_kernel_ptr(),
-                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           prefill_smem_bytes()) != cudaSuccess ||
-      cudaFuncSetAttribute(decode_kernel_ptr(),
-                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           decode_smem_bytes()) != cudaSuccess ||
-      cudaFuncSetAttribute(decode_d128_kernel_ptr(),
-                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           decode_d128_smem_bytes()) != cudaSuccess ||
-      cudaFuncSetAttribute(decode_d128_kernel_ptr(),
-                           cudaFuncAttributePreferredSharedMemoryCarveout,
-                           cudaSharedmemCarveoutMaxShared) != cudaSuccess ||
-      cudaFuncSetAttribute(prefill_d128_kernel_ptr(),
-                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           prefill_d128_smem_bytes()) != cudaSuccess ||
-      cudaFuncSetAttribute(decode_gqa_kernel_ptr(64),
-                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           decode_gqa_smem_bytes(64)) != cudaSuccess ||
-      cudaFuncSetAttribute(decode_gqa_kernel_ptr(128),
-                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           decode_gqa_smem_bytes(128)) != cudaSuccess ||
-      // Both kernels are sized for two CTAs per SM, which needs the whole
-      // unified L1/shared array configured as shared memory.
-      cudaFuncSetAttribute(prefill_kernel_ptr(),
-                           cudaFuncAttributePreferredSharedMemoryCarveout,
-                           cudaSharedmemCarveoutMaxShared) != cudaSuccess ||
-      cudaFuncSetAttribute(decode_kernel_ptr(),
-                           cudaFuncAttributePreferredSharedMemoryCarveout,
-                           cudaSharedmemCarveoutMaxShared) != cudaSuccess) {
-    st.status = FA_ECUDA;
-    return st.status;
+  // Every kernel instantiation: its dynamic shared memory limit, and the
+  // whole unified L1/shared array configured as shared memory.
+  for (int dt = FA_DTYPE_F16; dt <= FA_DTYPE_BF16; ++dt) {
+    const void *big_smem[] = {prefill_kernel_ptr(dt), decode_kernel_ptr(dt),
+                              decode_d128_kernel_ptr(dt),
+                              prefill_d128_kernel_ptr(dt),
+                              decode_gqa_kernel_ptr(64, dt),
+                              decode_gqa_kernel_ptr(128, dt)};
+    const int bytes[] = {prefill_smem_bytes(), decode_smem_bytes(),
+                         decode_d128_smem_bytes(), prefill_d128_smem_bytes(),
+                         decode_gqa_smem_bytes(64), decode_gqa_smem_bytes(128)};
+    for (int i = 0; i < 6; ++i) {
+      if (cudaFuncSetAttribute(big_smem[i],
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               bytes[i]) != cudaSuccess ||
+          cudaFuncSetAttribute(big_smem[i],
+                               cudaFuncAttributePreferredSharedMemoryCarveout,
+                               cudaSharedmemCarveoutMaxShared) != cudaSuccess) {
+        st.status = FA_ECUDA;
+        return st.status;
+      }
+    }
   }
   if (!g_encode) {
     void *fn = nullptr;
@@ -122,7 +113,7 @@ int ensure_device(int *device_out) {
 // Boxes are always 64 columns (128 bytes, the swizzle span); a 128-wide
 // head is loaded as two boxes at columns 0 and 64.
 int make_bhnd_map(CUtensorMap *map, const void *base, int BH, int N, int D,
-                  int box_rows) {
+                  int box_rows, int dtype = FA_DTYPE_F16) {
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(D),
                         static_cast<cuuint64_t>(N),
                         static_cast<cuuint64_t>(BH)};
@@ -130,17 +121,17 @@ int make_bhnd_map(CUtensorMap *map, const void *base, int BH, int N, int D,
                            static_cast<cuuint64_t>(N) * D * 2};
   cuuint32_t box[3] = {64, static_cast<cuuint32_t>(box_rows), 1};
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+  CUresult r = g_encode(map,
+                        dtype == FA_DTYPE_BF16
+                            ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                            : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                        3,
                         const_cast<void *>(base), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE,
                         CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? FA_OK : FA_EINVAL;
-}
-
-int make_bhn64_map(CUtensorMap *map, const void *base, int BH, int N) {
-  return make_bhnd_map(map, base, BH, N, FA_HEAD_DIM, 128);
 }
 
 int decode_grid(int sms, int B, int H, int S_max, int split_size) {
@@ -213,7 +204,7 @@ int run_decode_gqa(const void *q, const void *k_cache, const void *v_cache,
                    const void *k_new = nullptr, const void *v_new = nullptr,
                    float *const *x_peers = nullptr, int x_rank = 0,
                    int x_world = 1, uint32_t x_epoch = 0,
-                   int head_dim = FA_HEAD_DIM) {
+                   int head_dim = FA_HEAD_DIM, int dtype = FA_DTYPE_F16) {
   if (head_dim != FA_HEAD_DIM && (head_dim != 128 || H_kv == H || x_peers ||
                                   partial_out || split_size > 0))
     return FA_EINVAL;
@@ -246,6 +237,7 @@ int run_decode_gqa(const void *q, const void *k_cache, const void *v_cache,
                   x_world > 32 || x_rank < 0 || x_rank >= x_world))
     return FA_EINVAL;
   DecodeArgs a{};
+  a.dtype = dtype;
   a.x_peers = x_peers;
   a.x_rank = x_rank;
   a.x_world = x_world;
@@ -272,8 +264,10 @@ int run_decode_gqa(const void *q, const void *k_cache, const void *v_cache,
   if (grouped) {
     CUtensorMap tk, tv;
     const int rows = decode_gqa_box_rows(head_dim);
-    if (make_bhnd_map(&tk, k_cache, B * H_kv, S_max, head_dim, rows) != FA_OK ||
-        make_bhnd_map(&tv, v_cache, B * H_kv, S_max, head_dim, rows) != FA_OK)
+    if (make_bhnd_map(&tk, k_cache, B * H_kv, S_max, head_dim, rows, dtype) !=
+            FA_OK ||
+        make_bhnd_map(&tv, v_cache, B * H_kv, S_max, head_dim, rows, dtype) !=
+            FA_OK)
       return FA_EINVAL;
     return launch_decode_gqa_kernel(a, tk, tv, head_dim,
                                     static_cast<cudaStream_t>(stream)) ==
@@ -297,6 +291,42 @@ int run_decode(const void *q, const void *k_cache, const void *v_cache,
                         counters, counter_count, stream);
 }
 
+// Prefill for head_dim 64 or 128, fp16 or bf16: argument checks, tensor
+// maps and the launch.
+int run_prefill(const void *q, const void *k, const void *v, void *o, int B,
+                int H, int H_kv, int N, int head_dim, int dtype, int causal,
+                float scale, void *stream) {
+  if (head_dim != FA_HEAD_DIM && head_dim != 128) return FA_EINVAL;
+  if (B <= 0 || H <= 0 || N <= 0 || !isfinite(scale)) return FA_EINVAL;
+  if (H_kv <= 0 || H % H_kv != 0) return FA_EINVAL;
+  if (static_cast<long long>(B) * H >= (1ll << 31) / head_dim ||
+      static_cast<long long>(N) >= (1ll << 31))
+    return FA_EINVAL;
+  if (!q || !k || !v || !o) return FA_EINVAL;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+    return FA_EALIGN;
+  int dev = 0;
+  int rc = ensure_device(&dev);
+  if (rc != FA_OK) return rc;
+  CUtensorMap tq, tk, tv;
+  const int kv_rows = head_dim == FA_HEAD_DIM ? 128 : 64;
+  if (make_bhnd_map(&tq, q, B * H, N, head_dim, 128, dtype) != FA_OK ||
+      make_bhnd_map(&tk, k, B * H_kv, N, head_dim, kv_rows, dtype) != FA_OK ||
+      make_bhnd_map(&tv, v, B * H_kv, N, head_dim, kv_rows, dtype) != FA_OK)
+    return FA_EINVAL;
+  const cudaError_t err =
+      head_dim == FA_HEAD_DIM
+          ? launch_prefill_kernel(tq, tk, tv, static_cast<__half *>(o), B, H,
+                                  N, causal != 0, scale, H_kv,
+                                  g_devices[dev].sms, dtype,
+                                  static_cast<cudaStream_t>(stream))
+          : launch_prefill_d128_kernel(tq, tk, tv, static_cast<__half *>(o), B,
+                                       H, N, causal != 0, scale, H_kv,
+                                       g_devices[dev].sms, dtype,
+                                       static_cast<cudaStream_t>(stream));
+  return err == cudaSuccess ? FA_OK : FA_ECUDA;
+}
+
 }  // namespace
 }  // namespace fa
 
@@ -312,58 +342,23 @@ int fa_prefill(const void *q, const void *k, const void *v, void *o, int B,
 int fa_prefill_hd(const void *q, const void *k, const void *v, void *o, int B,
                   int H, int H_kv, int N, int head_dim, int causal,
                   float scale, void *stream) {
-  if (head_dim == FA_HEAD_DIM)
-    return fa_prefill_gqa(q, k, v, o, B, H, H_kv, N, causal, scale, stream);
-  if (head_dim != 128) return FA_EINVAL;
-  if (B <= 0 || H <= 0 || N <= 0 || !isfinite(scale)) return FA_EINVAL;
-  if (H_kv <= 0 || H % H_kv != 0) return FA_EINVAL;
-  if (static_cast<long long>(B) * H >= (1ll << 31) / 128 ||
-      static_cast<long long>(N) >= (1ll << 31))
-    return FA_EINVAL;
-  if (!q || !k || !v || !o) return FA_EINVAL;
-  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
-    return FA_EALIGN;
-  int dev = 0;
-  int rc = ensure_device(&dev);
-  if (rc != FA_OK) return rc;
-  CUtensorMap tq, tk, tv;
-  if (make_bhnd_map(&tq, q, B * H, N, 128, 128) != FA_OK ||
-      make_bhnd_map(&tk, k, B * H_kv, N, 128, 64) != FA_OK ||
-      make_bhnd_map(&tv, v, B * H_kv, N, 128, 64) != FA_OK)
-    return FA_EINVAL;
-  return launch_prefill_d128_kernel(tq, tk, tv, static_cast<__half *>(o), B,
-                                    H, N, causal != 0, scale, H_kv,
-                                    g_devices[dev].sms,
-                                    static_cast<cudaStream_t>(stream)) ==
-                 cudaSuccess
-             ? FA_OK
-             : FA_ECUDA;
+  return run_prefill(q, k, v, o, B, H, H_kv, N, head_dim, FA_DTYPE_F16,
+                     causal, scale, stream);
 }
 
 int fa_prefill_gqa(const void *q, const void *k, const void *v, void *o, int B,
                    int H, int H_kv, int N, int causal, float scale,
                    void *stream) {
-  if (B <= 0 || H <= 0 || N <= 0 || !isfinite(scale)) return FA_EINVAL;
-  if (H_kv <= 0 || H % H_kv != 0) return FA_EINVAL;
-  if (static_cast<long long>(B) * H >= (1ll << 31) / 64 ||
-      static_cast<long long>(N) >= (1ll << 31))
-    return FA_EINVAL;
-  if (!q || !k || !v || !o) return FA_EINVAL;
-  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
-    return FA_EALIGN;
-  int dev = 0;
-  int rc = ensure_device(&dev);
-  if (rc != FA_OK) return rc;
-  CUtensorMap tq, tk, tv;
-  if (make_bhn64_map(&tq, q, B * H, N) != FA_OK ||
-      make_bhn64_map(&tk, k, B * H_kv, N) != FA_OK ||
-      make_bhn64_map(&tv, v, B * H_kv, N) != FA_OK)
-    return FA_EINVAL;
-  return launch_prefill_kernel(tq, tk, tv, static_cast<__half *>(o), B, H, N,
-                               causal != 0, scale, H_kv, g_devices[dev].sms,
-                               static_cast<cudaStream_t>(stream)) == cudaSuccess
-             ? FA_OK
-             : FA_ECUDA;
+  return run_prefill(q, k, v, o, B, H, H_kv, N, FA_HEAD_DIM, FA_DTYPE_F16,
+                     causal, scale, stream);
+}
+
+int fa_prefill_ex(const void *q, const void *k, const void *v, void *o, int B,
+                  int H, int H_kv, int N, int head_dim, int dtype, int causal,
+                  float scale, void *stream) {
+  if (dtype != FA_DTYPE_F16 && dtype != FA_DTYPE_BF16) return FA_EINVAL;
+  return run_prefill(q, k, v, o, B, H, H_kv, N, head_dim, dtype, causal,
+                     scale, stream);
 }
 
 size_t fa_decode_workspace_bytes(int B, int H, int S_max, int split_size,
@@ -452,7 +447,7 @@ int run_decode_d128(const void *q, const void *k_cache, const void *v_cache,
                     float scale, int split_size, void *workspace,
                     size_t workspace_bytes, uint32_t *counters,
                     size_t counter_count, void *stream, const void *k_new,
-                    const void *v_new) {
+                    const void *v_new, int dtype = FA_DTYPE_F16) {
   if (!decode_shape_ok(B, H, S_max, scale)) return FA_EINVAL;
   if (split_size > 0 && split_size % 4 != 0) return FA_EINVAL;
   if (!q || !k_cache || !v_cache || !seq_lens || !o || !workspace || !counters)
@@ -473,6 +468,7 @@ int run_decode_d128(const void *q, const void *k_cache, const void *v_cache,
   if ((k_new == nullptr) != (v_new == nullptr)) return FA_EINVAL;
   if (k_new && (!aligned16(k_new) || !aligned16(v_new))) return FA_EALIGN;
   DecodeArgs a{};
+  a.dtype = dtype;
   a.k_new = static_cast<const __half *>(k_new);
   a.v_new = static_cast<const __half *>(v_new);
   a.k_cache_w = k_new ? static_cast<__half *>(const_cast<void *>(k_cache)) : nullptr;
@@ -567,6 +563,28 @@ int fa_decode_gqa_hd(const void *q, const void *k_cache, const void *v_cache,
                         S_max, scale, 0, workspace, workspace_bytes, counters,
                         counter_count, stream, nullptr, nullptr, nullptr, 0, 1,
                         0, head_dim);
+}
+
+size_t fa_decode_ex_workspace_bytes(int B, int H, int H_kv, int S_max,
+                                    int head_dim, int device) {
+  return fa_decode_gqa_hd_workspace_bytes(B, H, H_kv, S_max, head_dim, device);
+}
+
+int fa_decode_ex(const void *q, const void *k_cache, const void *v_cache,
+                 const int32_t *seq_lens, void *o, int B, int H, int H_kv,
+                 int S_max, int head_dim, int dtype, float scale,
+                 void *workspace, size_t workspace_bytes, uint32_t *counters,
+                 size_t counter_count, void *stream) {
+  if (dtype != FA_DTYPE_F16 && dtype != FA_DTYPE_BF16) return FA_EINVAL;
+  if (!o || (head_dim != FA_HEAD_DIM && head_dim != 128)) return FA_EINVAL;
+  if (head_dim == 128 && H_kv == H)
+    return run_decode_d128(q, k_cache, v_cache, seq_lens, o, B, H, S_max,
+                           scale, 0, workspace, workspace_bytes, counters,
+                           counter_count, stream, nullptr, nullptr, dtype);
+  return run_decode_gqa(q, k_cache, v_cache, seq_lens, o, nullptr, B, H, H_kv,
+                        S_max, scale, 0, workspace, workspace_bytes, counters,
+                        counter_count, stream, nullptr, nullptr, nullptr, 0, 1,
+                        0, head_dim, dtype);
 }
 
 size_t fa_decode_gqa_workspace_bytes(int B, int H, int H_kv, int S_max,

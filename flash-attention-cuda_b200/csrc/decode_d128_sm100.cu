@@ -88,7 +88,7 @@ __device__ __forceinline__ void finish_segment(const DecodeArgs &a, size_t g,
     const float inv = L > 0.f ? 1.f / L : 0.f;
 #pragma unroll
     for (int i = 0; i < 4; ++i)
-      a.out[g * kD + 32 * i + lane] = __float2half_rn(A[i] * inv);
+      a.out[g * kD + 32 * i + lane] = store_elem(A[i] * inv, a.dtype);
   }
 }
 
@@ -167,6 +167,7 @@ __device__ void merger(const DecodeArgs &a, uint8_t *red_base,
   }
 }
 
+template <typename Dt>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     decode_d128_kernel(const DecodeArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -250,10 +251,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       }
       const uint4 qv = *reinterpret_cast<const uint4 *>(
           a.q + static_cast<size_t>(cur_g) * kD + sub * 8);
-      const __half2 *qh = reinterpret_cast<const __half2 *>(&qv);
+      const uint32_t *qh = reinterpret_cast<const uint32_t *>(&qv);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float2 f = __half22float2(qh[e]);
+        const float2 f = Dt::unpack2(qh[e]);
         qf[2 * e] = f.x * a.scale_log2;
         qf[2 * e + 1] = f.y * a.scale_log2;
       }
@@ -277,10 +278,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         float d = 0.f;
         if (row < hd.n) {
           const uint4 kv = ld_shared_v4(kb + row * kRowB + sub * 16);
-          const __half2 *kh = reinterpret_cast<const __half2 *>(&kv);
+          const uint32_t *kh = reinterpret_cast<const uint32_t *>(&kv);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const float2 f = __half22float2(kh[e]);
+            const float2 f = Dt::unpack2(kh[e]);
             d = fmaf(qf[2 * e], f.x, d);
             d = fmaf(qf[2 * e + 1], f.y, d);
           }
@@ -315,10 +316,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         const int row = row_base + kRowsPerInstr * i;
         if (row < hd.n) {
           const uint4 vv = ld_shared_v4(vb + row * kRowB + sub * 16);
-          const __half2 *vh = reinterpret_cast<const __half2 *>(&vv);
+          const uint32_t *vh = reinterpret_cast<const uint32_t *>(&vv);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const float2 f = __half22float2(vh[e]);
+            const float2 f = Dt::unpack2(vh[e]);
             acc[2 * e] = fmaf(p[i], f.x, acc[2 * e]);
             acc[2 * e + 1] = fmaf(p[i], f.y, acc[2 * e + 1]);
           }
@@ -374,8 +375,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 
 }  // namespace decode128
 
-const void *decode_d128_kernel_ptr() {
-  return reinterpret_cast<const void *>(decode128::decode_d128_kernel);
+const void *decode_d128_kernel_ptr(int dtype) {
+  return dtype == FA_DTYPE_BF16
+             ? reinterpret_cast<const void *>(decode128::decode_d128_kernel<BF16>)
+             : reinterpret_cast<const void *>(decode128::decode_d128_kernel<F16>);
 }
 int decode_d128_smem_bytes() {
   return static_cast<int>(decode128::kSmemBytes);
@@ -384,8 +387,11 @@ int decode_d128_partial_floats() { return decode128::kPF; }
 
 cudaError_t launch_decode_d128_kernel(const DecodeArgs &args,
                                       cudaStream_t stream) {
-  decode128::decode_d128_kernel<<<args.grid, decode128::kThreads,
-                                  decode128::kSmemBytes, stream>>>(args);
+  auto kernel = args.dtype == FA_DTYPE_BF16
+                    ? decode128::decode_d128_kernel<BF16>
+                    : decode128::decode_d128_kernel<F16>;
+  kernel<<<args.grid, decode128::kThreads, decode128::kSmemBytes, stream>>>(
+      args);
   return cudaGetLastError();
 }
 

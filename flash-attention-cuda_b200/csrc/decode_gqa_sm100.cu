@@ -107,7 +107,7 @@ __device__ __forceinline__ void gqa_finish_head(const DecodeArgs &a, size_t gq,
     const float inv = L > 0.f ? 1.f / L : 0.f;
 #pragma unroll
     for (int i = 0; i < D / 32; ++i)
-      a.out[gq * D + 32 * i + lane] = __float2half_rn(A[i] * inv);
+      a.out[gq * D + 32 * i + lane] = store_elem(A[i] * inv, a.dtype);
   }
 }
 
@@ -343,11 +343,12 @@ __device__ void coop_merge(const DecodeArgs &a, int g, int c0, int c1,
       }
     } else {
       const float inv = L > 0.f ? 1.f / L : 0.f;
-      __half2 h01 = __floats2half2_rn(acc[k].x * inv, acc[k].y * inv);
-      __half2 h23 = __floats2half2_rn(acc[k].z * inv, acc[k].w * inv);
+      const bool bf = a.dtype == FA_DTYPE_BF16;
       uint2 v;
-      v.x = *reinterpret_cast<uint32_t *>(&h01);
-      v.y = *reinterpret_cast<uint32_t *>(&h23);
+      v.x = bf ? BF16::pack2(acc[k].x * inv, acc[k].y * inv)
+               : F16::pack2(acc[k].x * inv, acc[k].y * inv);
+      v.y = bf ? BF16::pack2(acc[k].z * inv, acc[k].w * inv)
+               : F16::pack2(acc[k].z * inv, acc[k].w * inv);
       *reinterpret_cast<uint2 *>(a.out + gq * D + 4 * dq) = v;
     }
   }
@@ -355,7 +356,7 @@ __device__ void coop_merge(const DecodeArgs &a, int g, int c0, int c1,
 }
 
 // Consumer warps of the grouped kernel.
-template <int D>
+template <int D, typename Dt>
 __device__ __forceinline__ void gqa_consume(
     const DecodeArgs &a, int nseg, int n_hc, int group, uint8_t *smem,
     uint64_t *full, uint64_t *empty, uint64_t *red_full, uint64_t *red_empty,
@@ -458,8 +459,8 @@ __device__ __forceinline__ void gqa_consume(
           ldsm_x4(kb + blk * C::kBlock + row * 128 +
                       ((chunk ^ (row & 7)) << 4),
                   kf);
-          mma_16816(sc[j], qa[2 * pp], kf[0], kf[1]);
-          mma_16816(sc[j], qa[2 * pp + 1], kf[2], kf[3]);
+          Dt::mma16816(sc[j], qa[2 * pp], kf[0], kf[1]);
+          Dt::mma16816(sc[j], qa[2 * pp + 1], kf[2], kf[3]);
         }
       }
       // online softmax per head row (rows quad and quad + 8)
@@ -502,10 +503,10 @@ __device__ __forceinline__ void gqa_consume(
         o[dt][3] *= corr1;
       }
       // P as the A operand: k index = key within the 16 (C -> A layout)
-      const uint32_t pa[4] = {pack_half2(p[0][0], p[0][1]),
-                              pack_half2(p[0][2], p[0][3]),
-                              pack_half2(p[1][0], p[1][1]),
-                              pack_half2(p[1][2], p[1][3])};
+      const uint32_t pa[4] = {Dt::pack2(p[0][0], p[0][1]),
+                              Dt::pack2(p[0][2], p[0][3]),
+                              Dt::pack2(p[1][0], p[1][1]),
+                              Dt::pack2(p[1][2], p[1][3])};
       // O += P V over dims 8dt..8dt+8, V read transposed; chunk c of the
       // row (8 dims) lives in block c / 8
       const int vrow = key0 + 8 * ((lane >> 3) & 1) + (lane & 7);
@@ -516,8 +517,8 @@ __device__ __forceinline__ void gqa_consume(
         ldsm_x4_trans(vb + (chunk >> 3) * C::kBlock + vrow * 128 +
                           (((chunk & 7) ^ (vrow & 7)) << 4),
                       vf);
-        mma_16816(o[2 * dp], pa, vf[0], vf[1]);
-        mma_16816(o[2 * dp + 1], pa, vf[2], vf[3]);
+        Dt::mma16816(o[2 * dp], pa, vf[0], vf[1]);
+        Dt::mma16816(o[2 * dp + 1], pa, vf[2], vf[3]);
       }
     }
     __syncwarp();
@@ -567,7 +568,7 @@ __device__ __forceinline__ void gqa_consume(
   }
 }
 
-template <int D>
+template <int D, typename Dt>
 __global__ void __launch_bounds__(GqaCfg<D>::kThreads, 1)
     decode_gqa_kernel(const DecodeArgs a,
                       const __grid_constant__ CUtensorMap tm_k,
@@ -630,7 +631,7 @@ __global__ void __launch_bounds__(GqaCfg<D>::kThreads, 1)
     merger_gqa<D>(a, nseg, n_hc, group, smem + C::kRedOff, red_full,
                   red_empty, pend);
   } else {
-    gqa_consume<D>(a, nseg, n_hc, group, smem, full, empty, red_full,
+    gqa_consume<D, Dt>(a, nseg, n_hc, group, smem, full, empty, red_full,
                    red_empty, hdr);
   }
   // Streaming is over for every warp (the stage and hand-off buffers are
@@ -658,10 +659,15 @@ __global__ void __launch_bounds__(GqaCfg<D>::kThreads, 1)
 
 }  // namespace decode
 
-const void *decode_gqa_kernel_ptr(int head_dim) {
-  return head_dim == 128
-             ? reinterpret_cast<const void *>(decode::decode_gqa_kernel<128>)
-             : reinterpret_cast<const void *>(decode::decode_gqa_kernel<64>);
+const void *decode_gqa_kernel_ptr(int head_dim, int dtype) {
+  const bool bf = dtype == FA_DTYPE_BF16;
+  if (head_dim == 128)
+    return bf ? reinterpret_cast<const void *>(
+                    decode::decode_gqa_kernel<128, BF16>)
+              : reinterpret_cast<const void *>(
+                    decode::decode_gqa_kernel<128, F16>);
+  return bf ? reinterpret_cast<const void *>(decode::decode_gqa_kernel<64, BF16>)
+            : reinterpret_cast<const void *>(decode::decode_gqa_kernel<64, F16>);
 }
 int decode_gqa_smem_bytes(int head_dim) {
   return static_cast<int>(head_dim == 128 ? decode::GqaCfg<128>::kSmemBytes
@@ -677,14 +683,17 @@ cudaError_t launch_decode_gqa_kernel(const DecodeArgs &args,
                                      const CUtensorMap &tm_k,
                                      const CUtensorMap &tm_v, int head_dim,
                                      cudaStream_t stream) {
+  const bool bf = args.dtype == FA_DTYPE_BF16;
   if (head_dim == 128) {
     using C = decode::GqaCfg<128>;
-    decode::decode_gqa_kernel<128>
-        <<<args.grid, C::kThreads, C::kSmemBytes, stream>>>(args, tm_k, tm_v);
+    auto kernel = bf ? decode::decode_gqa_kernel<128, BF16>
+                     : decode::decode_gqa_kernel<128, F16>;
+    kernel<<<args.grid, C::kThreads, C::kSmemBytes, stream>>>(args, tm_k, tm_v);
   } else {
     using C = decode::GqaCfg<64>;
-    decode::decode_gqa_kernel<64>
-        <<<args.grid, C::kThreads, C::kSmemBytes, stream>>>(args, tm_k, tm_v);
+    auto kernel = bf ? decode::decode_gqa_kernel<64, BF16>
+                     : decode::decode_gqa_kernel<64, F16>;
+    kernel<<<args.grid, C::kThreads, C::kSmemBytes, stream>>>(args, tm_k, tm_v);
   }
   return cudaGetLastError();
 }

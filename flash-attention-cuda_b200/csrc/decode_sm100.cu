@@ -246,8 +246,8 @@ __device__ void x_finish(const DecodeArgs &a, size_t g, int lane) {
     B1 = fmaf(__ldcg(p + 4 + 32 + lane), f, B1);
   }
   const float inv = L > 0.f ? 1.f / L : 0.f;
-  a.out[g * kHeadDim + lane] = __float2half_rn(B0 * inv);
-  a.out[g * kHeadDim + 32 + lane] = __float2half_rn(B1 * inv);
+  a.out[g * kHeadDim + lane] = store_elem(B0 * inv, a.dtype);
+  a.out[g * kHeadDim + 32 + lane] = store_elem(B1 * inv, a.dtype);
 }
 
 // Writes a finished (m, l, acc) for segment g: the fp16 output, or the
@@ -273,8 +273,8 @@ __device__ __forceinline__ void finish_segment(const DecodeArgs &a, size_t g,
     }
   } else {
     const float inv = L > 0.f ? 1.f / L : 0.f;
-    a.out[g * kHeadDim + lane] = __float2half_rn(A0 * inv);
-    a.out[g * kHeadDim + 32 + lane] = __float2half_rn(A1 * inv);
+    a.out[g * kHeadDim + lane] = store_elem(A0 * inv, a.dtype);
+    a.out[g * kHeadDim + 32 + lane] = store_elem(A1 * inv, a.dtype);
   }
 }
 
@@ -540,6 +540,7 @@ __device__ void produce(const DecodeArgs &a, int nseg, int seg_per_plane,
     }
 }
 
+template <typename Dt>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     decode_kernel(const DecodeArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -618,10 +619,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       }
       const uint4 qv = *reinterpret_cast<const uint4 *>(
           a.q + static_cast<size_t>(cur_g) * kHeadDim + sub * 8);
-      const __half2 *qh = reinterpret_cast<const __half2 *>(&qv);
+      const uint32_t *qh = reinterpret_cast<const uint32_t *>(&qv);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float2 f = __half22float2(qh[e]);
+        const float2 f = Dt::unpack2(qh[e]);
         qf[2 * e] = f.x * a.scale_log2;
         qf[2 * e + 1] = f.y * a.scale_log2;
       }
@@ -650,10 +651,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         float d = 0.f;
         if (row < hd.n) {
           const uint4 kv = ld_shared_v4(kb + row * kRowBytes + sub * 16);
-          const __half2 *kh = reinterpret_cast<const __half2 *>(&kv);
+          const uint32_t *kh = reinterpret_cast<const uint32_t *>(&kv);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const float2 f = __half22float2(kh[e]);
+            const float2 f = Dt::unpack2(kh[e]);
             d = fmaf(qf[2 * e], f.x, d);
             d = fmaf(qf[2 * e + 1], f.y, d);
           }
@@ -688,10 +689,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         const int row = row_base + 4 * i;
         if (row < hd.n) {
           const uint4 vv = ld_shared_v4(vb + row * kRowBytes + sub * 16);
-          const __half2 *vh = reinterpret_cast<const __half2 *>(&vv);
+          const uint32_t *vh = reinterpret_cast<const uint32_t *>(&vv);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const float2 f = __half22float2(vh[e]);
+            const float2 f = Dt::unpack2(vh[e]);
             acc[2 * e] = fmaf(p[i], f.x, acc[2 * e]);
             acc[2 * e + 1] = fmaf(p[i], f.y, acc[2 * e + 1]);
           }
@@ -776,8 +777,10 @@ __global__ void __launch_bounds__(kHeadDim)
 
 }  // namespace decode
 
-const void *decode_kernel_ptr() {
-  return reinterpret_cast<const void *>(decode::decode_kernel);
+const void *decode_kernel_ptr(int dtype) {
+  return dtype == FA_DTYPE_BF16
+             ? reinterpret_cast<const void *>(decode::decode_kernel<BF16>)
+             : reinterpret_cast<const void *>(decode::decode_kernel<F16>);
 }
 int decode_threads() { return decode::kThreads; }
 int decode_smem_bytes() { return static_cast<int>(decode::kSmemBytes); }
@@ -785,8 +788,9 @@ int decode_ctas_per_sm() { return decode::kCtasPerSm; }
 int decode_min_rows_per_cta() { return decode::kMinRowsPerCta; }
 
 cudaError_t launch_decode_kernel(const DecodeArgs &args, cudaStream_t stream) {
-  decode::decode_kernel<<<args.grid, decode::kThreads, decode::kSmemBytes,
-                          stream>>>(args);
+  auto kernel = args.dtype == FA_DTYPE_BF16 ? decode::decode_kernel<BF16>
+                                            : decode::decode_kernel<F16>;
+  kernel<<<args.grid, decode::kThreads, decode::kSmemBytes, stream>>>(args);
   return cudaGetLastError();
 }
 

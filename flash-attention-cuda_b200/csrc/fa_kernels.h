@@ -6,27 +6,30 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "fa_b200.h"
+
 namespace fa {
 
 // ---- prefill (prefill_sm100.cu) -------------------------------------------
-const void *prefill_kernel_ptr();
+const void *prefill_kernel_ptr(int dtype = FA_DTYPE_F16);
 int prefill_threads();
 int prefill_smem_bytes();
 cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
                                   const CUtensorMap &tm_k,
                                   const CUtensorMap &tm_v, __half *out, int B,
                                   int H, int N, bool causal, float scale,
-                                  int H_kv, int sms, cudaStream_t stream);
+                                  int H_kv, int sms, int dtype,
+                                  cudaStream_t stream);
 
 // ---- prefill, head_dim 128 (prefill_d128_sm100.cu) -------------------------
-const void *prefill_d128_kernel_ptr();
+const void *prefill_d128_kernel_ptr(int dtype = FA_DTYPE_F16);
 int prefill_d128_smem_bytes();
 cudaError_t launch_prefill_d128_kernel(const CUtensorMap &tm_q,
                                        const CUtensorMap &tm_k,
                                        const CUtensorMap &tm_v, __half *out,
                                        int B, int H, int N, bool causal,
                                        float scale, int H_kv, int sms,
-                                       cudaStream_t stream);
+                                       int dtype, cudaStream_t stream);
 
 // ---- decode (decode_sm100.cu) ---------------------------------------------
 struct DecodeArgs {
@@ -58,11 +61,12 @@ struct DecodeArgs {
   float scale_log2;
   long long rows_per_cta;  // 0: balance the valid rows over the grid
   int grid;
+  int dtype;  // FA_DTYPE_F16 or FA_DTYPE_BF16 (q, caches, new rows, out)
 };
 
 constexpr int kPartialFloats = 68;  // m, l, pad, pad, acc[64]
 
-const void *decode_kernel_ptr();
+const void *decode_kernel_ptr(int dtype = FA_DTYPE_F16);
 int decode_threads();
 int decode_smem_bytes();
 int decode_ctas_per_sm();
@@ -74,7 +78,7 @@ cudaError_t launch_decode_kernel(const DecodeArgs &args, cudaStream_t stream);
 // decode_gqa_max_heads() query heads).
 // (decode_gqa_sm100.cu) head_dim 64 or 128; K/V TMA boxes of
 // decode_gqa_box_rows(head_dim) rows; partials of 4 + head_dim floats.
-const void *decode_gqa_kernel_ptr(int head_dim);
+const void *decode_gqa_kernel_ptr(int head_dim, int dtype = FA_DTYPE_F16);
 int decode_gqa_smem_bytes(int head_dim);
 int decode_gqa_max_heads();
 int decode_gqa_box_rows(int head_dim);
@@ -85,7 +89,7 @@ cudaError_t launch_decode_gqa_kernel(const DecodeArgs &args,
 
 // head_dim 128 per-head decode (decode_d128_sm100.cu); partials are
 // decode_d128_partial_floats() = 132 floats, grid as decode_kernel's.
-const void *decode_d128_kernel_ptr();
+const void *decode_d128_kernel_ptr(int dtype = FA_DTYPE_F16);
 int decode_d128_smem_bytes();
 int decode_d128_partial_floats();
 cudaError_t launch_decode_d128_kernel(const DecodeArgs &args,

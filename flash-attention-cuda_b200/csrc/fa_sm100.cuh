@@ -9,6 +9,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
 
@@ -317,13 +318,15 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
          (static_cast<uint64_t>(2u) << 61);         // SWIZZLE_128B
 }
 
-// Instruction descriptor for kind::f16 with fp16 A/B and fp32 accumulate.
-//   bits 4-5 D format (1 = f32), 7-9 A format (0 = f16), 10-12 B format,
-//   bit 15 A major (0 = K), bit 16 B major (1 = MN), 17-22 N >> 3,
-//   24-28 M >> 4.
+// Instruction descriptor for kind::f16 with 16-bit A/B and fp32 accumulate.
+//   bits 4-5 D format (1 = f32), 7-9 A format (0 = f16, 1 = bf16), 10-12 B
+//   format (A and B always the same here), bit 15 A major (0 = K), bit 16 B
+//   major (1 = MN), 17-22 N >> 3, 24-28 M >> 4.
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n,
-                                                     bool b_mn_major) {
-  return (1u << 4) | (static_cast<uint32_t>(b_mn_major) << 16) |
+                                                     bool b_mn_major,
+                                                     uint32_t fmt = 0) {
+  return (1u << 4) | (fmt << 7) | (fmt << 10) |
+         (static_cast<uint32_t>(b_mn_major) << 16) |
          (static_cast<uint32_t>(n >> 3) << 17) |
          (static_cast<uint32_t>(m >> 4) << 24);
 }
@@ -349,6 +352,17 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t addr,
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
       : "r"(addr)
       : "memory");
+}
+
+// D (16x8 fp32) += A (16x16 bf16, row) * B (16x8 bf16, col).
+__device__ __forceinline__ void mma_16816_bf16(float (&d)[4],
+                                               const uint32_t (&a)[4],
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
+      "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
 // D (16x8 fp32) += A (16x16 fp16, row) * B (16x8 fp16, col).
@@ -419,6 +433,53 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t *>(&h);
+}
+
+// ---------------------------------------------------------------------------
+// 16-bit element types. Tensors are 16-bit storage either way (the kernels'
+// pointers are typed __half); the element type decides how values convert
+// to and from fp32 and which format the tensor cores are given. Both MMA
+// operands always have the same type.
+// ---------------------------------------------------------------------------
+struct F16 {
+  static constexpr int kDtype = FA_DTYPE_F16;
+  static constexpr uint32_t kFmt = 0;  // instruction-descriptor format
+  __device__ static __forceinline__ uint32_t pack2(float lo, float hi) {
+    return pack_half2(lo, hi);
+  }
+  __device__ static __forceinline__ float2 unpack2(uint32_t w) {
+    return __half22float2(*reinterpret_cast<const __half2 *>(&w));
+  }
+  __device__ static __forceinline__ void mma16816(float (&d)[4],
+                                                  const uint32_t (&a)[4],
+                                                  uint32_t b0, uint32_t b1) {
+    mma_16816(d, a, b0, b1);
+  }
+};
+
+struct BF16 {
+  static constexpr int kDtype = FA_DTYPE_BF16;
+  static constexpr uint32_t kFmt = 1;
+  __device__ static __forceinline__ uint32_t pack2(float lo, float hi) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&h);
+  }
+  __device__ static __forceinline__ float2 unpack2(uint32_t w) {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w));
+  }
+  __device__ static __forceinline__ void mma16816(float (&d)[4],
+                                                  const uint32_t (&a)[4],
+                                                  uint32_t b0, uint32_t b1) {
+    mma_16816_bf16(d, a, b0, b1);
+  }
+};
+
+// One output element in the tensor's 16-bit storage (run-time type: the
+// rarely executed output paths of the decode kernels).
+__device__ __forceinline__ __half store_elem(float x, int dtype) {
+  return dtype == FA_DTYPE_BF16
+             ? __ushort_as_half(__bfloat16_as_ushort(__float2bfloat16_rn(x)))
+             : __float2half_rn(x);
 }
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a,

@@ -78,31 +78,35 @@ constexpr uint32_t kTmemS = 0;    // + 64 * tile
 constexpr uint32_t kTmemO = 128;  // + 128 * tile
 constexpr uint32_t kTmemP = 384;  // + 32 * tile
 
-constexpr uint32_t kIdescS = idesc_f16_f32(kBlockM, kBlockN, false);
-constexpr uint32_t kIdescPV = idesc_f16_f32(kBlockM, kD, true);
+template <typename Dt>
+constexpr uint32_t kIdescS = idesc_f16_f32(kBlockM, kBlockN, false, Dt::kFmt);
+template <typename Dt>
+constexpr uint32_t kIdescPV = idesc_f16_f32(kBlockM, kD, true, Dt::kFmt);
 constexpr float kRescaleThreshold = 8.0f;
 constexpr int kMufuPairsOf4 = 2;
 
 // S = Q K^T for one 128x64 tile: 8 MMAs of K=16; steps 0-3 read the first
 // 64-dim half of Q and K, steps 4-7 the second half (a separate block).
+template <typename Dt>
 __device__ __forceinline__ void issue_s_tile(uint32_t d, uint64_t q_desc,
                                              uint64_t k_desc) {
 #pragma unroll
   for (int kk = 0; kk < kD / 16; ++kk) {
     const uint64_t off_q = (kk >> 2) * (kQHalf >> 4) + 2 * (kk & 3);
     const uint64_t off_k = (kk >> 2) * (kKVHalf >> 4) + 2 * (kk & 3);
-    mma_f16_ss(d, q_desc + off_q, k_desc + off_k, kIdescS, kk > 0 ? 1u : 0u);
+    mma_f16_ss(d, q_desc + off_q, k_desc + off_k, kIdescS<Dt>, kk > 0 ? 1u : 0u);
   }
 }
 
 // O (+)= P V for one tile: 4 MMAs of K=16 keys, N=128 head dims. V is the
 // MN-major B operand whose two 64-dim halves are kKVHalf bytes apart (the
 // descriptor's leading byte offset); each step advances 16 rows.
+template <typename Dt>
 __device__ __forceinline__ void issue_pv_tile(uint32_t d, uint32_t p_tmem,
                                               uint64_t v_desc, bool accumulate) {
 #pragma unroll
   for (int kk = 0; kk < kBlockN / 16; ++kk)
-    mma_f16_ts(d, p_tmem + 8 * kk, v_desc + 128 * kk, kIdescPV,
+    mma_f16_ts(d, p_tmem + 8 * kk, v_desc + 128 * kk, kIdescPV<Dt>,
                (accumulate || kk > 0) ? 1u : 0u);
 }
 
@@ -135,6 +139,7 @@ __device__ __forceinline__ TileInfo tile_info(int pair, int t, int N,
   return ti;
 }
 
+template <typename Dt>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_d128_kernel(const __grid_constant__ CUtensorMap tm_q,
                         const __grid_constant__ CUtensorMap tm_k,
@@ -264,7 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (leader) {
           for (int t = 0; t < kTilesPerCta; ++t) {
             if (n_t[t] == 0) continue;
-            issue_s_tile(tmem + kTmemS + 64 * t,
+            issue_s_tile<Dt>(tmem + kTmemS + 64 * t,
                          desc0 + ((kQOff + t * kQTile) >> 4),
                          desc0 + (kKOff >> 4));
             mma_commit(&bars[kBarSFull + t]);
@@ -293,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tc_fence_after();
             if (leader) {
-              issue_s_tile(tmem + kTmemS + 64 * t,
+              issue_s_tile<Dt>(tmem + kTmemS + 64 * t,
                            desc0 + ((kQOff + t * kQTile) >> 4),
                            desc0 + ((kKOff + s1 * kKVTile) >> 4));
               mma_commit(&bars[kBarSFull + t]);
@@ -306,7 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           if (leader) {
-            issue_pv_tile(tmem + kTmemO + 128 * t, tmem + kTmemP + 32 * t,
+            issue_pv_tile<Dt>(tmem + kTmemO + 128 * t, tmem + kTmemP + 32 * t,
                           vdesc0 + ((kVOff + s * kKVTile) >> 4), j > 0);
             mma_commit(&bars[kBarODone + t]);
           }
@@ -409,7 +414,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
         }
         rs[(c >> 1) & 3] = fadd2(rs[(c >> 1) & 3], p);
-        pk[c >> 1] = pack_half2(p.x, p.y);
+        pk[c >> 1] = Dt::pack2(p.x, p.y);
       }
       const float2 rsum = fadd2(fadd2(rs[0], rs[1]), fadd2(rs[2], rs[3]));
       l_sum += rsum.x + rsum.y;
@@ -455,13 +460,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int c = 0; c < 4; ++c) {
               const uint32_t *src = &o[c * 8];
               uint4 v;
-              v.x = pack_half2(__uint_as_float(src[0]) * inv_l,
+              v.x = Dt::pack2(__uint_as_float(src[0]) * inv_l,
                                __uint_as_float(src[1]) * inv_l);
-              v.y = pack_half2(__uint_as_float(src[2]) * inv_l,
+              v.y = Dt::pack2(__uint_as_float(src[2]) * inv_l,
                                __uint_as_float(src[3]) * inv_l);
-              v.z = pack_half2(__uint_as_float(src[4]) * inv_l,
+              v.z = Dt::pack2(__uint_as_float(src[4]) * inv_l,
                                __uint_as_float(src[5]) * inv_l);
-              v.w = pack_half2(__uint_as_float(src[6]) * inv_l,
+              v.w = Dt::pack2(__uint_as_float(src[6]) * inv_l,
                                __uint_as_float(src[7]) * inv_l);
               dst[4 * h + c] = v;
             }
@@ -483,8 +488,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace prefill128
 
-const void *prefill_d128_kernel_ptr() {
-  return reinterpret_cast<const void *>(prefill128::prefill_d128_kernel);
+const void *prefill_d128_kernel_ptr(int dtype) {
+  return dtype == FA_DTYPE_BF16
+             ? reinterpret_cast<const void *>(
+                   prefill128::prefill_d128_kernel<BF16>)
+             : reinterpret_cast<const void *>(
+                   prefill128::prefill_d128_kernel<F16>);
 }
 int prefill_d128_smem_bytes() {
   return static_cast<int>(prefill128::kSmemBytes);
@@ -495,7 +504,7 @@ cudaError_t launch_prefill_d128_kernel(const CUtensorMap &tm_q,
                                        const CUtensorMap &tm_v, __half *out,
                                        int B, int H, int N, bool causal,
                                        float scale, int H_kv, int sms,
-                                       cudaStream_t stream) {
+                                       int dtype, cudaStream_t stream) {
   const int BH = B * H;
   const int n_qt = (N + prefill128::kBlockM - 1) / prefill128::kBlockM;
   const int n_pairs =
@@ -506,8 +515,9 @@ cudaError_t launch_prefill_d128_kernel(const CUtensorMap &tm_q,
   // One wave of CTAs: zig-zag pairs of equal causal work, so the kernel
   // does not wait on the heaviest pair. Several waves: heaviest first.
   const int zigzag = causal && grid <= static_cast<unsigned>(sms) ? 2 : 0;
-  prefill128::prefill_d128_kernel<<<grid, prefill128::kThreads,
-                                    prefill128::kSmemBytes, stream>>>(
+  auto kernel = dtype == FA_DTYPE_BF16 ? prefill128::prefill_d128_kernel<BF16>
+                                       : prefill128::prefill_d128_kernel<F16>;
+  kernel<<<grid, prefill128::kThreads, prefill128::kSmemBytes, stream>>>(
       tm_q, tm_k, tm_v, out, N, BH, (causal ? 1 : 0) | zigzag, scale_log2, H,
       H / H_kv);
   return cudaGetLastError();

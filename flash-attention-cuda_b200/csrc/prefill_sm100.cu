@@ -79,8 +79,10 @@ constexpr uint32_t kTmemS = 0;    // + 128 * tile
 constexpr uint32_t kTmemO = 256;  // + 64 * tile
 constexpr uint32_t kTmemP = 384;  // + 64 * tile
 
-constexpr uint32_t kIdescS = idesc_f16_f32(kBlockM, kBlockN, false);
-constexpr uint32_t kIdescPV = idesc_f16_f32(kBlockM, kHeadDim, true);
+template <typename Dt>
+constexpr uint32_t kIdescS = idesc_f16_f32(kBlockM, kBlockN, false, Dt::kFmt);
+template <typename Dt>
+constexpr uint32_t kIdescPV = idesc_f16_f32(kBlockM, kHeadDim, true, Dt::kFmt);
 
 // The max is only moved (and O rescaled) when a row's running max grows by
 // more than this many powers of two; until then exponents are taken against
@@ -94,20 +96,22 @@ constexpr int kMufuPairsOf4 = 2;
 
 // S = Q K^T for one 128x128 tile: 4 MMAs of K=16 (32 bytes further along
 // the swizzled 128-byte rows each).
+template <typename Dt>
 __device__ __forceinline__ void issue_s_tile(uint32_t d, uint64_t q_desc,
                                              uint64_t k_desc) {
 #pragma unroll
   for (int kk = 0; kk < kHeadDim / 16; ++kk)
-    mma_f16_ss(d, q_desc + 2 * kk, k_desc + 2 * kk, kIdescS, kk > 0 ? 1u : 0u);
+    mma_f16_ss(d, q_desc + 2 * kk, k_desc + 2 * kk, kIdescS<Dt>, kk > 0 ? 1u : 0u);
 }
 
 // O (+)= P V for one tile: 8 MMAs of K=16 keys. P is read from tensor memory
 // (8 columns = 16 fp16 per step); V steps by 16 rows = 2048 bytes.
+template <typename Dt>
 __device__ __forceinline__ void issue_pv_tile(uint32_t d, uint32_t p_tmem,
                                               uint64_t v_desc, bool accumulate) {
 #pragma unroll
   for (int kk = 0; kk < kBlockN / 16; ++kk)
-    mma_f16_ts(d, p_tmem + 8 * kk, v_desc + 128 * kk, kIdescPV,
+    mma_f16_ts(d, p_tmem + 8 * kk, v_desc + 128 * kk, kIdescPV<Dt>,
                (accumulate || kk > 0) ? 1u : 0u);
 }
 
@@ -131,6 +135,7 @@ __device__ __forceinline__ TileInfo tile_info(int pair, int t, int N,
   return ti;
 }
 
+template <typename Dt>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
                    const __grid_constant__ CUtensorMap tm_k,
@@ -267,11 +272,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       if (leader) {
         if (n0 > 0) {
-          issue_s_tile(tmem + kTmemS, desc0 + (kQOff >> 4), desc0 + (kKOff >> 4));
+          issue_s_tile<Dt>(tmem + kTmemS, desc0 + (kQOff >> 4), desc0 + (kKOff >> 4));
           mma_commit(&bars[kBarSFull + 0]);
         }
         if (n1 > 0) {
-          issue_s_tile(tmem + kTmemS + 128, desc0 + ((kQOff + kTileBytes) >> 4),
+          issue_s_tile<Dt>(tmem + kTmemS + 128, desc0 + ((kQOff + kTileBytes) >> 4),
                        desc0 + (kKOff >> 4));
           mma_commit(&bars[kBarSFull + 1]);
         }
@@ -302,7 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           FA_TRACE_EVENT(2048 + j * 16 + t * 8 + 3);
           tc_fence_after();
           if (leader) {
-            issue_s_tile(tmem + kTmemS + 128 * t,
+            issue_s_tile<Dt>(tmem + kTmemS + 128 * t,
                          desc0 + ((kQOff + t * kTileBytes) >> 4),
                          desc0 + ((kKOff + s1 * kTileBytes) >> 4));
             mma_commit(&bars[kBarSFull + t]);
@@ -317,7 +322,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         FA_TRACE_EVENT(2048 + j * 16 + t * 8 + 4);
         tc_fence_after();
         if (leader) {
-          issue_pv_tile(tmem + kTmemO + 64 * t, tmem + kTmemP + 64 * t,
+          issue_pv_tile<Dt>(tmem + kTmemO + 64 * t, tmem + kTmemP + 64 * t,
                         desc0 + ((kVOff + s * kTileBytes) >> 4), j > 0);
           mma_commit(&bars[kBarODone + t]);
         }
@@ -438,7 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
         }
         rs[(c >> 1) & 3] = fadd2(rs[(c >> 1) & 3], p);
-        pk[c >> 6][(c >> 1) & 31] = pack_half2(p.x, p.y);
+        pk[c >> 6][(c >> 1) & 31] = Dt::pack2(p.x, p.y);
       }
       const float2 rsum = fadd2(fadd2(rs[0], rs[1]), fadd2(rs[2], rs[3]));
       l_sum += rsum.x + rsum.y;
@@ -489,13 +494,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int c = 0; c < 8; ++c) {
             uint4 v;
             const uint32_t *src = &o[c >> 2][(c & 3) * 8];
-            v.x = pack_half2(__uint_as_float(src[0]) * inv_l,
+            v.x = Dt::pack2(__uint_as_float(src[0]) * inv_l,
                              __uint_as_float(src[1]) * inv_l);
-            v.y = pack_half2(__uint_as_float(src[2]) * inv_l,
+            v.y = Dt::pack2(__uint_as_float(src[2]) * inv_l,
                              __uint_as_float(src[3]) * inv_l);
-            v.z = pack_half2(__uint_as_float(src[4]) * inv_l,
+            v.z = Dt::pack2(__uint_as_float(src[4]) * inv_l,
                              __uint_as_float(src[5]) * inv_l);
-            v.w = pack_half2(__uint_as_float(src[6]) * inv_l,
+            v.w = Dt::pack2(__uint_as_float(src[6]) * inv_l,
                              __uint_as_float(src[7]) * inv_l);
             dst[c] = v;
           }
@@ -516,8 +521,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace prefill
 
-const void *prefill_kernel_ptr() {
-  return reinterpret_cast<const void *>(prefill::prefill_kernel);
+const void *prefill_kernel_ptr(int dtype) {
+  return dtype == FA_DTYPE_BF16
+             ? reinterpret_cast<const void *>(prefill::prefill_kernel<BF16>)
+             : reinterpret_cast<const void *>(prefill::prefill_kernel<F16>);
 }
 int prefill_threads() { return prefill::kThreads; }
 int prefill_smem_bytes() { return static_cast<int>(prefill::kSmemBytes); }
@@ -526,7 +533,8 @@ cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
                                   const CUtensorMap &tm_k,
                                   const CUtensorMap &tm_v, __half *out, int B,
                                   int H, int N, bool causal, float scale,
-                                  int H_kv, int sms, cudaStream_t stream) {
+                                  int H_kv, int sms, int dtype,
+                                  cudaStream_t stream) {
   static_assert(prefill::kBlockM == prefill::kBlockN,
                 "causal tile skipping assumes square tiles");
   const int BH = B * H;
@@ -538,10 +546,11 @@ cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
   // One wave of CTAs: zig-zag pairs of equal causal work, so the kernel
   // does not wait on the heaviest pair. Several waves: heaviest first.
   const int zigzag = causal && grid <= static_cast<unsigned>(sms) ? 2 : 0;
-  prefill::prefill_kernel<<<grid, prefill::kThreads, prefill::kSmemBytes,
-                            stream>>>(tm_q, tm_k, tm_v, out, N, BH,
-                                      (causal ? 1 : 0) | zigzag, scale_log2, H,
-                                      H / H_kv);
+  auto kernel = dtype == FA_DTYPE_BF16 ? prefill::prefill_kernel<BF16>
+                                       : prefill::prefill_kernel<F16>;
+  kernel<<<grid, prefill::kThreads, prefill::kSmemBytes, stream>>>(
+      tm_q, tm_k, tm_v, out, N, BH, (causal ? 1 : 0) | zigzag, scale_log2, H,
+      H / H_kv);
   return cudaGetLastError();
 }
 

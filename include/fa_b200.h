@@ -37,6 +37,11 @@ extern "C" {
 #define FA_ERR_TIMEOUT 1u   /* a pipeline wait exceeded its time limit   */
 #define FA_ERR_SMEM_ALIGN 2u /* dynamic shared memory was not 1 KiB aligned */
 
+/* Element types of q/k/v/o and the caches for the _ex entry points (every
+ * other entry point is fp16). */
+#define FA_DTYPE_F16 0
+#define FA_DTYPE_BF16 1
+
 /* head_dim every kernel is built for (reference flash_common.h:11). */
 #define FA_HEAD_DIM 64
 
@@ -71,6 +76,20 @@ int fa_prefill_gqa(const void *q, const void *k, const void *v, void *o, int B,
  */
 int fa_prefill_hd(const void *q, const void *k, const void *v, void *o, int B,
                   int H, int H_kv, int N, int head_dim, int causal,
+                  float scale, void *stream);
+
+/*
+ * Prefill for either 16-bit element type: q, k, v, o are fp16
+ * (dtype = FA_DTYPE_F16) or bf16 (FA_DTYPE_BF16), all the same type, with
+ * the shapes of fa_prefill_hd (head_dim 64 or 128, grouped K/V heads). The
+ * arithmetic is the same (fp32 scores, accumulators and softmax); with bf16
+ * the probabilities P enter the PV product as bf16 and O is rounded to
+ * bf16. fa_prefill_hd is this call with FA_DTYPE_F16. The reference is
+ * fp16-only and names bf16 as a next variant (README.md:229-231,397); no
+ * reference counterpart.
+ */
+int fa_prefill_ex(const void *q, const void *k, const void *v, void *o, int B,
+                  int H, int H_kv, int N, int head_dim, int dtype, int causal,
                   float scale, void *stream);
 
 /*
@@ -134,6 +153,26 @@ int fa_decode(const void *q, const void *k_cache, const void *v_cache,
               float scale, int split_size, void *workspace,
               size_t workspace_bytes, uint32_t *counters,
               size_t counter_count, void *stream);
+
+/*
+ * Decode for either 16-bit element type: q (B, H, 1, head_dim), caches
+ * (B, H_kv, S_max, head_dim) and o, all fp16 (FA_DTYPE_F16) or all bf16
+ * (FA_DTYPE_BF16); head_dim 64 or 128; H % H_kv == 0 (grouped K/V heads
+ * read once per group). Automatic length-balanced split; seq_lens, clamping
+ * and empty sequences as fa_decode. Scratch from
+ * fa_decode_ex_workspace_bytes, counters as fa_decode (B * H, zero before
+ * the first call, left at zero). No reference counterpart (the reference is
+ * fp16-only; bf16 is its named next variant, README.md:229-231,397).
+ */
+int fa_decode_ex(const void *q, const void *k_cache, const void *v_cache,
+                 const int32_t *seq_lens, void *o, int B, int H, int H_kv,
+                 int S_max, int head_dim, int dtype, float scale,
+                 void *workspace, size_t workspace_bytes, uint32_t *counters,
+                 size_t counter_count, void *stream);
+
+/* Scratch bytes fa_decode_ex needs (the same for both element types). */
+size_t fa_decode_ex_workspace_bytes(int B, int H, int H_kv, int S_max,
+                                    int head_dim, int device);
 
 /*
  * Scratch bytes fa_decode_gqa needs for this shape (0 on invalid arguments).

@@ -223,3 +223,21 @@ def test_prefill_host_plan_and_validation(lib):
                                ws, None) == FA_EINVAL
     assert lib.fa_prefill_host(p, p, p, p, 1, 2, 2, 256, 64, 1, math.inf, p,
                                ws, None) == FA_EINVAL
+
+
+def test_dtype_entry_points_reject_bad_arguments_without_a_device(lib):
+    vp, ci = ctypes.c_void_p, ctypes.c_int
+    p = ctypes.c_void_p(4096)
+    lib.fa_prefill_ex.argtypes = [vp] * 4 + [ci] * 7 + [ctypes.c_float, vp]
+    lib.fa_decode_ex.argtypes = [vp] * 5 + [ci] * 6 + [
+        ctypes.c_float, vp, ctypes.c_size_t, vp, ctypes.c_size_t, vp]
+    # dtype codes: 0 fp16, 1 bf16; anything else is rejected
+    assert lib.fa_prefill_ex(p, p, p, p, 1, 2, 2, 16, 64, 2, 1, 0.1, None) == FA_EINVAL
+    assert lib.fa_prefill_ex(p, p, p, p, 1, 2, 2, 16, 96, 1, 1, 0.1, None) == FA_EINVAL
+    assert lib.fa_prefill_ex(p, p, p, p, 1, 6, 4, 16, 128, 1, 1, 0.1, None) == FA_EINVAL
+    odd = ctypes.c_void_p(4096 + 8)
+    assert lib.fa_prefill_ex(p, p, odd, p, 1, 2, 2, 16, 64, 1, 1, 0.1, None) == FA_EALIGN
+    assert lib.fa_decode_ex(p, p, p, p, p, 1, 2, 2, 8, 64, -1, 0.1, p, 1 << 20,
+                            p, 2, None) == FA_EINVAL
+    assert lib.fa_decode_ex(p, p, p, p, None, 1, 2, 2, 8, 64, 1, 0.1, p, 1 << 20,
+                            p, 2, None) == FA_EINVAL
