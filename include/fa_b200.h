@@ -1,5 +1,7 @@
 /*
- * fa_b200.h — C ABI of the B200 (sm_100a) head_dim-64 fp16 attention forward.
+ * fa_b200.h — C ABI of the B200 (sm_100a) attention forward: head_dim 64
+ * fp16 as in the reference, plus head_dim 128, grouped K/V heads and bf16
+ * through the entry points that say so.
  *
  * Every entry point takes plain device pointers (fa_prefill_host: host
  * pointers for q/k/v/o), sizes and a cudaStream_t passed as void*. No entry
@@ -8,8 +10,9 @@
  * other host language bind these symbols directly.
  *
  * Tensor layout (identical to the reference's pybind contract): every
- * q/k/v/o/cache tensor is a contiguous (B, H, rows, 64) fp16 array; row r of
- * head (b, h) starts at element ((b * H + h) * rows + r) * 64.
+ * q/k/v/o/cache tensor is a contiguous (B, H, rows, head_dim) array of
+ * 16-bit elements (fp16 unless an entry point takes a dtype); row r of head
+ * (b, h) starts at element ((b * H + h) * rows + r) * head_dim.
  *
  * Return value of every int-returning call: FA_OK (0) or one FA_E* code;
  * fa_status_string() names it. Argument errors are detected on the host
