@@ -364,9 +364,11 @@ at::Tensor decode_append(const at::Tensor &q, const at::Tensor &k_new,
                          at::Tensor v_cache, const at::Tensor &seq_lens,
                          double scale) {
   check_decode_inputs(q, k_cache, v_cache, seq_lens, scale);
-  TORCH_CHECK(q.scalar_type() == at::kHalf, "decode_append needs fp16 tensors");
   check_bhnd_any(k_new, "k_new");
   check_bhnd_any(v_new, "v_new");
+  TORCH_CHECK(k_new.scalar_type() == q.scalar_type() &&
+                  v_new.scalar_type() == q.scalar_type(),
+              "k_new and v_new must have the dtype of q and the caches");
   TORCH_CHECK(k_new.sizes() == v_new.sizes() && k_new.size(0) == k_cache.size(0) &&
                   k_new.size(1) == k_cache.size(1) && k_new.size(2) == 1 &&
                   k_new.size(3) == k_cache.size(3),
@@ -386,10 +388,11 @@ at::Tensor decode_append(const at::Tensor &q, const at::Tensor &k_new,
   TORCH_CHECK(bytes > 0, "fa_decode_gqa_workspace_bytes failed");
   DecodeScratch &ws = decode_scratch(q, bytes, static_cast<size_t>(B) * H);
   check_status(
-      fa_decode_append_hd(q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(),
+      fa_decode_append_ex(q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(),
                        k_cache.data_ptr(), v_cache.data_ptr(),
                        seq_lens.data_ptr<int32_t>(), o.data_ptr(), B, H, H_kv,
-                       S, D, static_cast<float>(scale), ws.partials.data_ptr(),
+                       S, D, dtype_code(q), static_cast<float>(scale),
+                       ws.partials.data_ptr(),
                        static_cast<size_t>(ws.partials.numel()),
                        reinterpret_cast<uint32_t *>(ws.counters.data_ptr<int32_t>()),
                        static_cast<size_t>(ws.counters.numel()), current_stream()),

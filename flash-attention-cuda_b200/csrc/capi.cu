@@ -533,6 +533,25 @@ int fa_decode_append_hd(const void *q, const void *k_new, const void *v_new,
                         128);
 }
 
+int fa_decode_append_ex(const void *q, const void *k_new, const void *v_new,
+                        void *k_cache, void *v_cache, const int32_t *seq_lens,
+                        void *o, int B, int H, int H_kv, int S_max,
+                        int head_dim, int dtype, float scale, void *workspace,
+                        size_t workspace_bytes, uint32_t *counters,
+                        size_t counter_count, void *stream) {
+  if (dtype != FA_DTYPE_F16 && dtype != FA_DTYPE_BF16) return FA_EINVAL;
+  if (!o || !k_new || !v_new) return FA_EINVAL;
+  if (head_dim != FA_HEAD_DIM && head_dim != 128) return FA_EINVAL;
+  if (head_dim == 128 && H_kv == H)
+    return run_decode_d128(q, k_cache, v_cache, seq_lens, o, B, H, S_max,
+                           scale, 0, workspace, workspace_bytes, counters,
+                           counter_count, stream, k_new, v_new, dtype);
+  return run_decode_gqa(q, k_cache, v_cache, seq_lens, o, nullptr, B, H, H_kv,
+                        S_max, scale, 0, workspace, workspace_bytes, counters,
+                        counter_count, stream, k_new, v_new, nullptr, 0, 1, 0,
+                        head_dim, dtype);
+}
+
 size_t fa_decode_gqa_hd_workspace_bytes(int B, int H, int H_kv, int S_max,
                                         int head_dim, int device) {
   if (head_dim == FA_HEAD_DIM)

@@ -173,6 +173,20 @@ int fa_decode_ex(const void *q, const void *k_cache, const void *v_cache,
                  void *workspace, size_t workspace_bytes, uint32_t *counters,
                  size_t counter_count, void *stream);
 
+/*
+ * fa_decode_append_hd for either 16-bit element type (q, new rows, caches
+ * and o all fp16 or all bf16): stores each sequence's new K/V row at row
+ * seq_lens[b] of the caches and attends seq_lens[b] + 1 rows, in one
+ * launch. Scratch from fa_decode_ex_workspace_bytes. No reference
+ * counterpart (see fa_decode_append and fa_decode_ex).
+ */
+int fa_decode_append_ex(const void *q, const void *k_new, const void *v_new,
+                        void *k_cache, void *v_cache, const int32_t *seq_lens,
+                        void *o, int B, int H, int H_kv, int S_max,
+                        int head_dim, int dtype, float scale, void *workspace,
+                        size_t workspace_bytes, uint32_t *counters,
+                        size_t counter_count, void *stream);
+
 /* Scratch bytes fa_decode_ex needs (the same for both element types). */
 size_t fa_decode_ex_workspace_bytes(int B, int H, int H_kv, int S_max,
                                     int head_dim, int device);

@@ -114,6 +114,10 @@ def test_mixed_dtypes_are_rejected():
         flashattn_cuda.decode(bf(1, 2, 1, 64), q.half(), q.half(), lens, 0.1)
     with pytest.raises(RuntimeError, match="needs fp16"):
         flashattn_cuda.decode_partial(bf(1, 2, 1, 64), q, q, lens, 0.1)
+    with pytest.raises(RuntimeError, match="dtype of q"):
+        flashattn_cuda.decode_append(bf(1, 2, 1, 64),
+                                     bf(1, 2, 1, 64).half(), bf(1, 2, 1, 64),
+                                     q.clone(), q.clone(), lens, 0.1)
 
 
 def test_c_abi_bf16_entry_points():
@@ -150,3 +154,30 @@ def test_c_abi_bf16_entry_points():
         want = decode_reference(qd, kc, vc, lens.cpu(), 128 ** -0.5)
         assert (od.float() - want).abs().max().item() <= TOL
     assert int(ctr.abs().sum()) == 0
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("h,h_kv", [(12, 12), (14, 2)])
+def test_decode_append_bf16(d, h, h_kv):
+    """The new rows land at seq_lens[b] of bf16 caches (bit copies) and are
+    attended in the same launch; a full cache attends its old rows only."""
+    torch.manual_seed(d + h)
+    b, s_max = 4, 1500
+    q = bf(b, h, 1, d)
+    k, v = bf(b, h_kv, s_max, d), bf(b, h_kv, s_max, d)
+    k_new, v_new = bf(b, h_kv, 1, d), bf(b, h_kv, 1, d)
+    lens = torch.tensor([0, 700, s_max - 1, s_max], dtype=torch.int32,
+                        device="cuda")
+    k_want, v_want = k.clone(), v.clone()
+    new_lens = []
+    for i, n in enumerate(lens.tolist()):
+        if n < s_max:
+            k_want[i, :, n] = k_new[i, :, 0]
+            v_want[i, :, n] = v_new[i, :, 0]
+        new_lens.append(min(n + 1, s_max))
+    got = flashattn_cuda.decode_append(q, k_new, v_new, k, v, lens, d ** -0.5)
+    assert got.dtype == torch.bfloat16
+    assert torch.equal(k, k_want) and torch.equal(v, v_want)
+    want = decode_reference(q, k_want, v_want, new_lens, d ** -0.5)
+    assert (got.float() - want).abs().max().item() <= TOL
+    assert flashattn_cuda.take_device_error() == 0
