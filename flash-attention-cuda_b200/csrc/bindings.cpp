@@ -199,7 +199,7 @@ at::Tensor prefill_host(const at::Tensor &q, const at::Tensor &k,
                         c10::optional<at::Tensor> out, bool non_blocking) {
   for (const auto *t : {&q, &k, &v}) {
     TORCH_CHECK(t->device().is_cpu(), "prefill_host expects CPU tensors");
-    check_half(*t, "q/k/v");
+    check_16bit(*t, "q/k/v");
     check_contiguous(*t, "q/k/v");
     TORCH_CHECK(t->dim() == 4 && (t->size(3) == kHeadDim || t->size(3) == 128),
                 "q/k/v must be 4-D (B, H, N, 64 or 128), got ", t->sizes());
@@ -213,12 +213,15 @@ at::Tensor prefill_host(const at::Tensor &q, const at::Tensor &k,
               q.sizes(), " k=", k.sizes(), " v=", v.sizes());
   TORCH_CHECK(q.size(2) > 0, "sequence length must be > 0");
   TORCH_CHECK(std::isfinite(scale), "scale must be finite");
+  TORCH_CHECK(q.scalar_type() == k.scalar_type() &&
+                  q.scalar_type() == v.scalar_type(),
+              "q, k and v must have the same dtype");
   at::Tensor o;
   if (out.has_value()) {
     o = *out;
-    TORCH_CHECK(o.device().is_cpu() && o.scalar_type() == at::kHalf &&
+    TORCH_CHECK(o.device().is_cpu() && o.scalar_type() == q.scalar_type() &&
                     o.is_contiguous() && o.sizes() == q.sizes(),
-                "out must be a contiguous fp16 CPU tensor shaped like q");
+                "out must be a contiguous CPU tensor of q's dtype and shape");
   } else {
     o = at::empty(q.sizes(), q.options().pinned_memory(true));
   }
@@ -234,8 +237,9 @@ at::Tensor prefill_host(const at::Tensor &q, const at::Tensor &k,
                             .device(at::kCUDA, at::cuda::current_device())
                             .dtype(at::kByte);
   at::Tensor ws = at::empty({static_cast<int64_t>(ws_bytes)}, dev_opts);
-  check_status(fa_prefill_host(q.data_ptr(), k.data_ptr(), v.data_ptr(),
-                               o.data_ptr(), B, H, H_kv, N, D, causal ? 1 : 0,
+  check_status(fa_prefill_host_ex(q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                               o.data_ptr(), B, H, H_kv, N, D, dtype_code(q),
+                               causal ? 1 : 0,
                                static_cast<float>(scale), ws.data_ptr(),
                                ws_bytes, current_stream()),
                "fa_prefill_host");

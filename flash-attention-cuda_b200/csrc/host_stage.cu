@@ -161,6 +161,15 @@ int fa_prefill_host(const void *q, const void *k, const void *v, void *o,
                     int B, int H, int H_kv, int N, int head_dim, int causal,
                     float scale, void *workspace, size_t workspace_bytes,
                     void *stream) {
+  return fa_prefill_host_ex(q, k, v, o, B, H, H_kv, N, head_dim, FA_DTYPE_F16,
+                            causal, scale, workspace, workspace_bytes, stream);
+}
+
+int fa_prefill_host_ex(const void *q, const void *k, const void *v, void *o,
+                       int B, int H, int H_kv, int N, int head_dim, int dtype,
+                       int causal, float scale, void *workspace,
+                       size_t workspace_bytes, void *stream) {
+  if (dtype != FA_DTYPE_F16 && dtype != FA_DTYPE_BF16) return FA_EINVAL;
   HostPlan p;
   int rc = make_plan(B, H, H_kv, N, head_dim, &p);
   if (rc != FA_OK) return rc;
@@ -216,8 +225,8 @@ int fa_prefill_host(const void *q, const void *k, const void *v, void *o,
         (c >= p.slots &&
          cudaStreamWaitEvent(cs, st->out_done[r], 0) != cudaSuccess))
       return FA_ECUDA;
-    rc = fa_prefill_hd(sq, sk, sv, so, nu, p.unit_heads, 1, N, head_dim,
-                       causal, scale, stream);
+    rc = fa_prefill_ex(sq, sk, sv, so, nu, p.unit_heads, 1, N, head_dim,
+                       dtype, causal, scale, stream);
     if (rc != FA_OK) return rc;
     if (cudaEventRecord(st->computed[r], cs) != cudaSuccess ||
         cudaStreamWaitEvent(st->copy_out, st->computed[r], 0) != cudaSuccess ||

@@ -116,6 +116,13 @@ int fa_prefill_host(const void *q, const void *k, const void *v, void *o,
                     float scale, void *workspace, size_t workspace_bytes,
                     void *stream);
 
+/* fa_prefill_host for either 16-bit element type (q, k, v, o all fp16 or
+ * all bf16, dtype as fa_prefill_ex); fa_prefill_host is the fp16 case. */
+int fa_prefill_host_ex(const void *q, const void *k, const void *v, void *o,
+                       int B, int H, int H_kv, int N, int head_dim, int dtype,
+                       int causal, float scale, void *workspace,
+                       size_t workspace_bytes, void *stream);
+
 /*
  * Plan of fa_prefill_host for this shape: the number of chunks (one kernel
  * launch each) and the device workspace it needs. Host-only.

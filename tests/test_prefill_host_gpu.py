@@ -92,3 +92,16 @@ def test_prefill_host_rejects_device_tensors():
     q = torch.zeros(1, 1, 8, 64, dtype=torch.float16, device="cuda")
     with pytest.raises(RuntimeError, match="CPU tensors"):
         flashattn_cuda.prefill_host(q, q, q, True, 0.1)
+
+
+@pytest.mark.parametrize("d", [64, 128])
+def test_prefill_host_bf16(d):
+    g = torch.Generator().manual_seed(d)
+    q = torch.randn(2, 8, 1500, d, generator=g).bfloat16().pin_memory()
+    k = torch.randn(2, 2, 1500, d, generator=g).bfloat16().pin_memory()
+    v = torch.randn(2, 2, 1500, d, generator=g).bfloat16().pin_memory()
+    got = flashattn_cuda.prefill_host(q, k, v, True, d ** -0.5)
+    assert got.dtype == torch.bfloat16 and got.is_pinned()
+    want = flashattn_cuda.prefill(q.cuda(), k.cuda(), v.cuda(), True,
+                                  d ** -0.5).cpu()
+    assert torch.equal(got, want)
