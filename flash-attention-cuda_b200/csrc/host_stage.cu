@@ -200,7 +200,8 @@ int fa_prefill_host_ex(const void *q, const void *k, const void *v, void *o,
       cudaStreamWaitEvent(st->copy_out, st->start, 0) != cudaSuccess)
     return FA_ECUDA;
 
-  for (int c = 0; c < p.chunks; ++c) {
+  rc = FA_OK;
+  for (int c = 0; c < p.chunks && rc == FA_OK; ++c) {
     const int r = c % p.slots;
     int u0 = 0, nu = 0;
     chunk_range(p, c, &u0, &nu);
@@ -210,35 +211,40 @@ int fa_prefill_host_ex(const void *q, const void *k, const void *v, void *o,
     char *so = sv + kv_cap;
     const size_t qb = nu * p.unit_q, kvb = nu * p.unit_kv;
     const size_t qoff = u0 * p.unit_q, kvoff = u0 * p.unit_kv;
-    if (c >= p.slots &&
-        cudaStreamWaitEvent(st->copy_in, st->computed[r], 0) != cudaSuccess)
-      return FA_ECUDA;
-    if (cudaMemcpyAsync(sq, hq + qoff, qb, cudaMemcpyHostToDevice,
+    if ((c >= p.slots &&
+         cudaStreamWaitEvent(st->copy_in, st->computed[r], 0) != cudaSuccess) ||
+        cudaMemcpyAsync(sq, hq + qoff, qb, cudaMemcpyHostToDevice,
                         st->copy_in) != cudaSuccess ||
         cudaMemcpyAsync(sk, hk + kvoff, kvb, cudaMemcpyHostToDevice,
                         st->copy_in) != cudaSuccess ||
         cudaMemcpyAsync(sv, hv + kvoff, kvb, cudaMemcpyHostToDevice,
                         st->copy_in) != cudaSuccess ||
-        cudaEventRecord(st->in_done[r], st->copy_in) != cudaSuccess)
-      return FA_ECUDA;
-    if (cudaStreamWaitEvent(cs, st->in_done[r], 0) != cudaSuccess ||
+        cudaEventRecord(st->in_done[r], st->copy_in) != cudaSuccess ||
+        cudaStreamWaitEvent(cs, st->in_done[r], 0) != cudaSuccess ||
         (c >= p.slots &&
-         cudaStreamWaitEvent(cs, st->out_done[r], 0) != cudaSuccess))
-      return FA_ECUDA;
+         cudaStreamWaitEvent(cs, st->out_done[r], 0) != cudaSuccess)) {
+      rc = FA_ECUDA;
+      break;
+    }
     rc = fa_prefill_ex(sq, sk, sv, so, nu, p.unit_heads, 1, N, head_dim,
                        dtype, causal, scale, stream);
-    if (rc != FA_OK) return rc;
+    if (rc != FA_OK) break;
     if (cudaEventRecord(st->computed[r], cs) != cudaSuccess ||
         cudaStreamWaitEvent(st->copy_out, st->computed[r], 0) != cudaSuccess ||
         cudaMemcpyAsync(ho + qoff, so, qb, cudaMemcpyDeviceToHost,
                         st->copy_out) != cudaSuccess ||
         cudaEventRecord(st->out_done[r], st->copy_out) != cudaSuccess)
-      return FA_ECUDA;
+      rc = FA_ECUDA;
   }
-  const int last = (p.chunks - 1) % p.slots;
-  return cudaStreamWaitEvent(cs, st->out_done[last], 0) == cudaSuccess
-             ? FA_OK
-             : FA_ECUDA;
+  // The caller's stream waits for everything enqueued on both copy streams
+  // (after an error midway too), so the workspace and the host buffers are
+  // free once that stream reaches this point.
+  if (cudaEventRecord(st->in_done[0], st->copy_in) != cudaSuccess ||
+      cudaEventRecord(st->out_done[0], st->copy_out) != cudaSuccess ||
+      cudaStreamWaitEvent(cs, st->in_done[0], 0) != cudaSuccess ||
+      cudaStreamWaitEvent(cs, st->out_done[0], 0) != cudaSuccess)
+    return FA_ECUDA;
+  return rc;
 }
 
 }  // extern "C"
