@@ -448,7 +448,6 @@ at::Tensor decode_exchange(const at::Tensor &q, const at::Tensor &k_cache,
                            const at::Tensor &peers, int64_t rank,
                            int64_t world, int64_t epoch) {
   check_decode_inputs(q, k_cache, v_cache, seq_lens, scale);
-  TORCH_CHECK(q.scalar_type() == at::kHalf, "decode_exchange needs fp16 tensors");
   TORCH_CHECK(q.size(3) == kHeadDim && k_cache.size(1) == q.size(1),
               "sharded decode needs head_dim == ", kHeadDim,
               " and one K/V head per query head");
@@ -466,9 +465,9 @@ at::Tensor decode_exchange(const at::Tensor &q, const at::Tensor &k_cache,
   TORCH_CHECK(bytes > 0, "fa_decode_workspace_bytes failed");
   DecodeScratch &ws = decode_scratch(q, bytes, static_cast<size_t>(B) * H);
   check_status(
-      fa_decode_exchange(
+      fa_decode_exchange_ex(
           q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
-          seq_lens.data_ptr<int32_t>(), o.data_ptr(), B, H, S,
+          seq_lens.data_ptr<int32_t>(), o.data_ptr(), B, H, S, dtype_code(q),
           static_cast<float>(scale), ws.partials.data_ptr(),
           static_cast<size_t>(ws.partials.numel()),
           reinterpret_cast<uint32_t *>(ws.counters.data_ptr<int32_t>()),

@@ -425,6 +425,21 @@ int fa_decode_exchange(const void *q, const void *k_cache, const void *v_cache,
                         rank, world, epoch);
 }
 
+int fa_decode_exchange_ex(const void *q, const void *k_cache,
+                          const void *v_cache, const int32_t *seq_lens,
+                          void *o, int B, int H, int S_max, int dtype,
+                          float scale, void *workspace, size_t workspace_bytes,
+                          uint32_t *counters, size_t counter_count,
+                          float *const *peer_buffers, int rank, int world,
+                          uint32_t epoch, void *stream) {
+  if (dtype != FA_DTYPE_F16 && dtype != FA_DTYPE_BF16) return FA_EINVAL;
+  if (!o || !peer_buffers || epoch == 0) return FA_EINVAL;
+  return run_decode_gqa(q, k_cache, v_cache, seq_lens, o, nullptr, B, H, H,
+                        S_max, scale, 0, workspace, workspace_bytes, counters,
+                        counter_count, stream, nullptr, nullptr, peer_buffers,
+                        rank, world, epoch, FA_HEAD_DIM, dtype);
+}
+
 size_t fa_decode_hd_workspace_bytes(int B, int H, int S_max, int head_dim,
                                     int split_size, int device) {
   if (head_dim == FA_HEAD_DIM)

@@ -189,7 +189,8 @@ class PeerExchange:
 def sharded_decode_fused(q, k_local, v_local, seq_lens_local, scale, xchg):
     """sharded_decode with the combine inside the decode kernel: every rank
     passes the full q and its own KV chunk (lengths clamped to the chunk, see
-    local_seq_lens) and gets the full fp16 output from one launch."""
+    local_seq_lens) and gets the full output (fp16 or bf16, the dtype of q
+    and the cache) from one launch."""
     from . import _C
 
     if tuple(q.shape[:2]) != xchg.shape:

@@ -36,6 +36,24 @@ def test_single_rank_exchange_equals_decode():
     assert flashattn_cuda.take_device_error() == 0
 
 
+def test_single_rank_exchange_bf16_equals_decode():
+    torch.manual_seed(1)
+    b, h, s = 3, 14, 3000
+    q = torch.randn(b, h, 1, 64, device="cuda").bfloat16()
+    k, v = (torch.randn(b, h, s, 64, device="cuda").bfloat16() for _ in range(2))
+    lens = torch.tensor([3000, 17, 0], dtype=torch.int32, device="cuda")
+    xchg = fadist.PeerExchange(b, h)
+    try:
+        for _ in range(2):
+            got = fadist.sharded_decode_fused(q, k, v, lens, SCALE, xchg)
+            assert got.dtype == torch.bfloat16
+            want = flashattn_cuda.decode(q, k, v, lens, SCALE)
+            assert torch.equal(got, want)
+    finally:
+        xchg.close()
+    assert flashattn_cuda.take_device_error() == 0
+
+
 def _two_rank_worker(rank, world, port, result):
     import torch.distributed as dist
 
