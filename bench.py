@@ -496,6 +496,10 @@ def run_ours(args, rank, world, local_rank):
                         "once for its 7 query heads; L2 flushed between steps"}
             del qd, kc, vc
 
+        # ------- host cost of a small decode step: eager vs CUDA graph ------
+        if world == 1:
+            secondary["decode_step_graph"] = graph_step_measure(fa, randn)
+
         # ------- NVIDIA's library attention on the headline shape (context) --
         # cuDNN's fused attention through torch SDPA: a library kernel, timed
         # beside ours for reference only; nothing of it is on our path.
@@ -644,6 +648,44 @@ def cpu_baseline(budget_s):
             "sample": f"{heads} causal N=4096 (batch, head) evaluations, cycling "
                       f"over config 3's 56 heads, through the numpy restatement "
                       f"of src/attention_cpu.py ({secs:.1f} s)"}
+
+
+def graph_step_measure(fa, randn, calls=200):
+    """Wall time per call of 200 back-to-back tiny decode steps (B=1, H=2,
+    256 cached rows: a few us of device work, so the host's per-call cost
+    shows), launched eagerly through the Python API and as replays of a
+    captured CUDA graph."""
+    import time
+    import torch
+    q = randn(1, 2, 1, HEAD_DIM, seed=120)
+    k = randn(1, 2, 256, HEAD_DIM, seed=121)
+    v = randn(1, 2, 256, HEAD_DIM, seed=122)
+    lens = torch.tensor([256], dtype=torch.int32, device="cuda")
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        fa.decode(q, k, v, lens, SCALE)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            fa.decode(q, k, v, lens, SCALE)
+    torch.cuda.current_stream().wait_stream(side)
+
+    def per_call(fn):
+        for _ in range(20):
+            fn()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(calls):
+            fn()
+        torch.cuda.synchronize()
+        return (time.perf_counter() - t0) / calls * 1e6
+
+    eager = per_call(lambda: fa.decode(q, k, v, lens, SCALE))
+    replay = per_call(graph.replay)
+    return {"eager_us_per_call": round(eager, 2),
+            "graph_us_per_call": round(replay, 2),
+            "note": "wall clock per call, 200 calls back to back, B=1 H=2 "
+                    "S=256 decode; the graph replays one captured launch"}
 
 
 def cudnn_measure(timer, randn, steps, warmup, ours_tflops):
