@@ -171,15 +171,26 @@ GqaPlan gqa_plan(int H, int H_kv) {
   return p;
 }
 
+// Grouped decode grid: at least kGqaMinRowsPerCta cache rows per CTA, at
+// most one CTA per SM, and at most as many CTAs per segment as one round
+// of the final merge gathers (measured, B1 H14 H_kv 2 d64: 74 CTAs per
+// segment took two gather rounds and 36.9 us at S 131072, 64 took 28.7;
+// S 16384 with 1024-row pieces 20.5 us against 26.8 with 128-row pieces).
+constexpr long long kGqaMinRowsPerCta = 1024;
+
 int decode_gqa_grid(int sms, int B, const GqaPlan &p, int S_max,
-                    int split_size) {
-  const long long cap_rows = static_cast<long long>(B) * p.n_seg_per_b * S_max;
+                    int split_size, int head_dim) {
+  const long long segs = static_cast<long long>(B) * p.n_seg_per_b;
+  const long long cap_rows = segs * S_max;
   long long g;
   if (split_size > 0) {
     g = (cap_rows + split_size - 1) / split_size;
   } else {
-    g = (cap_rows + decode_min_rows_per_cta() - 1) / decode_min_rows_per_cta();
+    g = (cap_rows + kGqaMinRowsPerCta - 1) / kGqaMinRowsPerCta;
     if (g > sms) g = sms;  // one CTA per SM
+    const long long by_merge =
+        segs * decode_gqa_merge_batch(head_dim, p.heads_per_seg);
+    if (g > by_merge) g = by_merge;
   }
   return static_cast<int>(g < 1 ? 1 : g);
 }
@@ -225,7 +236,8 @@ int run_decode_gqa(const void *q, const void *k_cache, const void *v_cache,
   const bool grouped = H_kv < H;
   const GqaPlan plan = gqa_plan(H, H_kv);
   const int grid =
-      grouped ? decode_gqa_grid(g_devices[dev].sms, B, plan, S_max, split_size)
+      grouped ? decode_gqa_grid(g_devices[dev].sms, B, plan, S_max, split_size,
+                                head_dim)
               : decode_grid(g_devices[dev].sms, B, H, S_max, split_size);
   const size_t need = grouped ? gqa_workspace_bytes_for(B, plan, grid, head_dim)
                               : workspace_bytes_for(B, H, grid);
@@ -580,7 +592,8 @@ size_t fa_decode_gqa_hd_workspace_bytes(int B, int H, int H_kv, int S_max,
       cudaSuccess)
     return 0;
   const GqaPlan p = gqa_plan(H, H_kv);
-  return gqa_workspace_bytes_for(B, p, decode_gqa_grid(sms, B, p, S_max, 0), 128);
+  return gqa_workspace_bytes_for(B, p, decode_gqa_grid(sms, B, p, S_max, 0, 128),
+                                 128);
 }
 
 int fa_decode_gqa_hd(const void *q, const void *k_cache, const void *v_cache,
@@ -631,7 +644,8 @@ size_t fa_decode_gqa_workspace_bytes(int B, int H, int H_kv, int S_max,
   if (H_kv == H)
     return workspace_bytes_for(B, H, decode_grid(sms, B, H, S_max, 0));
   const GqaPlan p = gqa_plan(H, H_kv);
-  return gqa_workspace_bytes_for(B, p, decode_gqa_grid(sms, B, p, S_max, 0));
+  return gqa_workspace_bytes_for(
+      B, p, decode_gqa_grid(sms, B, p, S_max, 0, FA_HEAD_DIM));
 }
 
 int fa_decode(const void *q, const void *k_cache, const void *v_cache,

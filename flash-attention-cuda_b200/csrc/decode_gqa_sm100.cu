@@ -674,6 +674,17 @@ int decode_gqa_smem_bytes(int head_dim) {
                                           : decode::GqaCfg<64>::kSmemBytes);
 }
 int decode_gqa_max_heads() { return decode::kGqaMaxHeads; }
+int decode_gqa_merge_batch(int head_dim, int heads_per_seg) {
+  // partial records of one segment that one gather round of the final merge
+  // holds (coop_merge: the stage buffers less the per-head statistics)
+  const uint32_t bar_off = head_dim == 128 ? decode::GqaCfg<128>::kBarOff
+                                           : decode::GqaCfg<64>::kBarOff;
+  const uint32_t pf = head_dim == 128 ? decode::GqaCfg<128>::kPF
+                                      : decode::GqaCfg<64>::kPF;
+  const uint32_t gather = bar_off - 3 * decode::kGqaMaxHeads * 4;
+  const uint32_t rec = static_cast<uint32_t>(heads_per_seg) * pf * 4;
+  return rec > 0 ? static_cast<int>(gather / rec) : 1;
+}
 int decode_gqa_box_rows(int head_dim) {
   return head_dim == 128 ? decode::GqaCfg<128>::kRows
                          : decode::GqaCfg<64>::kRows;

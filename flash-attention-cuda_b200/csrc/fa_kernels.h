@@ -81,6 +81,8 @@ cudaError_t launch_decode_kernel(const DecodeArgs &args, cudaStream_t stream);
 const void *decode_gqa_kernel_ptr(int head_dim, int dtype = FA_DTYPE_F16);
 int decode_gqa_smem_bytes(int head_dim);
 int decode_gqa_max_heads();
+// Partial records of one segment one round of the final merge gathers.
+int decode_gqa_merge_batch(int head_dim, int heads_per_seg);
 int decode_gqa_box_rows(int head_dim);
 cudaError_t launch_decode_gqa_kernel(const DecodeArgs &args,
                                      const CUtensorMap &tm_k,
