@@ -405,9 +405,11 @@ at::Tensor decode_append(const at::Tensor &q, const at::Tensor &k_new,
 }
 
 // ---- sequence-sharded decode with the cross-GPU combine in the kernel ----
-size_t exchange_bytes(int64_t B, int64_t H, int64_t world) {
-  const size_t n = fa_exchange_bytes(to_int(B, "batch"), to_int(H, "heads"),
-                                     to_int(world, "world"));
+size_t exchange_bytes(int64_t B, int64_t H, int64_t world,
+                      int64_t head_dim) {
+  const size_t n = fa_exchange_bytes_hd(to_int(B, "batch"), to_int(H, "heads"),
+                                        to_int(world, "world"),
+                                        to_int(head_dim, "head_dim"));
   TORCH_CHECK(n > 0, "invalid exchange shape");
   return n;
 }
@@ -448,9 +450,8 @@ at::Tensor decode_exchange(const at::Tensor &q, const at::Tensor &k_cache,
                            const at::Tensor &peers, int64_t rank,
                            int64_t world, int64_t epoch) {
   check_decode_inputs(q, k_cache, v_cache, seq_lens, scale);
-  TORCH_CHECK(q.size(3) == kHeadDim && k_cache.size(1) == q.size(1),
-              "sharded decode needs head_dim == ", kHeadDim,
-              " and one K/V head per query head");
+  TORCH_CHECK(k_cache.size(1) == q.size(1),
+              "sharded decode needs one K/V head per query head");
   check_cuda(peers, "peers");
   TORCH_CHECK(peers.scalar_type() == at::kLong && peers.dim() == 1 &&
                   peers.size(0) == world && peers.device() == q.device(),
@@ -461,13 +462,14 @@ at::Tensor decode_exchange(const at::Tensor &q, const at::Tensor &k_cache,
   const int H = to_int(q.size(1), "heads");
   const int S = to_int(k_cache.size(2), "cache length");
   at::Tensor o = at::empty_like(q);
-  const size_t bytes = fa_decode_workspace_bytes(B, H, S, 0, q.get_device());
+  const int D = to_int(q.size(3), "head_dim");
+  const size_t bytes = fa_decode_hd_workspace_bytes(B, H, S, D, 0, q.get_device());
   TORCH_CHECK(bytes > 0, "fa_decode_workspace_bytes failed");
   DecodeScratch &ws = decode_scratch(q, bytes, static_cast<size_t>(B) * H);
   check_status(
       fa_decode_exchange_ex(
           q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
-          seq_lens.data_ptr<int32_t>(), o.data_ptr(), B, H, S, dtype_code(q),
+          seq_lens.data_ptr<int32_t>(), o.data_ptr(), B, H, S, D, dtype_code(q),
           static_cast<float>(scale), ws.partials.data_ptr(),
           static_cast<size_t>(ws.partials.numel()),
           reinterpret_cast<uint32_t *>(ws.counters.data_ptr<int32_t>()),
@@ -593,7 +595,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "Decode with the new token's K/V row stored into the cache in the same launch",
         py::arg("q"), py::arg("k_new"), py::arg("v_new"), py::arg("k_cache"),
         py::arg("v_cache"), py::arg("seq_lens"), py::arg("scale"));
-  m.def("_exchange_bytes", &exchange_bytes);
+  m.def("_exchange_bytes", &exchange_bytes, py::arg("B"), py::arg("H"),
+        py::arg("world"), py::arg("head_dim") = 64);
   m.def("_exchange_alloc", &exchange_alloc);
   m.def("_exchange_open", &exchange_open);
   m.def("_exchange_close", &exchange_close);

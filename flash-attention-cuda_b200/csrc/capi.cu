@@ -384,9 +384,14 @@ size_t fa_decode_workspace_bytes(int B, int H, int S_max, int split_size,
 }
 
 size_t fa_exchange_bytes(int B, int H, int world) {
+  return fa_exchange_bytes_hd(B, H, world, FA_HEAD_DIM);
+}
+
+size_t fa_exchange_bytes_hd(int B, int H, int world, int head_dim) {
   if (B <= 0 || H <= 0 || world <= 0 || world > 32) return 0;
+  if (head_dim != FA_HEAD_DIM && head_dim != 128) return 0;
   const size_t bh = static_cast<size_t>(B) * H;
-  return align_up(bh * world * kPartialFloats * sizeof(float) +
+  return align_up(bh * world * (4 + head_dim) * sizeof(float) +
                       bh * sizeof(uint32_t),
                   256);
 }
@@ -437,20 +442,6 @@ int fa_decode_exchange(const void *q, const void *k_cache, const void *v_cache,
                         rank, world, epoch);
 }
 
-int fa_decode_exchange_ex(const void *q, const void *k_cache,
-                          const void *v_cache, const int32_t *seq_lens,
-                          void *o, int B, int H, int S_max, int dtype,
-                          float scale, void *workspace, size_t workspace_bytes,
-                          uint32_t *counters, size_t counter_count,
-                          float *const *peer_buffers, int rank, int world,
-                          uint32_t epoch, void *stream) {
-  if (dtype != FA_DTYPE_F16 && dtype != FA_DTYPE_BF16) return FA_EINVAL;
-  if (!o || !peer_buffers || epoch == 0) return FA_EINVAL;
-  return run_decode_gqa(q, k_cache, v_cache, seq_lens, o, nullptr, B, H, H,
-                        S_max, scale, 0, workspace, workspace_bytes, counters,
-                        counter_count, stream, nullptr, nullptr, peer_buffers,
-                        rank, world, epoch, FA_HEAD_DIM, dtype);
-}
 
 size_t fa_decode_hd_workspace_bytes(int B, int H, int S_max, int head_dim,
                                     int split_size, int device) {
@@ -474,7 +465,9 @@ int run_decode_d128(const void *q, const void *k_cache, const void *v_cache,
                     float scale, int split_size, void *workspace,
                     size_t workspace_bytes, uint32_t *counters,
                     size_t counter_count, void *stream, const void *k_new,
-                    const void *v_new, int dtype = FA_DTYPE_F16) {
+                    const void *v_new, int dtype = FA_DTYPE_F16,
+                    float *const *x_peers = nullptr, int x_rank = 0,
+                    int x_world = 1, uint32_t x_epoch = 0) {
   if (!decode_shape_ok(B, H, S_max, scale)) return FA_EINVAL;
   if (split_size > 0 && split_size % 4 != 0) return FA_EINVAL;
   if (!q || !k_cache || !v_cache || !seq_lens || !o || !workspace || !counters)
@@ -494,8 +487,15 @@ int run_decode_d128(const void *q, const void *k_cache, const void *v_cache,
     return FA_ENOSPACE;
   if ((k_new == nullptr) != (v_new == nullptr)) return FA_EINVAL;
   if (k_new && (!aligned16(k_new) || !aligned16(v_new))) return FA_EALIGN;
+  if (x_peers && (k_new || x_world < 1 || x_world > 32 || x_rank < 0 ||
+                  x_rank >= x_world))
+    return FA_EINVAL;
   DecodeArgs a{};
   a.dtype = dtype;
+  a.x_peers = x_peers;
+  a.x_rank = x_rank;
+  a.x_world = x_world;
+  a.x_epoch = x_epoch;
   a.k_new = static_cast<const __half *>(k_new);
   a.v_new = static_cast<const __half *>(v_new);
   a.k_cache_w = k_new ? static_cast<__half *>(const_cast<void *>(k_cache)) : nullptr;
@@ -522,6 +522,27 @@ int run_decode_d128(const void *q, const void *k_cache, const void *v_cache,
 }
 }  // namespace
 }  // namespace fa
+
+int fa_decode_exchange_ex(const void *q, const void *k_cache,
+                          const void *v_cache, const int32_t *seq_lens,
+                          void *o, int B, int H, int S_max, int head_dim,
+                          int dtype, float scale, void *workspace,
+                          size_t workspace_bytes, uint32_t *counters,
+                          size_t counter_count, float *const *peer_buffers,
+                          int rank, int world, uint32_t epoch, void *stream) {
+  if (dtype != FA_DTYPE_F16 && dtype != FA_DTYPE_BF16) return FA_EINVAL;
+  if (!o || !peer_buffers || epoch == 0) return FA_EINVAL;
+  if (head_dim != FA_HEAD_DIM && head_dim != 128) return FA_EINVAL;
+  if (head_dim == 128)
+    return run_decode_d128(q, k_cache, v_cache, seq_lens, o, B, H, S_max,
+                           scale, 0, workspace, workspace_bytes, counters,
+                           counter_count, stream, nullptr, nullptr, dtype,
+                           peer_buffers, rank, world, epoch);
+  return run_decode_gqa(q, k_cache, v_cache, seq_lens, o, nullptr, B, H, H,
+                        S_max, scale, 0, workspace, workspace_bytes, counters,
+                        counter_count, stream, nullptr, nullptr, peer_buffers,
+                        rank, world, epoch, FA_HEAD_DIM, dtype);
+}
 
 int fa_decode_hd(const void *q, const void *k_cache, const void *v_cache,
                  const int32_t *seq_lens, void *o, int B, int H, int S_max,

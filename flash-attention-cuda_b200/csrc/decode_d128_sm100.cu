@@ -74,6 +74,11 @@ __device__ void write_empty_sequence(const DecodeArgs &a, int b) {
 __device__ __forceinline__ void finish_segment(const DecodeArgs &a, size_t g,
                                                float M, float L,
                                                const float (&A)[4], int lane) {
+  if (a.x_peers) {  // sequence-sharded: send to every rank, merge all
+    decode::x_send<kD>(a, g, M, L, A, lane);
+    decode::x_finish<kD>(a, g, lane);
+    return;
+  }
   if (a.partial_out) {
     float *p = a.partial_out + g * kPF;
 #pragma unroll
@@ -198,8 +203,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     // rows, so it only sees their lengths
     for (int b = lane; b < a.B; b += 32) {
       const int len = decode::seq_rows(a, b);
-      if (len == 0 && (b % static_cast<int>(gridDim.x)) ==
-                          static_cast<int>(blockIdx.x))
+      if (len == 0 && !a.x_peers &&  // sharded: exchanged in produce()
+          (b % static_cast<int>(gridDim.x)) == static_cast<int>(blockIdx.x))
         write_empty_sequence(a, b);
     }
     decode::produce<false, kStages, kD, kStageRows>(

@@ -179,21 +179,26 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
   return v;
 }
 
+// Exchange buffer of rank r for head_dim D: (x_world, B*H, 4 + D) fp32
+// partials, then B*H uint32 arrival counters.
+template <int D>
 __device__ __forceinline__ uint32_t *x_counters(const DecodeArgs &a, int r) {
   return reinterpret_cast<uint32_t *>(
-      a.x_peers[r] + static_cast<size_t>(a.x_world) * a.B * a.H * kPartialFloats);
+      a.x_peers[r] + static_cast<size_t>(a.x_world) * a.B * a.H * (4 + D));
 }
 
 // Whole warp: stores this rank's (m, l, acc) of segment g into slot
 // [x_rank][g] of every rank's buffer (peer memory over NVLink, plain
-// stores), then raises each rank's counter of g. Lane l holds dims l, l+32.
+// stores), then raises each rank's counter of g. Lane l holds dims
+// l + 32 i.
+template <int D>
 __device__ void x_send(const DecodeArgs &a, size_t g, float M, float L,
-                       float A0, float A1, int lane) {
+                       const float (&A)[D / 32], int lane) {
   const size_t BH = static_cast<size_t>(a.B) * a.H;
   for (int r = 0; r < a.x_world; ++r) {
-    float *dst = a.x_peers[r] + (static_cast<size_t>(a.x_rank) * BH + g) * kPartialFloats;
-    dst[4 + lane] = A0;
-    dst[4 + 32 + lane] = A1;
+    float *dst = a.x_peers[r] + (static_cast<size_t>(a.x_rank) * BH + g) * (4 + D);
+#pragma unroll
+    for (int i = 0; i < D / 32; ++i) dst[4 + 32 * i + lane] = A[i];
     if (lane == 0) {
       dst[0] = M;
       dst[1] = L;
@@ -201,16 +206,17 @@ __device__ void x_send(const DecodeArgs &a, size_t g, float M, float L,
   }
   __threadfence_system();
   __syncwarp();
-  if (lane < a.x_world) atomicAdd_system(x_counters(a, lane) + g, 1u);
+  if (lane < a.x_world) atomicAdd_system(x_counters<D>(a, lane) + g, 1u);
   __syncwarp();
 }
 
 // Whole warp: waits (bounded) until all x_world partials of segment g are
 // in this rank's buffer, merges them (log-sum-exp, empty partials skipped,
-// rank order) and writes the fp16 output row.
+// rank order) and writes the output row.
+template <int D>
 __device__ void x_finish(const DecodeArgs &a, size_t g, int lane) {
   const size_t BH = static_cast<size_t>(a.B) * a.H;
-  const uint32_t *ctr = x_counters(a, a.x_rank) + g;
+  const uint32_t *ctr = x_counters<D>(a, a.x_rank) + g;
   const uint32_t target = a.x_epoch * static_cast<uint32_t>(a.x_world);
   int ok = 1;
   if (lane == 0) {
@@ -232,22 +238,27 @@ __device__ void x_finish(const DecodeArgs &a, size_t g, int lane) {
   const float *base = a.x_peers[a.x_rank];
   float M = kNegBig;
   for (int r = 0; r < a.x_world; ++r) {
-    const float *p = base + (static_cast<size_t>(r) * BH + g) * kPartialFloats;
+    const float *p = base + (static_cast<size_t>(r) * BH + g) * (4 + D);
     if (__ldcg(p + 1) > 0.f) M = fmaxf(M, __ldcg(p));
   }
-  float L = 0.f, B0 = 0.f, B1 = 0.f;
+  float L = 0.f;
+  float acc[D / 32];
+#pragma unroll
+  for (int i = 0; i < D / 32; ++i) acc[i] = 0.f;
   for (int r = 0; r < a.x_world; ++r) {
-    const float *p = base + (static_cast<size_t>(r) * BH + g) * kPartialFloats;
+    const float *p = base + (static_cast<size_t>(r) * BH + g) * (4 + D);
     const float l = __ldcg(p + 1);
     if (l <= 0.f) continue;
     const float f = fast_exp2(__ldcg(p) - M);
     L = fmaf(l, f, L);
-    B0 = fmaf(__ldcg(p + 4 + lane), f, B0);
-    B1 = fmaf(__ldcg(p + 4 + 32 + lane), f, B1);
+#pragma unroll
+    for (int i = 0; i < D / 32; ++i)
+      acc[i] = fmaf(__ldcg(p + 4 + 32 * i + lane), f, acc[i]);
   }
   const float inv = L > 0.f ? 1.f / L : 0.f;
-  a.out[g * kHeadDim + lane] = store_elem(B0 * inv, a.dtype);
-  a.out[g * kHeadDim + 32 + lane] = store_elem(B1 * inv, a.dtype);
+#pragma unroll
+  for (int i = 0; i < D / 32; ++i)
+    a.out[g * D + 32 * i + lane] = store_elem(acc[i] * inv, a.dtype);
 }
 
 // Writes a finished (m, l, acc) for segment g: the fp16 output, or the
@@ -257,8 +268,9 @@ __device__ __forceinline__ void finish_segment(const DecodeArgs &a, size_t g,
                                                float M, float L, float A0,
                                                float A1, int lane) {
   if (a.x_peers) {
-    x_send(a, g, M, L, A0, A1, lane);
-    x_finish(a, g, lane);
+    const float A[2] = {A0, A1};
+    x_send<kHeadDim>(a, g, M, L, A, lane);
+    x_finish<kHeadDim>(a, g, lane);
     return;
   }
   if (a.partial_out) {
@@ -383,14 +395,15 @@ __device__ void produce(const DecodeArgs &a, int nseg, int seg_per_plane,
           0xffffffffu, b < a.B && len == 0 &&
                            (b % static_cast<int>(gridDim.x)) ==
                                static_cast<int>(blockIdx.x));
-      while (kD == kHeadDim && todo) {
+      while (todo && (kD == kHeadDim || a.x_peers)) {
         const int i = __ffs(todo) - 1;
         todo &= todo - 1;
         if (a.x_peers) {
           // an empty partial for every rank now; merged after streaming
+          const float zero[kD / 32] = {};
           for (int h = 0; h < a.H; ++h)
-            x_send(a, static_cast<size_t>(chunk + i) * a.H + h, kNegBig, 0.f,
-                   0.f, 0.f, lane);
+            x_send<kD>(a, static_cast<size_t>(chunk + i) * a.H + h, kNegBig,
+                       0.f, zero, lane);
         } else if (lane == 0) {
           write_empty_sequence(a, chunk + i);
         }
@@ -522,7 +535,7 @@ __device__ void produce(const DecodeArgs &a, int nseg, int seg_per_plane,
     }
     // Sharded: the rows of this CTA's empty sequences come from other
     // ranks; merge them now that this CTA's own stream is issued.
-    if (kD == kHeadDim && a.x_peers) {
+    if (a.x_peers) {
       __syncwarp();
       for (int chunk = 0; chunk < a.B; chunk += 32) {
         const int b = chunk + lane;
@@ -534,7 +547,7 @@ __device__ void produce(const DecodeArgs &a, int nseg, int seg_per_plane,
           const int i = __ffs(todo) - 1;
           todo &= todo - 1;
           for (int h = 0; h < a.H; ++h)
-            x_finish(a, static_cast<size_t>(chunk + i) * a.H + h, lane);
+            x_finish<kD>(a, static_cast<size_t>(chunk + i) * a.H + h, lane);
         }
       }
     }

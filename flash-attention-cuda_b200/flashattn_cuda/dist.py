@@ -135,9 +135,10 @@ class PeerExchange:
     IPC handles are all-gathered on the host, and every rank maps the
     others' buffers; the kernel then stores its finished partials straight
     into every rank's buffer over NVLink. One instance serves any number of
-    calls with this (B, H); all ranks must call in the same order."""
+    calls with this (B, H) and head_dim; all ranks must call in the same
+    order."""
 
-    def __init__(self, batch, heads, group=None, device=None):
+    def __init__(self, batch, heads, group=None, device=None, head_dim=64):
         import torch
         import torch.distributed as dist
 
@@ -148,7 +149,8 @@ class PeerExchange:
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.device = torch.cuda.current_device() if device is None else device
         self.shape = (batch, heads)
-        nbytes = _C._exchange_bytes(batch, heads, self.world)
+        self.head_dim = head_dim
+        nbytes = _C._exchange_bytes(batch, heads, self.world, head_dim)
         self._own, handle = _C._exchange_alloc(nbytes, self.device)
         handles = [handle]
         if self.world > 1:
@@ -193,8 +195,9 @@ def sharded_decode_fused(q, k_local, v_local, seq_lens_local, scale, xchg):
     and the cache) from one launch."""
     from . import _C
 
-    if tuple(q.shape[:2]) != xchg.shape:
-        raise ValueError(f"exchange was sized for {xchg.shape}, got {tuple(q.shape[:2])}")
+    if tuple(q.shape[:2]) != xchg.shape or q.shape[3] != xchg.head_dim:
+        raise ValueError(f"exchange was sized for {xchg.shape} at head_dim "
+                         f"{xchg.head_dim}, got {tuple(q.shape)}")
     xchg.epoch += 1
     return _C.decode_exchange(q, k_local, v_local, seq_lens_local, scale,
                               xchg.peers, xchg.rank, xchg.world, xchg.epoch)

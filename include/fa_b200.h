@@ -249,15 +249,21 @@ int fa_decode_exchange(const void *q, const void *k_cache, const void *v_cache,
                        size_t counter_count, float *const *peer_buffers,
                        int rank, int world, uint32_t epoch, void *stream);
 /* fa_decode_exchange for either 16-bit element type (q, this rank's cache
- * chunk and o all fp16 or all bf16; dtype as fa_decode_ex). The exchanged
- * partials are fp32 either way. */
+ * chunk and o all fp16 or all bf16; dtype as fa_decode_ex) and head_dim 64
+ * or 128 (one K/V head per query head). The exchanged partials are fp32
+ * either way; peer_buffers sized by fa_exchange_bytes_hd. */
 int fa_decode_exchange_ex(const void *q, const void *k_cache,
                           const void *v_cache, const int32_t *seq_lens,
-                          void *o, int B, int H, int S_max, int dtype,
-                          float scale, void *workspace, size_t workspace_bytes,
-                          uint32_t *counters, size_t counter_count,
-                          float *const *peer_buffers, int rank, int world,
-                          uint32_t epoch, void *stream);
+                          void *o, int B, int H, int S_max, int head_dim,
+                          int dtype, float scale, void *workspace,
+                          size_t workspace_bytes, uint32_t *counters,
+                          size_t counter_count, float *const *peer_buffers,
+                          int rank, int world, uint32_t epoch, void *stream);
+
+/* Exchange buffer bytes for head_dim 64 (= fa_exchange_bytes) or 128; the
+ * buffers of one exchange are sized for the head_dim of the calls using
+ * it. head_dim 128 decode scratch is fa_decode_hd_workspace_bytes. */
+size_t fa_exchange_bytes_hd(int B, int H, int world, int head_dim);
 
 /*
  * Grouped-query decode for head_dim 64 or 128 (64: as fa_decode_gqa); K/V

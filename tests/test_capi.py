@@ -175,6 +175,14 @@ def test_exchange_buffer_size(lib):
         assert need <= n < need + 256 and n % 256 == 0
     assert lib.fa_exchange_bytes(1, 14, 0) == 0
     assert lib.fa_exchange_bytes(1, 14, 33) == 0
+    lib.fa_exchange_bytes_hd.restype = ctypes.c_size_t
+    lib.fa_exchange_bytes_hd.argtypes = [ctypes.c_int] * 4
+    for b, h, w in [(1, 14, 8), (3, 5, 2)]:
+        assert lib.fa_exchange_bytes_hd(b, h, w, 64) == lib.fa_exchange_bytes(b, h, w)
+        n = lib.fa_exchange_bytes_hd(b, h, w, 128)
+        need = b * h * w * 132 * 4 + b * h * 4
+        assert need <= n < need + 256 and n % 256 == 0
+    assert lib.fa_exchange_bytes_hd(1, 14, 8, 96) == 0
 
 
 def test_prefill_host_plan_and_validation(lib):

@@ -54,6 +54,30 @@ def test_single_rank_exchange_bf16_equals_decode():
     assert flashattn_cuda.take_device_error() == 0
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_single_rank_exchange_d128_equals_decode(dtype):
+    torch.manual_seed(2)
+    b, h, s = 3, 8, 4000
+    q = torch.randn(b, h, 1, 128, device="cuda").to(dtype)
+    k, v = (torch.randn(b, h, s, 128, device="cuda").to(dtype) for _ in range(2))
+    lens = torch.tensor([4000, 0, 333], dtype=torch.int32, device="cuda")
+    xchg = fadist.PeerExchange(b, h, head_dim=128)
+    try:
+        for _ in range(3):
+            got = fadist.sharded_decode_fused(q, k, v, lens, 128 ** -0.5, xchg)
+            want = flashattn_cuda.decode(q, k, v, lens, 128 ** -0.5)
+            assert torch.equal(got, want)
+        assert torch.all(got[1] == 0)
+        with pytest.raises(ValueError, match="head_dim"):
+            fadist.sharded_decode_fused(q[..., :64].contiguous(),
+                                        k[..., :64].contiguous(),
+                                        v[..., :64].contiguous(), lens, 0.1,
+                                        xchg)
+    finally:
+        xchg.close()
+    assert flashattn_cuda.take_device_error() == 0
+
+
 def _two_rank_worker(rank, world, port, result):
     import torch.distributed as dist
 
@@ -61,24 +85,28 @@ def _two_rank_worker(rank, world, port, result):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("nccl", rank=rank, world_size=world)
     try:
-        g = torch.Generator().manual_seed(1)
-        b, h, s = 2, 14, 20000
-        q = torch.randn(b, h, 1, 64, generator=g).half().cuda()
-        k = torch.randn(b, h, s, 64, generator=g).half()
-        v = torch.randn(b, h, s, 64, generator=g).half()
-        lens = torch.tensor([20000, 7000], dtype=torch.int32)
-        c0, c1 = fadist.seq_shard(s, world, rank)
-        kl = k[:, :, c0:c1].contiguous().cuda()
-        vl = v[:, :, c0:c1].contiguous().cuda()
-        ll = torch.as_tensor(fadist.local_seq_lens(lens.tolist(), c0, c1),
-                             dtype=torch.int32).cuda()
-        xchg = fadist.PeerExchange(b, h)
-        outs = [fadist.sharded_decode_fused(q, kl, vl, ll, SCALE, xchg)
-                for _ in range(3)]
-        torch.cuda.synchronize()
-        xchg.close()
-        want = flashattn_cuda.decode(q, k.cuda(), v.cuda(), lens.cuda(), SCALE)
-        err = max((o.float() - want.float()).abs().max().item() for o in outs)
+        err = 0.0
+        for d in (64, 128):  # head_dim 64 and 128 through the same exchange code
+            g = torch.Generator().manual_seed(1)
+            b, h, s = 2, 14, 20000
+            q = torch.randn(b, h, 1, d, generator=g).half().cuda()
+            k = torch.randn(b, h, s, d, generator=g).half()
+            v = torch.randn(b, h, s, d, generator=g).half()
+            lens = torch.tensor([20000, 7000], dtype=torch.int32)
+            c0, c1 = fadist.seq_shard(s, world, rank)
+            kl = k[:, :, c0:c1].contiguous().cuda()
+            vl = v[:, :, c0:c1].contiguous().cuda()
+            ll = torch.as_tensor(fadist.local_seq_lens(lens.tolist(), c0, c1),
+                                 dtype=torch.int32).cuda()
+            xchg = fadist.PeerExchange(b, h, head_dim=d)
+            outs = [fadist.sharded_decode_fused(q, kl, vl, ll, d ** -0.5, xchg)
+                    for _ in range(3)]
+            torch.cuda.synchronize()
+            xchg.close()
+            want = flashattn_cuda.decode(q, k.cuda(), v.cuda(), lens.cuda(),
+                                         d ** -0.5)
+            err = max([err] + [(o.float() - want.float()).abs().max().item()
+                               for o in outs])
         result[rank] = err if flashattn_cuda.take_device_error() == 0 else -1.0
     finally:
         dist.destroy_process_group()
