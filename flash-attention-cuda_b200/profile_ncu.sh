@@ -1,5 +1,5 @@
 #!/bin/bash
-# ncu capture of the two kernels on their BASELINE workloads, then a markdown
+# ncu capture of the two kernels on their benchmark workloads, then a markdown
 # summary (flashattn_cuda.ncu_extract). Run on a B200 from the repository root:
 #
 #   bash flash-attention-cuda_b200/profile_ncu.sh [OUT_DIR]
@@ -8,7 +8,7 @@
 # profiled); one launch per kernel is captured after two warm-up launches,
 # always with --clock-control none so the GPU's clocks are left untouched.
 set -euo pipefail
-OUT=${1:-gpurun_out}
+OUT=${1:-ncu_out}
 PKG=flash-attention-cuda_b200
 NCU=${NCU:-ncu}
 mkdir -p "$OUT"

@@ -1,8 +1,7 @@
 """Generates the golden vectors in tests/golden/ from the reference itself.
 
-Run in a container that has the reference checkout (path in FA_REFERENCE,
-default /root/reference); the outputs are committed, so tests never need the
-reference at run time:
+Run where the reference checkout is available (its path in FA_REFERENCE);
+the outputs are committed, so tests never need the reference at run time:
 
     FA_REFERENCE=/path/to/flash-attention-cuda python tests/golden/make_golden.py
 

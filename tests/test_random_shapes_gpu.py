@@ -1,6 +1,8 @@
 """Seeded random configurations across the whole surface (prefill and
 decode, head_dim 64 and 128, grouped K/V heads, ragged lengths, fused
-append) against fp32 PyTorch attention at the north star's 2e-3 bound."""
+append) against fp32 PyTorch attention: fp16 at the north star's 2e-3
+bound, bf16 at 1.5e-2 (bf16 output rounding alone reaches 3.9e-3 for
+values in [1, 2); the probabilities enter PV as bf16)."""
 
 import random
 
@@ -12,6 +14,8 @@ from conftest import requires_gpu
 import flashattn_cuda
 
 pytestmark = [pytest.mark.gpu, requires_gpu]
+DTYPES = [pytest.param(torch.float16, 2e-3, id="fp16"),
+          pytest.param(torch.bfloat16, 1.5e-2, id="bf16")]
 
 
 def sdpa(q, k, v, causal, scale):
@@ -38,8 +42,9 @@ def pick_heads(rng):
     return h_kv * rng.choice([1, 1, 2, 3, 7, 17]), h_kv
 
 
+@pytest.mark.parametrize("dtype,tol", DTYPES)
 @pytest.mark.parametrize("seed", range(24))
-def test_random_prefill(seed):
+def test_random_prefill(seed, dtype, tol):
     rng = random.Random(seed)
     d = rng.choice([64, 128])
     b = rng.randint(1, 3)
@@ -48,17 +53,18 @@ def test_random_prefill(seed):
     causal = rng.random() < 0.6
     scale = d ** -0.5
     g = torch.Generator(device="cuda").manual_seed(seed)
-    q = torch.randn(b, h, n, d, device="cuda", generator=g).half()
-    k = torch.randn(b, h_kv, n, d, device="cuda", generator=g).half()
-    v = torch.randn(b, h_kv, n, d, device="cuda", generator=g).half()
+    q = torch.randn(b, h, n, d, device="cuda", generator=g).to(dtype)
+    k = torch.randn(b, h_kv, n, d, device="cuda", generator=g).to(dtype)
+    v = torch.randn(b, h_kv, n, d, device="cuda", generator=g).to(dtype)
     got = flashattn_cuda.prefill(q, k, v, causal, scale)
     err = (got.float() - sdpa(q, k, v, causal, scale)).abs().max().item()
-    assert err <= 2e-3, (d, b, h, h_kv, n, causal, err)
+    assert err <= tol, (d, b, h, h_kv, n, causal, err)
     assert flashattn_cuda.take_device_error() == 0
 
 
+@pytest.mark.parametrize("dtype,tol", DTYPES)
 @pytest.mark.parametrize("seed", range(24))
-def test_random_decode(seed):
+def test_random_decode(seed, dtype, tol):
     rng = random.Random(1000 + seed)
     d = rng.choice([64, 128])
     b = rng.randint(1, 9)
@@ -66,15 +72,15 @@ def test_random_decode(seed):
     s = rng.choice([1, 17, 128, 129, 1000, 4096, 9000])
     scale = d ** -0.5
     g = torch.Generator(device="cuda").manual_seed(seed)
-    q = torch.randn(b, h, 1, d, device="cuda", generator=g).half()
-    k = torch.randn(b, h_kv, s, d, device="cuda", generator=g).half()
-    v = torch.randn(b, h_kv, s, d, device="cuda", generator=g).half()
+    q = torch.randn(b, h, 1, d, device="cuda", generator=g).to(dtype)
+    k = torch.randn(b, h_kv, s, d, device="cuda", generator=g).to(dtype)
+    v = torch.randn(b, h_kv, s, d, device="cuda", generator=g).to(dtype)
     lens = torch.tensor([rng.choice([0, 1, s, s + 5, rng.randint(0, s)])
                          for _ in range(b)], dtype=torch.int32, device="cuda")
     append = rng.random() < 0.4
     if append:
-        kn = torch.randn(b, h_kv, 1, d, device="cuda", generator=g).half()
-        vn = torch.randn(b, h_kv, 1, d, device="cuda", generator=g).half()
+        kn = torch.randn(b, h_kv, 1, d, device="cuda", generator=g).to(dtype)
+        vn = torch.randn(b, h_kv, 1, d, device="cuda", generator=g).to(dtype)
         k_ref, v_ref = k.clone(), v.clone()
         lens_after = []
         for i, n in enumerate(lens.tolist()):
@@ -91,5 +97,5 @@ def test_random_decode(seed):
         got = flashattn_cuda.decode(q, k, v, lens, scale)
         want = decode_ref(q, k, v, lens.cpu(), scale)
     err = (got.float() - want).abs().max().item()
-    assert err <= 2e-3, (d, b, h, h_kv, s, lens.tolist(), append, err)
+    assert err <= tol, (d, b, h, h_kv, s, lens.tolist(), append, err)
     assert flashattn_cuda.take_device_error() == 0
