@@ -135,7 +135,11 @@ __device__ __forceinline__ TileInfo tile_info(int pair, int t, int N,
   return ti;
 }
 
-template <typename Dt>
+// kHeadPairs (sequences of at most one 128-row tile): the CTA's two tile
+// slots hold one tile of each of two heads (2 * blockIdx.x and the next),
+// each with its own K/V head in its own ring stage, instead of two tiles of
+// one head; a lone tile would leave half of the CTA idle.
+template <typename Dt, bool kHeadPairs = false>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
                    const __grid_constant__ CUtensorMap tm_k,
@@ -158,13 +162,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   // last (most keys) to the first, heads fastest.
   const int n_qt = (N + kBlockM - 1) / kBlockM;
   const int n_pairs = (n_qt + 1) / 2;
-  const int pair = n_pairs - 1 - static_cast<int>(blockIdx.x / BH);
-  const int bh = static_cast<int>(blockIdx.x % BH);
-  // K/V head of this query head: `group` query heads share one K/V head
+  const int pair =
+      kHeadPairs ? 0 : n_pairs - 1 - static_cast<int>(blockIdx.x / BH);
+  const int bh = kHeadPairs ? 2 * static_cast<int>(blockIdx.x)
+                            : static_cast<int>(blockIdx.x % BH);
+  const int bh1 = kHeadPairs ? bh + 1 : bh;  // query head of tile 1
+  // K/V head of a query head: `group` query heads share one K/V head
   // (group == 1 without grouped-query attention).
   const int kv_bh = (bh / H) * (H / group) + (bh % H) / group;
-  const TileInfo t0 = tile_info(pair, 0, N, causal, zigzag);
-  const TileInfo t1 = tile_info(pair, 1, N, causal, zigzag);
+  const int kv_bh1 = (bh1 / H) * (H / group) + (bh1 % H) / group;
+  TileInfo t0, t1;
+  if (kHeadPairs) {
+    t0.qt = t1.qt = 0;
+    t0.n_kv = 1;
+    t1.n_kv = bh1 < BH ? 1 : 0;
+  } else {
+    t0 = tile_info(pair, 0, N, causal, zigzag);
+    t1 = tile_info(pair, 1, N, causal, zigzag);
+  }
   const int n_kv = t0.n_kv > t1.n_kv ? t0.n_kv : t1.n_kv;
 
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kBarOff);
@@ -199,7 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_load_3d(smem + kQOff, &tm_q, &bars[kBarQFull], 0, t0.qt * kBlockM, bh);
     if (two)
       tma_load_3d(smem + kQOff + kTileBytes, &tm_q, &bars[kBarQFull], 0,
-                  t1.qt * kBlockM, bh);
+                  t1.qt * kBlockM, bh1);
     for (; preissued < n_kv && preissued < kStages; ++preissued) {
       const int s = preissued;
       mbar_arrive_expect_tx(&bars[kBarKFull + s], 2 * kTileBytes);
@@ -207,6 +222,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                   0, preissued * kBlockN, kv_bh);
       tma_load_3d(smem + kVOff + s * kTileBytes, &tm_v, &bars[kBarKFull + s],
                   0, preissued * kBlockN, kv_bh);
+    }
+    if (kHeadPairs && two) {
+      // tile 1's head: its K/V tile in stage 1
+      mbar_arrive_expect_tx(&bars[kBarKFull + 1], 2 * kTileBytes);
+      tma_load_3d(smem + kKOff + kTileBytes, &tm_k, &bars[kBarKFull + 1], 0,
+                  0, kv_bh1);
+      tma_load_3d(smem + kVOff + kTileBytes, &tm_v, &bars[kBarKFull + 1], 0,
+                  0, kv_bh1);
+      preissued = 2;  // copies in flight (the loop below issues none)
     }
     *abort_flag = device_failed() ? 1u : 0u;
   }
@@ -275,9 +299,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           issue_s_tile<Dt>(tmem + kTmemS, desc0 + (kQOff >> 4), desc0 + (kKOff >> 4));
           mma_commit(&bars[kBarSFull + 0]);
         }
-        if (n1 > 0) {
+        if (n1 > 0 && (!kHeadPairs || mbar_wait(&bars[kBarKFull + 1], 0))) {
           issue_s_tile<Dt>(tmem + kTmemS + 128, desc0 + ((kQOff + kTileBytes) >> 4),
-                       desc0 + (kKOff >> 4));
+                       desc0 + ((kKOff + (kHeadPairs ? kTileBytes : 0)) >> 4));
           mma_commit(&bars[kBarSFull + 1]);
         }
       }
@@ -322,8 +346,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         FA_TRACE_EVENT(2048 + j * 16 + t * 8 + 4);
         tc_fence_after();
         if (leader) {
+          const int sv = kHeadPairs ? t : s;  // head pairs: V of tile t's head
           issue_pv_tile<Dt>(tmem + kTmemO + 64 * t, tmem + kTmemP + 64 * t,
-                        desc0 + ((kVOff + s * kTileBytes) >> 4), j > 0);
+                        desc0 + ((kVOff + sv * kTileBytes) >> 4), j > 0);
           mma_commit(&bars[kBarODone + t]);
         }
         __syncwarp();
@@ -489,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (q_row < N) {
           const float inv_l = (l_sum > 0.f) ? 1.f / l_sum : 0.f;
           uint4 *dst = reinterpret_cast<uint4 *>(
-              out + (static_cast<size_t>(bh) * N + q_row) * kHeadDim);
+              out + (static_cast<size_t>(t ? bh1 : bh) * N + q_row) * kHeadDim);
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             uint4 v;
@@ -521,6 +546,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace prefill
 
+const void *prefill_head_pairs_kernel_ptr(int dtype) {
+  return dtype == FA_DTYPE_BF16
+             ? reinterpret_cast<const void *>(prefill::prefill_kernel<BF16, true>)
+             : reinterpret_cast<const void *>(prefill::prefill_kernel<F16, true>);
+}
 const void *prefill_kernel_ptr(int dtype) {
   return dtype == FA_DTYPE_BF16
              ? reinterpret_cast<const void *>(prefill::prefill_kernel<BF16>)
@@ -546,6 +576,15 @@ cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
   // One wave of CTAs: zig-zag pairs of equal causal work, so the kernel
   // does not wait on the heaviest pair. Several waves: heaviest first.
   const int zigzag = causal && grid <= static_cast<unsigned>(sms) ? 2 : 0;
+  if (n_qt == 1) {
+    // one tile per head: two heads per CTA
+    auto kernel = dtype == FA_DTYPE_BF16 ? prefill::prefill_kernel<BF16, true>
+                                         : prefill::prefill_kernel<F16, true>;
+    kernel<<<(BH + 1) / 2, prefill::kThreads, prefill::kSmemBytes, stream>>>(
+        tm_q, tm_k, tm_v, out, N, BH, causal ? 1 : 0, scale_log2, H,
+        H / H_kv);
+    return cudaGetLastError();
+  }
   auto kernel = dtype == FA_DTYPE_BF16 ? prefill::prefill_kernel<BF16>
                                        : prefill::prefill_kernel<F16>;
   kernel<<<grid, prefill::kThreads, prefill::kSmemBytes, stream>>>(
