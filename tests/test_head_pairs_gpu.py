@@ -1,0 +1,38 @@
+"""Prefill of sequences that fit in one 128-row tile (N <= 128): the kernel
+then gives each CTA one tile of each of two heads. Edges: an odd number of
+(batch, head) units (the last CTA holds one head), grouped K/V heads (two
+heads of a pair may read different K/V heads), ragged N, both dtypes,
+against fp32 attention."""
+
+import pytest
+import torch
+
+from conftest import requires_gpu
+
+import flashattn_cuda
+
+pytestmark = [pytest.mark.gpu, requires_gpu]
+
+
+def reference(q, k, v, causal, scale):
+    group = q.shape[1] // k.shape[1]
+    return torch.nn.functional.scaled_dot_product_attention(
+        q.float(), k.float().repeat_interleave(group, 1),
+        v.float().repeat_interleave(group, 1), is_causal=causal, scale=scale)
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float16, 2e-3),
+                                       (torch.bfloat16, 1.5e-2)])
+@pytest.mark.parametrize("b,h,h_kv", [(1, 1, 1), (3, 5, 5), (2, 7, 1),
+                                      (4, 6, 3), (64, 32, 32)])
+@pytest.mark.parametrize("n", [1, 64, 100, 128])
+@pytest.mark.parametrize("causal", [True, False])
+def test_short_prefill_matches_fp32(dtype, tol, b, h, h_kv, n, causal):
+    torch.manual_seed(b * 100 + h * 10 + n)
+    q = torch.randn(b, h, n, 64, device="cuda").to(dtype)
+    k = torch.randn(b, h_kv, n, 64, device="cuda").to(dtype)
+    v = torch.randn(b, h_kv, n, 64, device="cuda").to(dtype)
+    got = flashattn_cuda.prefill(q, k, v, causal, 0.125)
+    err = (got.float() - reference(q, k, v, causal, 0.125)).abs().max().item()
+    assert err <= tol, err
+    assert flashattn_cuda.take_device_error() == 0
