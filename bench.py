@@ -460,6 +460,18 @@ def run_ours(args, rank, world, local_rank):
                 "gbs": round(bb / (tdb * 1e-3) / 1e9, 1),
                 "frac_of_measured_hbm": round(bb / (tdb * 1e-3) / 1e9 / hbm, 4)}
             del qdb, kcb, vcb
+            # many short prompts (N = 128: two heads per CTA)
+            qs, ks, vs = (randn(64, 32, 128, HEAD_DIM, seed=130 + i)
+                          for i in range(3))
+            tsh = timer.run(lambda: fa.prefill(qs, ks, vs, True, SCALE),
+                            args.steps, args.warmup) / args.steps
+            launches += args.steps
+            secondary["prefill_short_b64_h32_n128"] = {
+                "ms": round(tsh, 5),
+                "tflops": round(prefill_flops(64, 32, 128, True)
+                                / (tsh * 1e-3) / 1e12, 2),
+                "note": "causal prefill of 2048 heads of 128 tokens"}
+            del qs, ks, vs
             secondary["c3_prefill_gqa_kv2"] = {
                 "ms": round(t, 5),
                 "tflops": round(prefill_flops(C3["B"], C3["H"], C3["N"], True)
