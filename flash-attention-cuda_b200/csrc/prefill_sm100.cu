@@ -23,8 +23,8 @@
 //
 // Shared memory (1 KiB aligned, 128-byte-swizzled tiles as written by TMA):
 //   Q0, Q1  [128 rows x 128 B]            32 KiB
-//   K       3 stages x [128 keys x 128 B] 48 KiB
-//   V       3 stages x [128 keys x 128 B] 48 KiB
+//   K       6 slots x  [128 keys x 128 B] 96 KiB (3 used with one head)
+//   V       6 slots x  [128 keys x 128 B] 96 KiB
 //   mbarriers, TMEM base address, abort flag
 // Tensor memory (512 columns x 128 lanes, fp32 words):
 //   S0 [0,128)  S1 [128,256)  O0 [256,320)  O1 [320,384)
@@ -36,6 +36,10 @@
 #include <math.h>
 #include <stdint.h>
 
+#include <algorithm>
+#include <functional>
+#include <map>
+
 #include "fa_kernels.h"
 #include "fa_sm100.cuh"
 
@@ -45,7 +49,17 @@ namespace prefill {
 constexpr int kBlockM = 128;  // query rows per tile
 constexpr int kBlockN = 128;  // keys per KV tile
 constexpr int kTilesPerCta = 2;
-constexpr int kStages = 3;
+// K/V ring slots in shared memory. One head per CTA cycles through 3 of
+// them (two key tiles ahead of the one in use). Two heads per CTA use all
+// 6: three key steps of both heads, so each head's stream also runs two
+// steps ahead (with 4, one step ahead, a long sequence whose K/V misses L2
+// stalls on every tile).
+constexpr int kRingSlots = 6;
+#ifndef FA_HEAD_PAIR_MAX_TILES
+#define FA_HEAD_PAIR_MAX_TILES 7
+#endif
+// Odd query-tile counts up to this use the two-heads-per-CTA form.
+constexpr int kMaxHeadPairTiles = FA_HEAD_PAIR_MAX_TILES;
 constexpr int kSoftmaxThreads = 128;  // per query tile
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
@@ -58,13 +72,13 @@ constexpr uint32_t kTileBytes = kBlockN * kRowBytes;  // 16 KiB
 
 constexpr uint32_t kQOff = 0;
 constexpr uint32_t kKOff = kQOff + kTilesPerCta * kTileBytes;
-constexpr uint32_t kVOff = kKOff + kStages * kTileBytes;
-constexpr uint32_t kBarOff = kVOff + kStages * kTileBytes;
+constexpr uint32_t kVOff = kKOff + kRingSlots * kTileBytes;
+constexpr uint32_t kBarOff = kVOff + kRingSlots * kTileBytes;
 // barrier slots
 constexpr int kBarQFull = 0;
 constexpr int kBarKFull = kBarQFull + 1;          // + stage: K and V tile
-constexpr int kBarKVEmpty = kBarKFull + kStages;  // + stage
-constexpr int kBarSFull = kBarKVEmpty + kStages;  // + tile
+constexpr int kBarKVEmpty = kBarKFull + kRingSlots;  // + stage
+constexpr int kBarSFull = kBarKVEmpty + kRingSlots;  // + tile
 constexpr int kBarSFree = kBarSFull + kTilesPerCta;
 constexpr int kBarPFull = kBarSFree + kTilesPerCta;
 constexpr int kBarODone = kBarPFull + kTilesPerCta;
@@ -73,6 +87,7 @@ constexpr int kNumBars = kBarDrain + 1;
 constexpr uint32_t kTmemSlotOff = kBarOff + kNumBars * 8;
 constexpr uint32_t kAbortOff = kTmemSlotOff + 4;
 constexpr uint32_t kSmemBytes = kAbortOff + 4 + 8;
+static_assert(kSmemBytes <= 227 * 1024, "above the sm_100 per-CTA shared memory limit");
 
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemS = 0;    // + 128 * tile
@@ -135,11 +150,15 @@ __device__ __forceinline__ TileInfo tile_info(int pair, int t, int N,
   return ti;
 }
 
-// kHeadPairs (sequences of at most one 128-row tile): the CTA's two tile
-// slots hold one tile of each of two heads (2 * blockIdx.x and the next),
-// each with its own K/V head in its own ring stage, instead of two tiles of
-// one head; a lone tile would leave half of the CTA idle.
-template <typename Dt, bool kHeadPairs = false>
+// kHeadPairs (an odd number of query tiles per head, at most 7): the CTA's
+// two tile slots hold the same query tile of two heads (2 * hp and the
+// next), each streaming its own K/V head, instead of two tiles of one head
+// (which would leave the last tile of every head alone in a half-idle CTA).
+// The two K/V streams interleave in the ring: key tile j of slot t is ring
+// position 2 j + t (position j with one head per CTA). kOneTile: sequences
+// of at most one query tile, where every CTA runs exactly one key step and
+// the compiler drops the loops around it.
+template <typename Dt, bool kHeadPairs = false, bool kOneTile = false>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
                    const __grid_constant__ CUtensorMap tm_k,
@@ -147,6 +166,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                    __half *__restrict__ out, int N, int BH, int causal,
                    float scale_log2, int H, int group) {
   extern __shared__ __align__(1024) uint8_t smem[];
+  constexpr int kStages = kHeadPairs ? kRingSlots : 3;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
@@ -162,9 +182,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   // last (most keys) to the first, heads fastest.
   const int n_qt = (N + kBlockM - 1) / kBlockM;
   const int n_pairs = (n_qt + 1) / 2;
+  const int n_hp = (BH + 1) / 2;  // head pairs (kHeadPairs)
+  // heaviest first: kHeadPairs walks query tiles from the last, head pairs
+  // fastest
+  const int hp_qt = kHeadPairs && !kOneTile
+                        ? n_qt - 1 - static_cast<int>(blockIdx.x) / n_hp
+                        : 0;
   const int pair =
       kHeadPairs ? 0 : n_pairs - 1 - static_cast<int>(blockIdx.x / BH);
-  const int bh = kHeadPairs ? 2 * static_cast<int>(blockIdx.x)
+  const int bh = kHeadPairs ? 2 * (kOneTile ? static_cast<int>(blockIdx.x)
+                                            : static_cast<int>(blockIdx.x) % n_hp)
                             : static_cast<int>(blockIdx.x % BH);
   const int bh1 = kHeadPairs ? bh + 1 : bh;  // query head of tile 1
   // K/V head of a query head: `group` query heads share one K/V head
@@ -173,9 +200,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int kv_bh1 = (bh1 / H) * (H / group) + (bh1 % H) / group;
   TileInfo t0, t1;
   if (kHeadPairs) {
-    t0.qt = t1.qt = 0;
-    t0.n_kv = 1;
-    t1.n_kv = bh1 < BH ? 1 : 0;
+    t0.qt = t1.qt = hp_qt;
+    t0.n_kv = kOneTile ? 1 : causal ? hp_qt + 1 : n_qt;
+    t1.n_kv = bh1 < BH ? t0.n_kv : 0;
   } else {
     t0 = tile_info(pair, 0, N, causal, zigzag);
     t1 = tile_info(pair, 1, N, causal, zigzag);
@@ -186,6 +213,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kTmemSlotOff);
   volatile uint32_t *abort_flag =
       reinterpret_cast<volatile uint32_t *>(smem + kAbortOff);
+
+  // Ring positions: key tile j of tile slot t is position 2 j + t with two
+  // heads per CTA (tile 1's positions skipped when it has no head), else
+  // position j; a position's stage is p % kStages.
+  const int n_pos = kHeadPairs ? 2 * n_kv : n_kv;
+  auto pos_used = [&](int p) { return !kHeadPairs || !(p & 1) || t1.n_kv > 0; };
+  auto load_pos = [&](int p) {
+    if (!pos_used(p)) return;
+    const int j = kHeadPairs ? p >> 1 : p;
+    const int kvh = (kHeadPairs && (p & 1)) ? kv_bh1 : kv_bh;
+    const int s = p % kStages;
+    mbar_arrive_expect_tx(&bars[kBarKFull + s], 2 * kTileBytes);
+    tma_load_3d(smem + kKOff + s * kTileBytes, &tm_k, &bars[kBarKFull + s], 0,
+                j * kBlockN, kvh);
+    tma_load_3d(smem + kVOff + s * kTileBytes, &tm_v, &bars[kBarKFull + s], 0,
+                j * kBlockN, kvh);
+  };
 
   // The producer lane sets up the barriers and issues the Q tiles and the
   // first kStages K/V tiles before the CTA-wide barrier, so their latency
@@ -215,23 +259,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (two)
       tma_load_3d(smem + kQOff + kTileBytes, &tm_q, &bars[kBarQFull], 0,
                   t1.qt * kBlockM, bh1);
-    for (; preissued < n_kv && preissued < kStages; ++preissued) {
-      const int s = preissued;
-      mbar_arrive_expect_tx(&bars[kBarKFull + s], 2 * kTileBytes);
-      tma_load_3d(smem + kKOff + s * kTileBytes, &tm_k, &bars[kBarKFull + s],
-                  0, preissued * kBlockN, kv_bh);
-      tma_load_3d(smem + kVOff + s * kTileBytes, &tm_v, &bars[kBarKFull + s],
-                  0, preissued * kBlockN, kv_bh);
-    }
-    if (kHeadPairs && two) {
-      // tile 1's head: its K/V tile in stage 1
-      mbar_arrive_expect_tx(&bars[kBarKFull + 1], 2 * kTileBytes);
-      tma_load_3d(smem + kKOff + kTileBytes, &tm_k, &bars[kBarKFull + 1], 0,
-                  0, kv_bh1);
-      tma_load_3d(smem + kVOff + kTileBytes, &tm_v, &bars[kBarKFull + 1], 0,
-                  0, kv_bh1);
-      preissued = 2;  // copies in flight (the loop below issues none)
-    }
+    for (; preissued < n_pos && preissued < kStages; ++preissued)
+      load_pos(preissued);
     *abort_flag = device_failed() ? 1u : 0u;
   }
   if (warp == kMmaWarp) {
@@ -255,28 +284,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------ TMA
     if (lane == 0) {
       int issued = preissued;
-      for (int j = preissued; j < n_kv; ++j) {
+      for (int p = preissued; p < n_pos; ++p) {
         if (*abort_flag) break;
-        const int s = j % kStages;
-        const int use = j / kStages;
-        if (use > 0 && !mbar_wait(&bars[kBarKVEmpty + s], (use - 1) & 1)) {
+        const int s = p % kStages;
+        const int use = p / kStages;
+        if (pos_used(p) && use > 0 &&
+            !mbar_wait(&bars[kBarKVEmpty + s], (use - 1) & 1)) {
           *abort_flag = 1;
           break;
         }
-        mbar_arrive_expect_tx(&bars[kBarKFull + s], 2 * kTileBytes);
-        tma_load_3d(smem + kKOff + s * kTileBytes, &tm_k, &bars[kBarKFull + s],
-                    0, j * kBlockN, kv_bh);
-        tma_load_3d(smem + kVOff + s * kTileBytes, &tm_v, &bars[kBarKFull + s],
-                    0, j * kBlockN, kv_bh);
-        issued = j + 1;
+        load_pos(p);
+        issued = p + 1;
       }
       // No copy of ours may still be landing when the CTA exits (matters
       // only when another role gave up early).
       if (*abort_flag) {
         mbar_wait(&bars[kBarQFull], 0);
-        for (int j = (issued > kStages ? issued - kStages : 0); j < issued;
-             ++j) {
-          mbar_wait(&bars[kBarKFull + j % kStages], (j / kStages) & 1);
+        for (int p = (issued > kStages ? issued - kStages : 0); p < issued;
+             ++p) {
+          if (pos_used(p))
+            mbar_wait(&bars[kBarKFull + p % kStages], (p / kStages) & 1);
         }
       }
     }
@@ -290,8 +317,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int n0 = t0.n_kv;
     const int n1 = t1.n_kv;
     const uint64_t desc0 = sw128_desc(sbase);
+    // ring position of key tile j of slot t
+    auto kpos = [&](int t, int j) { return kHeadPairs ? 2 * j + t : j; };
     bool ok = mbar_wait(&bars[kBarQFull], 0) &&
-              mbar_wait(&bars[kBarKFull + 0], 0);
+              mbar_wait(&bars[kBarKFull + 0], 0) &&
+              (!kHeadPairs || kOneTile || n1 == 0 ||
+               mbar_wait(&bars[kBarKFull + 1], 0));
     if (ok) {
       tc_fence_after();
       if (leader) {
@@ -299,9 +330,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           issue_s_tile<Dt>(tmem + kTmemS, desc0 + (kQOff >> 4), desc0 + (kKOff >> 4));
           mma_commit(&bars[kBarSFull + 0]);
         }
-        if (n1 > 0 && (!kHeadPairs || mbar_wait(&bars[kBarKFull + 1], 0))) {
+        // With two heads tile 1's first K/V tile has its own ring position;
+        // one-tile CTAs issue S0 before waiting on it.
+        if (n1 > 0 && (!kOneTile || mbar_wait(&bars[kBarKFull + 1], 0))) {
           issue_s_tile<Dt>(tmem + kTmemS + 128, desc0 + ((kQOff + kTileBytes) >> 4),
-                       desc0 + ((kKOff + (kHeadPairs ? kTileBytes : 0)) >> 4));
+                       desc0 + ((kKOff + (kpos(1, 0) % kStages) * kTileBytes) >> 4));
           mma_commit(&bars[kBarSFull + 1]);
         }
       }
@@ -312,18 +345,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = false;
         break;
       }
-      const int s = j % kStages;
-      const int s1 = (j + 1) % kStages;
 #pragma unroll
       for (int t = 0; t < kTilesPerCta; ++t) {
         const int nt = t ? n1 : n0;
         if (!ok || j >= nt) continue;
+        const int s = kpos(t, j) % kStages;         // K_j, V_j of this slot
+        const int p1 = kpos(t, j + 1);
+        const int s1 = p1 % kStages;                // K_{j+1}
         if (j + 1 < nt) {
           // K/V tile j+1 is waited on once per round (by the first tile
-          // that uses it); V_j was waited on with K_j the round before.
-          const bool need_kv = (t == 0) || (n0 <= j + 1);
+          // that uses it, or by each slot with two heads); V_j was waited
+          // on with K_j the round before.
+          const bool need_kv = kHeadPairs || (t == 0) || (n0 <= j + 1);
           if ((need_kv &&
-               !mbar_wait(&bars[kBarKFull + s1], ((j + 1) / kStages) & 1)) ||
+               !mbar_wait(&bars[kBarKFull + s1], (p1 / kStages) & 1)) ||
               !mbar_wait(&bars[kBarSFree + t], j & 1)) {
             ok = false;
             continue;
@@ -346,16 +381,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         FA_TRACE_EVENT(2048 + j * 16 + t * 8 + 4);
         tc_fence_after();
         if (leader) {
-          const int sv = kHeadPairs ? t : s;  // head pairs: V of tile t's head
           issue_pv_tile<Dt>(tmem + kTmemO + 64 * t, tmem + kTmemP + 64 * t,
-                        desc0 + ((kVOff + sv * kTileBytes) >> 4), j > 0);
+                        desc0 + ((kVOff + s * kTileBytes) >> 4), j > 0);
           mma_commit(&bars[kBarODone + t]);
         }
         __syncwarp();
         FA_TRACE_EVENT(2048 + j * 16 + t * 8 + 2);
       }
       if (!ok) break;
-      if (leader) mma_commit(&bars[kBarKVEmpty + s]);
+      // release round j's ring positions (both slots' with two heads)
+      if (leader) {
+        mma_commit(&bars[kBarKVEmpty + kpos(0, j) % kStages]);
+        if (kHeadPairs) mma_commit(&bars[kBarKVEmpty + kpos(1, j) % kStages]);
+      }
       __syncwarp();
     }
     if (!ok && leader) *abort_flag = 1;
@@ -546,10 +584,72 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace prefill
 
-const void *prefill_head_pairs_kernel_ptr(int dtype) {
+namespace prefill {
+
+// Estimated run time, in key-step units, of CTAs list-scheduled heaviest
+// first on `sms` SMs (the order both grids launch in): each CTA starts on
+// the SM that frees up first. classes: (cost, count), decreasing cost.
+// SMs are kept as (time free, how many), so a class of c equal CTAs costs
+// one map operation per wave, not per CTA.
+static double list_makespan(const std::pair<double, long long> *classes,
+                            int n, int sms) {
+  std::map<double, long long> free_at{{0.0, sms}};
+  double end = 0.0;
+  for (int i = 0; i < n; ++i) {
+    long long left = classes[i].second;
+    while (left > 0) {
+      auto it = free_at.begin();
+      const double t = it->first + classes[i].first;
+      const long long k = std::min(left, it->second);
+      if ((it->second -= k) == 0) free_at.erase(it);
+      free_at[t] += k;
+      end = std::max(end, t);
+      left -= k;
+    }
+  }
+  return end;
+}
+
+// Whether an odd number of query tiles (n_qt) runs faster as the same tile
+// of two heads per CTA than as tile pairs of one head, whose last CTA per
+// head holds a lone tile with half the softmax warps idle. Cost model, in
+// key steps of a one-head CTA: a CTA costs kCtaFixed plus its key steps (a
+// CTA's step time hardly depends on whether it holds one query tile or
+// two); a two-head step costs kPairStep, since it streams two K/V heads
+// where one head's two tiles share each K/V tile. Both constants are fitted
+// to measured B200 times (B16/B8 x 12 heads, N 384-896, causal and full).
+bool head_pairs_pay(int BH, int n_qt, bool causal, int sms) {
+  constexpr double kCtaFixed = 1.0, kPairStep = 1.25;
+  std::pair<double, long long> one[(kMaxHeadPairTiles + 1) / 2],
+      two[kMaxHeadPairTiles];
+  const int n_pairs = (n_qt + 1) / 2;
+  const bool zigzag = causal && static_cast<long long>(n_pairs) * BH <= sms;
+  for (int p = 0; p < n_pairs; ++p) {
+    // key steps of a CTA: those of its longer tile
+    const int steps = !causal ? n_qt
+                      : zigzag ? n_qt - p
+                               : std::min(2 * p + 1, n_qt - 1) + 1;
+    one[p] = {kCtaFixed + steps, BH};
+  }
+  for (int q = 0; q < n_qt; ++q) {
+    const int steps = causal ? n_qt - q : n_qt;
+    two[q] = {kCtaFixed + kPairStep * steps, (BH + 1) / 2};
+  }
+  std::sort(one, one + n_pairs, std::greater<>());
+  return list_makespan(two, n_qt, sms) < list_makespan(one, n_pairs, sms);
+}
+
+}  // namespace prefill
+
+const void *prefill_head_pairs_kernel_ptr(int dtype, bool one_tile) {
+  using prefill::prefill_kernel;
+  if (one_tile)
+    return dtype == FA_DTYPE_BF16
+               ? reinterpret_cast<const void *>(prefill_kernel<BF16, true, true>)
+               : reinterpret_cast<const void *>(prefill_kernel<F16, true, true>);
   return dtype == FA_DTYPE_BF16
-             ? reinterpret_cast<const void *>(prefill::prefill_kernel<BF16, true>)
-             : reinterpret_cast<const void *>(prefill::prefill_kernel<F16, true>);
+             ? reinterpret_cast<const void *>(prefill_kernel<BF16, true>)
+             : reinterpret_cast<const void *>(prefill_kernel<F16, true>);
 }
 const void *prefill_kernel_ptr(int dtype) {
   return dtype == FA_DTYPE_BF16
@@ -576,11 +676,18 @@ cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
   // One wave of CTAs: zig-zag pairs of equal causal work, so the kernel
   // does not wait on the heaviest pair. Several waves: heaviest first.
   const int zigzag = causal && grid <= static_cast<unsigned>(sms) ? 2 : 0;
-  if (n_qt == 1) {
-    // one tile per head: two heads per CTA
-    auto kernel = dtype == FA_DTYPE_BF16 ? prefill::prefill_kernel<BF16, true>
-                                         : prefill::prefill_kernel<F16, true>;
-    kernel<<<(BH + 1) / 2, prefill::kThreads, prefill::kSmemBytes, stream>>>(
+  const long long hp_ctas = static_cast<long long>((BH + 1) / 2) * n_qt;
+  const bool head_pairs = (n_qt & 1) && n_qt <= prefill::kMaxHeadPairTiles &&
+                          prefill::head_pairs_pay(BH, n_qt, causal, sms);
+  if (head_pairs) {
+    using prefill::prefill_kernel;
+    auto kernel = n_qt == 1 ? (dtype == FA_DTYPE_BF16
+                                   ? prefill_kernel<BF16, true, true>
+                                   : prefill_kernel<F16, true, true>)
+                            : (dtype == FA_DTYPE_BF16 ? prefill_kernel<BF16, true>
+                                                      : prefill_kernel<F16, true>);
+    kernel<<<static_cast<unsigned>(hp_ctas), prefill::kThreads,
+             prefill::kSmemBytes, stream>>>(
         tm_q, tm_k, tm_v, out, N, BH, causal ? 1 : 0, scale_log2, H,
         H / H_kv);
     return cudaGetLastError();

@@ -1,8 +1,10 @@
-"""Prefill of sequences that fit in one 128-row tile (N <= 128): the kernel
-then gives each CTA one tile of each of two heads. Edges: an odd number of
+"""Prefill with an odd number of 128-row query tiles (up to 7) over more
+than one wave of SMs: the kernel then gives each CTA the same tile of two
+heads, their K/V tiles interleaved in one ring. Edges: an odd number of
 (batch, head) units (the last CTA holds one head), grouped K/V heads (two
 heads of a pair may read different K/V heads), ragged N, both dtypes,
-against fp32 attention."""
+causal and full, against fp32 attention. The small shapes stay below one
+wave and take the one-head-per-CTA form; same bar."""
 
 import pytest
 import torch
@@ -24,8 +26,9 @@ def reference(q, k, v, causal, scale):
 @pytest.mark.parametrize("dtype,tol", [(torch.float16, 2e-3),
                                        (torch.bfloat16, 1.5e-2)])
 @pytest.mark.parametrize("b,h,h_kv", [(1, 1, 1), (3, 5, 5), (2, 7, 1),
-                                      (4, 6, 3), (64, 32, 32)])
-@pytest.mark.parametrize("n", [1, 64, 100, 128])
+                                      (4, 6, 3), (64, 32, 32), (5, 31, 31),
+                                      (3, 50, 10)])
+@pytest.mark.parametrize("n", [1, 64, 100, 128, 300, 384, 640, 896])
 @pytest.mark.parametrize("causal", [True, False])
 def test_short_prefill_matches_fp32(dtype, tol, b, h, h_kv, n, causal):
     torch.manual_seed(b * 100 + h * 10 + n)
