@@ -79,12 +79,14 @@ int ensure_device(int *device_out) {
                               decode_gqa_kernel_ptr(64, dt),
                               decode_gqa_kernel_ptr(128, dt),
                               prefill_head_pairs_kernel_ptr(dt),
-                              prefill_head_pairs_kernel_ptr(dt, true)};
+                              prefill_head_pairs_kernel_ptr(dt, true),
+                              prefill_d128_kernel_ptr(dt, true)};
     const int bytes[] = {prefill_smem_bytes(), decode_smem_bytes(),
                          decode_d128_smem_bytes(), prefill_d128_smem_bytes(),
                          decode_gqa_smem_bytes(64), decode_gqa_smem_bytes(128),
-                         prefill_smem_bytes(), prefill_smem_bytes()};
-    for (int i = 0; i < 8; ++i) {
+                         prefill_smem_bytes(), prefill_smem_bytes(),
+                         prefill_d128_smem_bytes()};
+    for (int i = 0; i < 9; ++i) {
       if (cudaFuncSetAttribute(big_smem[i],
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                bytes[i]) != cudaSuccess ||

@@ -24,7 +24,8 @@ cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
                                   cudaStream_t stream);
 
 // ---- prefill, head_dim 128 (prefill_d128_sm100.cu) -------------------------
-const void *prefill_d128_kernel_ptr(int dtype = FA_DTYPE_F16);
+const void *prefill_d128_kernel_ptr(int dtype = FA_DTYPE_F16,
+                                   bool head_pairs = false);
 int prefill_d128_smem_bytes();
 cudaError_t launch_prefill_d128_kernel(const CUtensorMap &tm_q,
                                        const CUtensorMap &tm_k,

@@ -20,8 +20,8 @@
 // 128-byte-swizzled halves (head dims 0-63 and 64-127) in separate blocks,
 // the layout TMA writes with one 64-column box per half:
 //   Q0, Q1  2 x [128 rows x 128 B] each            64 KiB
-//   K       3 stages x 2 x [64 keys x 128 B]        48 KiB
-//   V       3 stages x 2 x [64 keys x 128 B]        48 KiB
+//   K       4 slots x 2 x [64 keys x 128 B]         64 KiB (3 used with one head)
+//   V       4 slots x 2 x [64 keys x 128 B]         64 KiB
 // Tensor memory (512 columns x 128 lanes, fp32 words):
 //   S_t [64t, 64t+64)   O_t [128+128t, 256+128t)   P_t [384+32t, 416+32t)
 
@@ -42,7 +42,10 @@ constexpr int kHalfBytes = 128;  // one swizzled half-row (64 dims)
 constexpr int kBlockM = 128;     // query rows per tile
 constexpr int kBlockN = 64;      // keys per K/V tile
 constexpr int kTilesPerCta = 2;
-constexpr int kStages = 3;
+// K/V ring slots: one head per CTA cycles through 3 of them; two heads per
+// CTA (sequences of one query tile, at most two 64-key tiles per head) hold
+// all four of their K/V tiles at once.
+constexpr int kRingSlots = 4;
 constexpr int kSoftmaxThreads = 128;
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
@@ -58,12 +61,12 @@ constexpr uint32_t kKVTile = 2 * kKVHalf;           // 16 KiB
 
 constexpr uint32_t kQOff = 0;
 constexpr uint32_t kKOff = kQOff + kTilesPerCta * kQTile;
-constexpr uint32_t kVOff = kKOff + kStages * kKVTile;
-constexpr uint32_t kBarOff = kVOff + kStages * kKVTile;
+constexpr uint32_t kVOff = kKOff + kRingSlots * kKVTile;
+constexpr uint32_t kBarOff = kVOff + kRingSlots * kKVTile;
 constexpr int kBarQFull = 0;
 constexpr int kBarKFull = kBarQFull + 1;          // + stage: K and V tile
-constexpr int kBarKVEmpty = kBarKFull + kStages;  // + stage
-constexpr int kBarSFull = kBarKVEmpty + kStages;  // + tile
+constexpr int kBarKVEmpty = kBarKFull + kRingSlots;  // + stage
+constexpr int kBarSFull = kBarKVEmpty + kRingSlots;  // + tile
 constexpr int kBarSFree = kBarSFull + kTilesPerCta;
 constexpr int kBarPFull = kBarSFree + kTilesPerCta;
 constexpr int kBarODone = kBarPFull + kTilesPerCta;
@@ -72,6 +75,8 @@ constexpr int kNumBars = kBarDrain + 1;
 constexpr uint32_t kTmemSlotOff = kBarOff + kNumBars * 8;
 constexpr uint32_t kAbortOff = kTmemSlotOff + 4;
 constexpr uint32_t kSmemBytes = kAbortOff + 4 + 8;
+static_assert(kSmemBytes <= 227 * 1024,
+              "above the sm_100 per-CTA shared memory limit");
 
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemS = 0;    // + 64 * tile
@@ -139,7 +144,12 @@ __device__ __forceinline__ TileInfo tile_info(int pair, int t, int N,
   return ti;
 }
 
-template <typename Dt>
+// kHeadPairs (sequences of one 128-row query tile, N <= 128): the CTA's two
+// tile slots hold query tile 0 of two heads (2 * blockIdx.x and the next)
+// instead of two tiles of one head, whose second slot would stay empty. The
+// two heads' K/V streams interleave in the ring: key tile j of slot t is
+// ring position 2 j + t (position j with one head per CTA).
+template <typename Dt, bool kHeadPairs = false>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_d128_kernel(const __grid_constant__ CUtensorMap tm_q,
                         const __grid_constant__ CUtensorMap tm_k,
@@ -147,6 +157,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         __half *__restrict__ out, int N, int BH, int causal,
                         float scale_log2, int H, int group) {
   extern __shared__ __align__(1024) uint8_t smem[];
+  constexpr int kStages = kHeadPairs ? kRingSlots : 3;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
@@ -161,17 +172,43 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Heaviest causal pairs first, heads fastest.
   const int n_qt = (N + kBlockM - 1) / kBlockM;
   const int n_pairs = (n_qt + kTilesPerCta - 1) / kTilesPerCta;
-  const int pair = n_pairs - 1 - static_cast<int>(blockIdx.x / BH);
-  const int bh = static_cast<int>(blockIdx.x % BH);
+  const int pair =
+      kHeadPairs ? 0 : n_pairs - 1 - static_cast<int>(blockIdx.x / BH);
+  const int bh = kHeadPairs ? 2 * static_cast<int>(blockIdx.x)
+                            : static_cast<int>(blockIdx.x % BH);
+  const int bh1 = kHeadPairs ? bh + 1 : bh;  // query head of tile 1
   const int kv_bh = (bh / H) * (H / group) + (bh % H) / group;
-  const TileInfo t0 = tile_info(pair, 0, N, causal, zigzag);
-  const TileInfo t1 = tile_info(pair, 1, N, causal, zigzag);
+  const int kv_bh1 = (bh1 / H) * (H / group) + (bh1 % H) / group;
+  TileInfo t0 = tile_info(pair, 0, N, causal, zigzag);
+  TileInfo t1 = tile_info(pair, 1, N, causal, zigzag);
+  if (kHeadPairs) {
+    t1.qt = 0;
+    t1.n_kv = bh1 < BH ? t0.n_kv : 0;
+  }
   const int n_kv = t0.n_kv > t1.n_kv ? t0.n_kv : t1.n_kv;
 
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kBarOff);
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kTmemSlotOff);
   volatile uint32_t *abort_flag =
       reinterpret_cast<volatile uint32_t *>(smem + kAbortOff);
+
+  // Ring positions (tile 1's skipped when the CTA has one head); a
+  // position's stage is p % kStages.
+  const int n_pos = kHeadPairs ? 2 * n_kv : n_kv;
+  auto pos_used = [&](int p) { return !kHeadPairs || !(p & 1) || t1.n_kv > 0; };
+  auto load_pos = [&](int p) {
+    if (!pos_used(p)) return;
+    const int j = kHeadPairs ? p >> 1 : p;
+    const int kvh = (kHeadPairs && (p & 1)) ? kv_bh1 : kv_bh;
+    const int s = p % kStages;
+    mbar_arrive_expect_tx(&bars[kBarKFull + s], 2 * kKVTile);
+    for (int h = 0; h < 2; ++h) {
+      tma_load_3d(smem + kKOff + s * kKVTile + h * kKVHalf, &tm_k,
+                  &bars[kBarKFull + s], 64 * h, j * kBlockN, kvh);
+      tma_load_3d(smem + kVOff + s * kKVTile + h * kKVHalf, &tm_v,
+                  &bars[kBarKFull + s], 64 * h, j * kBlockN, kvh);
+    }
+  };
 
   // The producer lane sets up the barriers and issues the Q tiles and the
   // first kStages K/V tiles before the CTA-wide barrier (their latency
@@ -201,18 +238,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row0 = (t == 0 ? t0.qt : t1.qt) * kBlockM;
       for (int h = 0; h < 2; ++h)
         tma_load_3d(smem + kQOff + t * kQTile + h * kQHalf, &tm_q,
-                    &bars[kBarQFull], 64 * h, row0, bh);
+                    &bars[kBarQFull], 64 * h, row0, t ? bh1 : bh);
     }
-    for (; preissued < n_kv && preissued < kStages; ++preissued) {
-      const int s = preissued;
-      mbar_arrive_expect_tx(&bars[kBarKFull + s], 2 * kKVTile);
-      for (int h = 0; h < 2; ++h) {
-        tma_load_3d(smem + kKOff + s * kKVTile + h * kKVHalf, &tm_k,
-                    &bars[kBarKFull + s], 64 * h, preissued * kBlockN, kv_bh);
-        tma_load_3d(smem + kVOff + s * kKVTile + h * kKVHalf, &tm_v,
-                    &bars[kBarKFull + s], 64 * h, preissued * kBlockN, kv_bh);
-      }
-    }
+    for (; preissued < n_pos && preissued < kStages; ++preissued)
+      load_pos(preissued);
     *abort_flag = device_failed() ? 1u : 0u;
   }
   if (warp == kMmaWarp) {
@@ -231,28 +260,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---------------------------------------------------------------- TMA
       if (lane == 0) {
         int issued = preissued;
-        for (int j = preissued; j < n_kv; ++j) {
+        // (two heads per CTA: every position was issued above)
+        for (int p = preissued; !kHeadPairs && p < n_pos; ++p) {
           if (*abort_flag) break;
-          const int s = j % kStages;
-          const int use = j / kStages;
-          if (use > 0 && !mbar_wait(&bars[kBarKVEmpty + s], (use - 1) & 1)) {
+          const int s = p % kStages;
+          const int use = p / kStages;
+          if (pos_used(p) && use > 0 &&
+              !mbar_wait(&bars[kBarKVEmpty + s], (use - 1) & 1)) {
             *abort_flag = 1;
             break;
           }
-          mbar_arrive_expect_tx(&bars[kBarKFull + s], 2 * kKVTile);
-          for (int h = 0; h < 2; ++h) {
-            tma_load_3d(smem + kKOff + s * kKVTile + h * kKVHalf, &tm_k,
-                        &bars[kBarKFull + s], 64 * h, j * kBlockN, kv_bh);
-            tma_load_3d(smem + kVOff + s * kKVTile + h * kKVHalf, &tm_v,
-                        &bars[kBarKFull + s], 64 * h, j * kBlockN, kv_bh);
-          }
-          issued = j + 1;
+          load_pos(p);
+          issued = p + 1;
         }
         if (*abort_flag) {
           mbar_wait(&bars[kBarQFull], 0);
-          for (int j = (issued > kStages ? issued - kStages : 0); j < issued;
-               ++j)
-            mbar_wait(&bars[kBarKFull + j % kStages], (j / kStages) & 1);
+          for (int p = (issued > kStages ? issued - kStages : 0); p < issued;
+               ++p)
+            if (pos_used(p))
+              mbar_wait(&bars[kBarKFull + p % kStages], (p / kStages) & 1);
         }
       }
     } else if (warp == kMmaWarp) {
@@ -262,8 +288,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n_t[2] = {t0.n_kv, t1.n_kv};
       const uint64_t desc0 = sw128_desc(sbase);
       const uint64_t vdesc0 = sw128_desc_lbo(sbase, kKVHalf);
+      // ring position of key tile j of slot t
+      auto kpos = [&](int t, int j) { return kHeadPairs ? 2 * j + t : j; };
+      // with two heads, tile 1's first K/V tile has its own ring position
       bool ok = mbar_wait(&bars[kBarQFull], 0) &&
-                mbar_wait(&bars[kBarKFull + 0], 0);
+                mbar_wait(&bars[kBarKFull + 0], 0) &&
+                (!kHeadPairs || n_t[1] == 0 ||
+                 mbar_wait(&bars[kBarKFull + 1], 0));
       if (ok) {
         tc_fence_after();
         if (leader) {
@@ -271,7 +302,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (n_t[t] == 0) continue;
             issue_s_tile<Dt>(tmem + kTmemS + 64 * t,
                          desc0 + ((kQOff + t * kQTile) >> 4),
-                         desc0 + (kKOff >> 4));
+                         desc0 + ((kKOff + kpos(t, 0) * kKVTile) >> 4));
             mma_commit(&bars[kBarSFull + t]);
           }
         }
@@ -282,16 +313,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        const int s = j % kStages;
-        const int s1 = (j + 1) % kStages;
 #pragma unroll
         for (int t = 0; t < kTilesPerCta; ++t) {
           const int nt = n_t[t];
           if (!ok || j >= nt) continue;
+          const int s = kpos(t, j) % kStages;  // K_j, V_j of this slot
+          const int p1 = kpos(t, j + 1);
+          const int s1 = p1 % kStages;         // K_{j+1}
           if (j + 1 < nt) {
-            const bool need_kv = (t == 0) || (n_t[0] <= j + 1);
+            // K/V tile j+1 is waited on once per round (by the first tile
+            // that uses it, or by each slot with two heads)
+            const bool need_kv = kHeadPairs || (t == 0) || (n_t[0] <= j + 1);
             if ((need_kv &&
-                 !mbar_wait(&bars[kBarKFull + s1], ((j + 1) / kStages) & 1)) ||
+                 !mbar_wait(&bars[kBarKFull + s1], (p1 / kStages) & 1)) ||
                 !mbar_wait(&bars[kBarSFree + t], j & 1)) {
               ok = false;
               continue;
@@ -318,7 +352,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
         }
         if (!ok) break;
-        if (leader) mma_commit(&bars[kBarKVEmpty + s]);
+        // release round j's ring positions (both slots' with two heads)
+        if (leader) {
+          mma_commit(&bars[kBarKVEmpty + kpos(0, j) % kStages]);
+          if (kHeadPairs) mma_commit(&bars[kBarKVEmpty + kpos(1, j) % kStages]);
+        }
         __syncwarp();
       }
       if (!ok && leader) *abort_flag = 1;
@@ -449,7 +487,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const float inv_l = (l_sum > 0.f) ? 1.f / l_sum : 0.f;
         uint4 *dst = reinterpret_cast<uint4 *>(
-            out + (static_cast<size_t>(bh) * N + q_row) * kD);
+            out + (static_cast<size_t>(t ? bh1 : bh) * N + q_row) * kD);
 #pragma unroll
         for (int h = 0; h < kD / 32; ++h) {
           uint32_t o[32];
@@ -488,12 +526,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace prefill128
 
-const void *prefill_d128_kernel_ptr(int dtype) {
+const void *prefill_d128_kernel_ptr(int dtype, bool head_pairs) {
+  using prefill128::prefill_d128_kernel;
+  if (head_pairs)
+    return dtype == FA_DTYPE_BF16
+               ? reinterpret_cast<const void *>(prefill_d128_kernel<BF16, true>)
+               : reinterpret_cast<const void *>(prefill_d128_kernel<F16, true>);
   return dtype == FA_DTYPE_BF16
-             ? reinterpret_cast<const void *>(
-                   prefill128::prefill_d128_kernel<BF16>)
-             : reinterpret_cast<const void *>(
-                   prefill128::prefill_d128_kernel<F16>);
+             ? reinterpret_cast<const void *>(prefill_d128_kernel<BF16>)
+             : reinterpret_cast<const void *>(prefill_d128_kernel<F16>);
 }
 int prefill_d128_smem_bytes() {
   return static_cast<int>(prefill128::kSmemBytes);
@@ -515,6 +556,19 @@ cudaError_t launch_prefill_d128_kernel(const CUtensorMap &tm_q,
   // One wave of CTAs: zig-zag pairs of equal causal work, so the kernel
   // does not wait on the heaviest pair. Several waves: heaviest first.
   const int zigzag = causal && grid <= static_cast<unsigned>(sms) ? 2 : 0;
+  // One query tile per head (N <= 128): query tile 0 of two heads per CTA,
+  // once the one-head grid no longer fits one wave of SMs (below that the
+  // heads run side by side on idle SMs instead).
+  if (n_qt == 1 && grid > static_cast<unsigned>(sms)) {
+    auto kernel = dtype == FA_DTYPE_BF16
+                      ? prefill128::prefill_d128_kernel<BF16, true>
+                      : prefill128::prefill_d128_kernel<F16, true>;
+    kernel<<<static_cast<unsigned>((BH + 1) / 2), prefill128::kThreads,
+             prefill128::kSmemBytes, stream>>>(
+        tm_q, tm_k, tm_v, out, N, BH, causal ? 1 : 0, scale_log2, H,
+        H / H_kv);
+    return cudaGetLastError();
+  }
   auto kernel = dtype == FA_DTYPE_BF16 ? prefill128::prefill_d128_kernel<BF16>
                                        : prefill128::prefill_d128_kernel<F16>;
   kernel<<<grid, prefill128::kThreads, prefill128::kSmemBytes, stream>>>(

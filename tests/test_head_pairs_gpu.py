@@ -39,3 +39,24 @@ def test_short_prefill_matches_fp32(dtype, tol, b, h, h_kv, n, causal):
     err = (got.float() - reference(q, k, v, causal, 0.125)).abs().max().item()
     assert err <= tol, err
     assert flashattn_cuda.take_device_error() == 0
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float16, 2e-3),
+                                       (torch.bfloat16, 1.5e-2)])
+@pytest.mark.parametrize("b,h,h_kv", [(1, 1, 1), (3, 5, 5), (64, 32, 32),
+                                      (5, 31, 31), (3, 50, 10)])
+@pytest.mark.parametrize("n", [1, 64, 65, 100, 128])
+@pytest.mark.parametrize("causal", [True, False])
+def test_short_prefill_d128_matches_fp32(dtype, tol, b, h, h_kv, n, causal):
+    """head_dim 128, one query tile per head: above one wave of SMs the
+    kernel takes query tile 0 of two heads per CTA (one or two 64-key K/V
+    tiles per head)."""
+    torch.manual_seed(b * 100 + h * 10 + n + 1)
+    q = torch.randn(b, h, n, 128, device="cuda").to(dtype)
+    k = torch.randn(b, h_kv, n, 128, device="cuda").to(dtype)
+    v = torch.randn(b, h_kv, n, 128, device="cuda").to(dtype)
+    scale = 128 ** -0.5
+    got = flashattn_cuda.prefill(q, k, v, causal, scale)
+    err = (got.float() - reference(q, k, v, causal, scale)).abs().max().item()
+    assert err <= tol, err
+    assert flashattn_cuda.take_device_error() == 0
