@@ -27,6 +27,10 @@ CASES = {
     "prefill_c2_causal": ("prefill", (8, 12, 1024), True, None),
     "prefill_c2_full": ("prefill", (8, 12, 1024), False, None),
     "prefill_small": ("prefill", (1, 8, 2048), True, None),
+    # two heads per CTA: one query tile each (N <= 128), and three tiles
+    "prefill_pairs_n128": ("prefill", (64, 32, 128), True, None),
+    "prefill_pairs_n384": ("prefill", (64, 32, 384), True, None),
+    "prefill_d128_pairs_n128": ("prefill_d128", (64, 32, 128), True, None),
     # config 3's shape at head_dim 128
     "prefill_d128_c3": ("prefill_d128", (4, 14, 4096), True, None),
     "decode_c4": ("decode", (64, 12, 8192), None, None),
