@@ -45,12 +45,13 @@ def test_short_prefill_matches_fp32(dtype, tol, b, h, h_kv, n, causal):
                                        (torch.bfloat16, 1.5e-2)])
 @pytest.mark.parametrize("b,h,h_kv", [(1, 1, 1), (3, 5, 5), (64, 32, 32),
                                       (5, 31, 31), (3, 50, 10)])
-@pytest.mark.parametrize("n", [1, 64, 65, 100, 128])
+@pytest.mark.parametrize("n", [1, 64, 65, 100, 128, 300, 384, 640])
 @pytest.mark.parametrize("causal", [True, False])
 def test_short_prefill_d128_matches_fp32(dtype, tol, b, h, h_kv, n, causal):
-    """head_dim 128, one query tile per head: above one wave of SMs the
-    kernel takes query tile 0 of two heads per CTA (one or two 64-key K/V
-    tiles per head)."""
+    """head_dim 128 with an odd number of query tiles (1, 3 or 5). With one
+    tile above one wave of SMs the kernel takes query tile 0 of two heads
+    per CTA (one or two 64-key K/V tiles per head); longer sequences keep
+    one head per CTA, whose last CTA holds a lone tile."""
     torch.manual_seed(b * 100 + h * 10 + n + 1)
     q = torch.randn(b, h, n, 128, device="cuda").to(dtype)
     k = torch.randn(b, h_kv, n, 128, device="cuda").to(dtype)
