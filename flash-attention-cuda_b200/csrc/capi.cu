@@ -396,7 +396,8 @@ size_t fa_exchange_bytes_hd(int B, int H, int world, int head_dim) {
   if (B <= 0 || H <= 0 || world <= 0 || world > 32) return 0;
   if (head_dim != FA_HEAD_DIM && head_dim != 128) return 0;
   const size_t bh = static_cast<size_t>(B) * H;
-  return align_up(bh * world * (4 + head_dim) * sizeof(float) +
+  // two banks of partials (alternate epochs) + one counter per segment
+  return align_up(2 * bh * world * (4 + head_dim) * sizeof(float) +
                       bh * sizeof(uint32_t),
                   256);
 }
@@ -807,6 +808,17 @@ int fa_take_device_error(unsigned int *bits) {
       cudaMemcpyToSymbol(g_fa_error_word, &zero, sizeof(zero)) != cudaSuccess)
     return FA_ECUDA;
   *bits = v;
+  return FA_OK;
+}
+
+int fa_set_wait_limit_ns(unsigned long long ns) {
+  if (ns < 1000ull || ns > 60000000000ull) return FA_EINVAL;
+  int dev = 0;
+  const int rc = ensure_device(&dev);
+  if (rc != FA_OK) return rc;
+  if (cudaDeviceSynchronize() != cudaSuccess ||
+      cudaMemcpyToSymbol(g_fa_wait_limit_ns, &ns, sizeof(ns)) != cudaSuccess)
+    return FA_ECUDA;
   return FA_OK;
 }
 

@@ -179,16 +179,27 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
   return v;
 }
 
-// Exchange buffer of rank r for head_dim D: (x_world, B*H, 4 + D) fp32
-// partials, then B*H uint32 arrival counters.
+// Exchange buffer of rank r for head_dim D: two banks of (x_world, B*H,
+// 4 + D) fp32 partials, then B*H uint32 arrival counters. Epoch e writes
+// bank e & 1. A rank can start epoch e + 1 (and store into the other bank)
+// while a peer still reads bank e & 1 of epoch e; it cannot reach epoch
+// e + 2 before every peer has finished epoch e, because finishing e + 1
+// needs every peer's e + 1 partials, which a peer sends only after its
+// epoch-e launch has completed on its stream.
+template <int D>
+__device__ __forceinline__ float *x_bank(const DecodeArgs &a, int r) {
+  return a.x_peers[r] + static_cast<size_t>(a.x_epoch & 1u) * a.x_world *
+                            a.B * a.H * (4 + D);
+}
+
 template <int D>
 __device__ __forceinline__ uint32_t *x_counters(const DecodeArgs &a, int r) {
   return reinterpret_cast<uint32_t *>(
-      a.x_peers[r] + static_cast<size_t>(a.x_world) * a.B * a.H * (4 + D));
+      a.x_peers[r] + 2 * static_cast<size_t>(a.x_world) * a.B * a.H * (4 + D));
 }
 
 // Whole warp: stores this rank's (m, l, acc) of segment g into slot
-// [x_rank][g] of every rank's buffer (peer memory over NVLink, plain
+// [x_rank][g] of this epoch's bank in every rank's buffer (peer memory over NVLink, plain
 // stores), then raises each rank's counter of g. Lane l holds dims
 // l + 32 i.
 template <int D>
@@ -196,7 +207,7 @@ __device__ void x_send(const DecodeArgs &a, size_t g, float M, float L,
                        const float (&A)[D / 32], int lane) {
   const size_t BH = static_cast<size_t>(a.B) * a.H;
   for (int r = 0; r < a.x_world; ++r) {
-    float *dst = a.x_peers[r] + (static_cast<size_t>(a.x_rank) * BH + g) * (4 + D);
+    float *dst = x_bank<D>(a, r) + (static_cast<size_t>(a.x_rank) * BH + g) * (4 + D);
 #pragma unroll
     for (int i = 0; i < D / 32; ++i) dst[4 + 32 * i + lane] = A[i];
     if (lane == 0) {
@@ -221,11 +232,13 @@ __device__ void x_finish(const DecodeArgs &a, size_t g, int lane) {
   int ok = 1;
   if (lane == 0) {
     unsigned long long t0 = 0;
+    const unsigned long long limit = wait_limit_ns();
     while (static_cast<int>(ld_acquire_sys(ctr) - target) < 0) {
       const unsigned long long now = global_timer_ns();
       if (t0 == 0) {
         t0 = now;
-      } else if (now - t0 > kWaitLimitNs) {
+      } else if (now - t0 > limit || device_failed()) {
+        // out of time, or another wait already ran out: give up at once
         record_error(FA_ERR_TIMEOUT);
         ok = 0;
         break;
@@ -235,7 +248,7 @@ __device__ void x_finish(const DecodeArgs &a, size_t g, int lane) {
   ok = __shfl_sync(0xffffffffu, ok, 0);
   if (!ok) return;
   (void)ld_acquire_sys(ctr);  // order this lane's reads after the arrivals
-  const float *base = a.x_peers[a.x_rank];
+  const float *base = x_bank<D>(a, a.x_rank);
   float M = kNegBig;
   for (int r = 0; r < a.x_world; ++r) {
     const float *p = base + (static_cast<size_t>(r) * BH + g) * (4 + D);

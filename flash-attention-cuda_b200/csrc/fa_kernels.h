@@ -52,7 +52,8 @@ struct DecodeArgs {
   __half *k_cache_w;
   __half *v_cache_w;
   // cross-GPU exchange (null when not sharded): x_peers[r] is rank r's
-  // exchange buffer, (x_world, B*H, 68) fp32 partials then B*H uint32
+  // exchange buffer, two epoch-parity banks of (x_world, B*H, 4 + D) fp32
+  // partials then B*H uint32
   // arrival counters; each finished segment is sent to every rank and the
   // merged output written once all x_world partials of it are present
   // (counters reach x_epoch * x_world)

@@ -22,9 +22,16 @@ namespace fa {
 constexpr int kHeadDim = 64;
 constexpr int kRowBytes = kHeadDim * 2;  // one fp16 row of K, V, Q or O
 
-// Longest a single wait on an mbarrier may spin before the kernel gives up,
-// records FA_ERR_TIMEOUT and unwinds. Normal waits last microseconds.
+// Longest a single wait (on an mbarrier or a peer's counter) may spin before
+// the kernel gives up, records FA_ERR_TIMEOUT and unwinds. Normal waits last
+// microseconds. The default is 1 s; fa_set_wait_limit_ns changes it (tests
+// shorten it to make a wait run out in milliseconds).
 constexpr unsigned long long kWaitLimitNs = 1000000000ull;  // 1 s
+__device__ unsigned long long g_fa_wait_limit_ns = kWaitLimitNs;
+
+__device__ __forceinline__ unsigned long long wait_limit_ns() {
+  return *reinterpret_cast<volatile unsigned long long *>(&g_fa_wait_limit_ns);
+}
 
 // Device-wide error word, OR-ed with FA_ERR_* bits by any kernel that has to
 // abandon its work. Read and cleared from the host by fa_take_device_error().
@@ -127,19 +134,20 @@ __device__ __forceinline__ bool mbar_test_wait(uint32_t addr, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity to complete. Returns false (and
-// records FA_ERR_TIMEOUT) if it has not completed within kWaitLimitNs, so a
+// records FA_ERR_TIMEOUT) if it has not completed within wait_limit_ns(), so a
 // lost arrival turns into an error status instead of a hung GPU.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_test_wait(addr, parity)) return true;
   if (mbar_try_wait(addr, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
+  const unsigned long long limit = wait_limit_ns();
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 32; ++i) {
       if (mbar_try_wait(addr, parity)) return true;
     }
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
+    if (global_timer_ns() - t0 > limit) {
       record_error(FA_ERR_TIMEOUT);
       return false;
     }

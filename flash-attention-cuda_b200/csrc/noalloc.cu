@@ -56,12 +56,17 @@ int scratch_address(int dev, uint8_t **out) {
   std::lock_guard<std::mutex> lock(g_mutex);
   DeviceScratch &d = g_scratch_of[dev];
   if (!d.ready) {
+    // A failed look-up is not cached: the next call on this device tries
+    // again instead of failing for the rest of the process.
     void *p = nullptr;
     d.status = cudaGetSymbolAddress(&p, g_scratch);
+    if (d.status != cudaSuccess || p == nullptr) {
+      cudaGetLastError();  // clear the runtime's last-error record
+      return FA_ECUDA;
+    }
     d.ptr = static_cast<uint8_t *>(p);
     d.ready = true;
   }
-  if (d.status != cudaSuccess || d.ptr == nullptr) return FA_ECUDA;
   *out = d.ptr;
   return FA_OK;
 }
@@ -77,6 +82,13 @@ extern "C" int fa_decode_noalloc(const void *q, const void *k_cache,
   if (B <= 0 || H <= 0) return FA_EINVAL;
   if (static_cast<long long>(B) * H > noalloc::kMaxSegments)
     return FA_ENOSPACE;  // beyond the fixed scratch array
+  // The checks run_decode makes, made here too so a rejected call writes
+  // nothing to the shared array (the counter clear below comes first).
+  if (!decode_shape_ok(B, H, S_max, scale)) return FA_EINVAL;
+  if (!q || !k_cache || !v_cache || !seq_lens || !o) return FA_EINVAL;
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) ||
+      !aligned16(o) || (reinterpret_cast<uintptr_t>(seq_lens) & 3u))
+    return FA_EALIGN;
   int dev = 0;
   int rc = ensure_device(&dev);
   if (rc != FA_OK) return rc;

@@ -232,7 +232,10 @@ int fa_decode_hd(const void *q, const void *k_cache, const void *v_cache,
  * ranks, starting at 1 and increasing by one per call. Each finished
  * (b, h) partial (m, l, acc[64]) is stored into every rank's buffer over
  * NVLink and counted; each rank then merges all ranks' partials (waits are
- * bounded) and writes the full (B, H, 1, 64) output. Replaces the
+ * bounded) and writes the full (B, H, 1, 64) output. Partials of odd and
+ * even epochs go to separate banks of the buffer, so a rank that has moved
+ * on to the next call never overwrites a partial a slower peer still reads;
+ * each rank must issue its calls in one stream order. Replaces the
  * reference-named exchange (decode_partial + NCCL all-gather + merge, the
  * (m, l, o) combine of csrc/decode.cu:143-175 across GPUs). After a
  * device error the buffers and epochs must be re-created.
@@ -405,6 +408,16 @@ int fa_occupancy(fa_occupancy_entry *out, int max_entries, int *count);
  * bounded waits.
  */
 int fa_take_device_error(unsigned int *bits);
+
+/*
+ * Sets how long any single device-side wait (a pipeline mbarrier, or a
+ * peer's arrival counter in fa_decode_exchange) may spin on the current
+ * device before the kernel records FA_ERR_TIMEOUT and unwinds; ns in
+ * [1e3, 6e10], default 1e9 (1 s). Synchronises the device first. A host
+ * that detects lost peers sooner, or a test that makes a wait run out on
+ * purpose, shortens it. No reference counterpart (no bounded waits there).
+ */
+int fa_set_wait_limit_ns(unsigned long long ns);
 
 /*
  * Single-head fp32 attention O = softmax(Q K^T / 8) V on (N, 64) fp32

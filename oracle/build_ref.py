@@ -22,7 +22,11 @@ import sysconfig
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT_DIR = os.path.join(HERE, "_ref")
-REFERENCE = os.environ.get("FA_REFERENCE", "/root/reference")
+# The reference checkout: $FA_REFERENCE, else a "reference" folder beside
+# this repository.
+REFERENCE = os.environ.get(
+    "FA_REFERENCE",
+    os.path.normpath(os.path.join(HERE, os.pardir, os.pardir, "reference")))
 MODULE = "ref_flashattn_C"
 # setup.py:14-20 of the reference lists these sources.
 SOURCES = [

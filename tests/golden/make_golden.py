@@ -75,7 +75,11 @@ def _load_reference(ref_root):
 
 def main():
     import torch
-    ref_root = os.environ.get("FA_REFERENCE", "/root/reference")
+    # $FA_REFERENCE, else a "reference" checkout beside this repository.
+    here = os.path.dirname(os.path.abspath(__file__))
+    ref_root = os.environ.get(
+        "FA_REFERENCE",
+        os.path.normpath(os.path.join(here, *[os.pardir] * 3, "reference")))
     attention_cpu, sdpa_reference, decode_reference = _load_reference(ref_root)
     out = {}
 

@@ -171,7 +171,7 @@ def test_exchange_buffer_size(lib):
     lib.fa_exchange_bytes.argtypes = [ctypes.c_int] * 3
     for b, h, w in [(1, 14, 8), (64, 12, 2), (3, 5, 1)]:
         n = lib.fa_exchange_bytes(b, h, w)
-        need = b * h * w * 68 * 4 + b * h * 4
+        need = 2 * b * h * w * 68 * 4 + b * h * 4
         assert need <= n < need + 256 and n % 256 == 0
     assert lib.fa_exchange_bytes(1, 14, 0) == 0
     assert lib.fa_exchange_bytes(1, 14, 33) == 0
@@ -180,7 +180,7 @@ def test_exchange_buffer_size(lib):
     for b, h, w in [(1, 14, 8), (3, 5, 2)]:
         assert lib.fa_exchange_bytes_hd(b, h, w, 64) == lib.fa_exchange_bytes(b, h, w)
         n = lib.fa_exchange_bytes_hd(b, h, w, 128)
-        need = b * h * w * 132 * 4 + b * h * 4
+        need = 2 * b * h * w * 132 * 4 + b * h * 4
         assert need <= n < need + 256 and n % 256 == 0
     assert lib.fa_exchange_bytes_hd(1, 14, 8, 96) == 0
 
@@ -249,3 +249,9 @@ def test_dtype_entry_points_reject_bad_arguments_without_a_device(lib):
                             p, 2, None) == FA_EINVAL
     assert lib.fa_decode_ex(p, p, p, p, None, 1, 2, 2, 8, 64, 1, 0.1, p, 1 << 20,
                             p, 2, None) == FA_EINVAL
+
+
+def test_wait_limit_range_is_checked_on_the_host(lib):
+    lib.fa_set_wait_limit_ns.argtypes = [ctypes.c_ulonglong]
+    assert lib.fa_set_wait_limit_ns(10) == 1  # FA_EINVAL: below 1 us
+    assert lib.fa_set_wait_limit_ns(10 ** 12) == 1  # above 60 s

@@ -123,3 +123,59 @@ def test_two_rank_exchange_equals_unsharded():
     assert sorted(result.keys()) == [0, 1]
     for r in (0, 1):
         assert 0.0 <= result[r] <= 1e-3, result[r]
+
+
+def _many_epochs_worker(rank, world, port, result):
+    """Back-to-back epochs with no host sync between them, new queries and
+    lengths every epoch, and sequences that have no rows on one rank (their
+    partials are sent before streaming, merged after): a rank that runs
+    ahead must never overwrite a partial a slower peer still merges."""
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("nccl", rank=rank, world_size=world)
+    try:
+        g = torch.Generator().manual_seed(5)
+        b, h, s, steps = 6, 8, 8192, 24
+        k = torch.randn(b, h, s, 64, generator=g).half()
+        v = torch.randn(b, h, s, 64, generator=g).half()
+        c0, c1 = fadist.seq_shard(s, world, rank)
+        kl = k[:, :, c0:c1].contiguous().cuda()
+        vl = v[:, :, c0:c1].contiguous().cuda()
+        qs, ls, outs = [], [], []
+        xchg = fadist.PeerExchange(b, h)
+        for step in range(steps):
+            q = torch.randn(b, h, 1, 64, generator=g).half().cuda()
+            # short sequences live on rank 0 only; long ones span both
+            lens = torch.randint(1, s + 1, (b,), generator=g, dtype=torch.int32)
+            lens[step % b] = 1 + step
+            lens[(step + 1) % b] = 0
+            ll = torch.as_tensor(fadist.local_seq_lens(lens.tolist(), c0, c1),
+                                 dtype=torch.int32).cuda()
+            qs.append(q)
+            ls.append(lens)
+            outs.append(fadist.sharded_decode_fused(q, kl, vl, ll, SCALE, xchg))
+        torch.cuda.synchronize()
+        xchg.close()
+        kc, vc = k.cuda(), v.cuda()
+        err = 0.0
+        for q, lens, o in zip(qs, ls, outs):
+            want = flashattn_cuda.decode(q, kc, vc, lens.cuda(), SCALE)
+            err = max(err, (o.float() - want.float()).abs().max().item())
+        result[rank] = err if flashattn_cuda.take_device_error() == 0 else -1.0
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_rank_exchange_many_back_to_back_epochs():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    result = ctx.Manager().dict()
+    mp.start_processes(_many_epochs_worker, args=(2, 29619, result), nprocs=2,
+                       start_method="spawn")
+    assert sorted(result.keys()) == [0, 1]
+    for r in (0, 1):
+        assert 0.0 <= result[r] <= 1e-3, result[r]

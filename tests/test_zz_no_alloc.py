@@ -90,3 +90,57 @@ def test_noalloc_matches_fa_decode_on_consecutive_calls():
     bits = ctypes.c_uint(1)
     assert lib.fa_take_device_error(ctypes.byref(bits)) == FA_OK
     assert bits.value == 0
+
+
+@pytest.mark.gpu
+@requires_gpu
+def test_noalloc_at_the_array_limit():
+    """B * H exactly at the limit uses the array's last counter and partial
+    slots; the result must still equal fa_decode's."""
+    lib = _lib()
+    ptr = lambda t: ctypes.c_void_p(t.data_ptr())
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    gen = torch.Generator(device="cuda").manual_seed(7)
+    B, H, S = 512, 16, 96
+    assert B * H == MAX_BH
+    q = torch.randn(B, H, 1, 64, generator=gen, device="cuda").half()
+    k = torch.randn(B, H, S, 64, generator=gen, device="cuda").half()
+    v = torch.randn(B, H, S, 64, generator=gen, device="cuda").half()
+    lens = torch.randint(0, S + 1, (B,), generator=gen, device="cuda",
+                         dtype=torch.int32)
+    nbytes = lib.fa_decode_workspace_bytes(B, H, S, 0,
+                                           torch.cuda.current_device())
+    ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    counters = torch.zeros(B * H, dtype=torch.int32, device="cuda")
+    want = torch.full_like(q, float("nan"))
+    assert lib.fa_decode(ptr(q), ptr(k), ptr(v), ptr(lens), ptr(want), B, H,
+                         S, SCALE, 0, ptr(ws), nbytes, ptr(counters), B * H,
+                         stream) == FA_OK
+    for _ in range(2):
+        got = torch.full_like(q, float("nan"))
+        assert lib.fa_decode_noalloc(ptr(q), ptr(k), ptr(v), ptr(lens),
+                                     ptr(got), B, H, S, SCALE,
+                                     stream) == FA_OK
+        torch.cuda.synchronize()
+        assert not torch.isnan(got).any()
+        assert (got.float() - want.float()).abs().max().item() <= TOL
+    bits = ctypes.c_uint(1)
+    assert lib.fa_take_device_error(ctypes.byref(bits)) == FA_OK
+    assert bits.value == 0
+
+
+@pytest.mark.gpu
+@requires_gpu
+def test_noalloc_rejects_bad_pointers_and_sizes():
+    """Misaligned pointers and empty caches are refused with the same codes
+    fa_decode gives; the checks run before the shared counters are cleared."""
+    lib = _lib()
+    q = torch.zeros(2, 2, 1, 64, device="cuda").half()
+    kv = torch.zeros(2, 2, 8, 64, device="cuda").half()
+    lens = torch.full((2,), 8, dtype=torch.int32, device="cuda")
+    bad = ctypes.c_void_p(q.data_ptr() + 2)
+    p = lambda t: ctypes.c_void_p(t.data_ptr())
+    assert lib.fa_decode_noalloc(bad, p(kv), p(kv), p(lens), p(q), 2, 2, 8,
+                                 SCALE, None) == 2  # FA_EALIGN
+    assert lib.fa_decode_noalloc(p(q), p(kv), p(kv), p(lens), p(q), 2, 2, 0,
+                                 SCALE, None) == 1  # FA_EINVAL (S_max 0)
