@@ -88,7 +88,13 @@ constexpr uint32_t kIdescS = idesc_f16_f32(kBlockM, kBlockN, false, Dt::kFmt);
 template <typename Dt>
 constexpr uint32_t kIdescPV = idesc_f16_f32(kBlockM, kD, true, Dt::kFmt);
 constexpr float kRescaleThreshold = 8.0f;
-constexpr int kMufuPairsOf4 = 2;
+#ifndef FA_D128_MASK8
+#define FA_D128_MASK8 0x3B
+#endif
+// Bit i set: column pair i of every 8 takes its exponentials from the MUFU
+// unit, the others from the polynomial on the FMA pipe (the same balance as
+// the head_dim-64 kernel).
+constexpr unsigned kMufuMask8 = FA_D128_MASK8;
 
 // S = Q K^T for one 128x64 tile: 8 MMAs of K=16; steps 0-3 read the first
 // 64-dim half of Q and K, steps 4-7 the second half (a separate block).
@@ -438,17 +444,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float neg_m = -m_use;
       const float2 sl2 = make_float2(sl, sl);
       const float2 nm2 = make_float2(neg_m, neg_m);
+      // polynomial argument in clamped affine form (exp2_poly2_affine)
+      const float xa = sl * (1.f / kExp2Span);
+      const float xb = (neg_m - kExp2Lo) * (1.f / kExp2Span);
       float2 rs[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) rs[i] = make_float2(0.f, 0.f);
       uint32_t pk[32];
 #pragma unroll
       for (int c = 0; c < kBlockN; c += 2) {
-        const float2 x = ffma2(make_float2(s[c], s[c + 1]), sl2, nm2);
         float2 p;
-        if (((c >> 1) & 3) >= kMufuPairsOf4) {
-          p = exp2_poly2(x);
+        if (!((kMufuMask8 >> ((c >> 1) & 7)) & 1)) {
+          p = exp2_poly2_affine(
+              make_float2(fma_sat(s[c], xa, xb), fma_sat(s[c + 1], xa, xb)));
         } else {
+          const float2 x = ffma2(make_float2(s[c], s[c + 1]), sl2, nm2);
           p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
         }
         rs[(c >> 1) & 3] = fadd2(rs[(c >> 1) & 3], p);
