@@ -205,7 +205,17 @@ class Timer:
         self.barrier()
         torch.cuda.synchronize()
         total = sum(s.elapsed_time(e) for s, e in evs)
-        return self.max_over_ranks(total)
+        self.last_all = self.all_ranks(total)
+        return max(self.last_all)
+
+    def all_ranks(self, x):
+        """x from every rank, in rank order."""
+        if self.world == 1:
+            return [x]
+        t = self.torch.tensor([x], dtype=self.torch.float64, device="cuda")
+        out = [self.torch.zeros_like(t) for _ in range(self.world)]
+        self.dist.all_gather(out, t)
+        return [float(o.item()) for o in out]
 
 
 # ---------------------------------------------------------------------------
@@ -245,6 +255,13 @@ def run_ours(args, rank, world, local_rank):
         total_ms = timer.run(step, args.steps, args.warmup)
         launches += args.steps
         ms = total_ms / args.steps
+        sms = torch.cuda.get_device_properties(local_rank).multi_processor_count
+        per_rank = {
+            "prefill_ms": [round(x / args.steps, 5) for x in timer.last_all],
+            "prefill_heads": [shard_range(bh, world, r)[1] - shard_range(bh, world, r)[0]
+                              for r in range(world)],
+            # one CTA per (head, query-tile pair), one CTA per SM at a time
+            "prefill_ctas_rank0": units * ((n + 255) // 256), "sms": sms}
         flops_total = prefill_flops(C3["B"], C3["H"], n, True)
         value = flops_total / (ms * 1e-3) / 1e12
         flops_rank = prefill_flops(1, units, n, True)
@@ -281,6 +298,19 @@ def run_ours(args, rank, world, local_rank):
         launches += args.steps
         h2d = 3 * hq.numel() * 2 * world
         d2h = hq.numel() * 2 * world
+        # the link itself: one pinned upload of the step's inputs and one
+        # download of its output, each alone, device-timed
+        dbuf = torch.empty(3 * hq.numel(), dtype=torch.float16, device="cuda")
+        hbuf = torch.empty_like(dbuf, device="cpu").pin_memory()
+        up_ms = timer.run(lambda: dbuf.copy_(hbuf, non_blocking=True),
+                          args.steps, args.warmup, flush=False) / args.steps
+        down_ms = timer.run(
+            lambda: hout.view(-1).copy_(dbuf[:hq.numel()], non_blocking=True),
+            args.steps, args.warmup, flush=False) / args.steps
+        del dbuf, hbuf
+        # uploads and downloads overlap in fa_prefill_host (PCIe is full
+        # duplex), so the link bound of a step is the longer of the two
+        link_ms = max(up_ms, down_ms)
         del q, k, v
 
         # ---------------- secondary: C2 prefill (replicated per rank) -----
@@ -315,6 +345,9 @@ def run_ours(args, rank, world, local_rank):
         bytes_all = int(all_lens.sum()) * C4["H"] * HEAD_DIM * 2 * 2
         bytes_rank = int(lens.sum()) * C4["H"] * HEAD_DIM * 2 * 2
         hbm = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+        parts = lpt_partition(all_lens.tolist(), world)
+        per_rank["c4_ms"] = [round(x / args.steps, 5) for x in timer.last_all]
+        per_rank["c4_rows"] = [int(sum(all_lens[i] for i in pr)) for pr in parts]
         secondary["c4_decode"] = {
             "ms": round(t, 5), "gbs_total": round(bytes_all / (t * 1e-3) / 1e9, 1),
             "gbs_per_gpu_rank0": round(bytes_rank / (t * 1e-3) / 1e9, 1),
@@ -381,6 +414,7 @@ def run_ours(args, rank, world, local_rank):
             t = timer.run(lambda: sharded_decode(qd, kc, vc, lens_local, SCALE),
                           args.steps, args.warmup) / args.steps
             launches += args.steps
+            c5_all = timer.last_all
             scaling = "single GPU"
         else:
             # the combine inside the decode kernel: partials stored into
@@ -390,6 +424,7 @@ def run_ours(args, rank, world, local_rank):
                 lambda: sharded_decode_fused(qd, kc, vc, lens_local, SCALE, xchg),
                 args.steps, args.warmup) / args.steps
             launches += args.steps
+            c5_all = timer.last_all
             xchg.close()
             scaling = ("strong (KV sequence sharded, partials exchanged over "
                        "NVLink peer memory inside the decode kernel)")
@@ -401,6 +436,10 @@ def run_ours(args, rank, world, local_rank):
                 "ms": round(t_nccl, 5),
                 "gbs_total": round(b_total / (t_nccl * 1e-3) / 1e9, 1),
                 "note": "decode_partial + NCCL all-gather + merge kernel"}
+        per_rank["c5_ms"] = [round(x / args.steps, 5) for x in c5_all]
+        per_rank["c5_rows"] = [shard_range(S, world, r)[1] - shard_range(S, world, r)[0]
+                               for r in range(world)]
+        secondary["per_rank"] = per_rank
         secondary["c5_decode"] = {
             "ms": round(t, 5), "gbs_total": round(b_total / (t * 1e-3) / 1e9, 1),
             "frac_of_measured_hbm_per_gpu": round(
@@ -519,6 +558,12 @@ def run_ours(args, rank, world, local_rank):
             secondary["cudnn_sdpa_c3"] = cudnn_measure(
                 timer, randn, args.steps, args.warmup, value)
 
+        # ------- the reference's published sweep shapes, libraries beside ---
+        if world == 1 and not args.no_library:
+            secondary["published_shapes"] = published_shapes(
+                fa, timer, randn, min(args.steps, 10), args.warmup)
+            launches += (len(PUB_PREFILL) + 2 + len(PUB_DECODE)) * min(args.steps, 10)
+
         # ------- the reference's own CUDA kernels on this B200 (baseline) ----
         if world == 1 and not args.no_ref_cuda:
             secondary["reference_cuda_kernels"] = ref_cuda_measure(
@@ -546,11 +591,7 @@ def run_ours(args, rank, world, local_rank):
         "vs_baseline": None,
         "dtype": "fp16 in, fp32 accumulate",
         "data": "synthetic N(0,1) fp16, seeded",
-        "config": {"workload": "config3_qwen2.5-0.5b_causal_prefill",
-                   "global_batch": C3["B"], "heads": C3["H"], "seq_len": n,
-                   "head_dim": HEAD_DIM, "causal": True,
-                   "parallelism": f"batch*head sharded over {world} GPU(s)",
-                   "l2": "flushed before every timed step (512 MiB written then read back)"},
+        "config": workload_config(world),
         "e2e": {"value": round(flops_total / (e2e_ms * 1e-3) / 1e12, 3),
                 "unit": "TFLOP/s", "ms_per_step": round(e2e_ms, 4),
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
@@ -558,6 +599,13 @@ def run_ours(args, rank, world, local_rank):
                        "pinned host q/k/v/out, per-chunk uploads, kernels and "
                        "downloads overlapped",
                 "serial_ms_per_step": round(e2e_serial_ms, 4),
+                "link": {"h2d_ms": round(up_ms, 4), "d2h_ms": round(down_ms, 4),
+                         "h2d_gbs": round(3 * hq.numel() * 2 / (up_ms * 1e-3) / 1e9, 1),
+                         "d2h_gbs": round(hq.numel() * 2 / (down_ms * 1e-3) / 1e9, 1),
+                         "bound_ms": round(link_ms, 4),
+                         "link_frac": round(link_ms / e2e_ms, 4),
+                         "note": "pinned copies timed alone on this box; "
+                                 "link_frac = bound_ms / ms_per_step"},
                 "serial_value": round(flops_total / (e2e_serial_ms * 1e-3) / 1e12, 3)},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2),
                      "peak": peak, "unit": "TFLOP/s",
@@ -633,16 +681,16 @@ def cpu_threads():
     return os.cpu_count() or 1
 
 
-def cpu_sample_heads(budget_s):
-    """Runs causal attention_cpu over C3 heads until `budget_s` elapses;
-    returns (heads done, seconds)."""
+def cpu_sample_heads(budget_s, heads=None):
+    """Runs causal attention_cpu over C3 heads until `budget_s` elapses (or
+    exactly `heads` of them); returns (heads done, seconds)."""
     sys.path.insert(0, ORACLE_DIR)
     import oracle
 
     rng = np.random.default_rng(0)
     n = C3["N"]
     done, t_total = 0, 0.0
-    while t_total < budget_s or done == 0:
+    while (done < heads) if heads else (t_total < budget_s or done == 0):
         q, k, v = (rng.standard_normal((n, HEAD_DIM), dtype=np.float32)
                    .astype(np.float16).astype(np.float32) for _ in range(3))
         t0 = time.perf_counter()
@@ -700,6 +748,79 @@ def graph_step_measure(fa, randn, calls=200):
                     "S=256 decode; the graph replays one captured launch"}
 
 
+# The reference's published sweep shapes (docs/benchmarks.md:28,72,113-117;
+# docs/profiles/analysis.md:76,113-114; swept by bench/run_bench.py:122-210),
+# measured here on the B200 with a library kernel beside each: cuDNN fused
+# attention (torch SDPA) for prefill, flash_attn_with_kvcache for decode.
+PUB_PREFILL = [(1, 12, 4096), (8, 12, 4096), (4, 12, 2048)]
+PUB_DECODE = [(1, 12, s) for s in (128, 256, 512, 1024, 2048, 4096)] + [(8, 12, 2048)]
+
+
+def published_shapes(fa, timer, randn, steps, warmup):
+    import torch
+    out = {}
+    try:
+        from torch.nn.attention import SDPBackend, sdpa_kernel
+    except Exception:  # pragma: no cover
+        sdpa_kernel = None
+    try:
+        from flash_attn import flash_attn_with_kvcache
+    except Exception as exc:
+        flash_attn_with_kvcache = None
+        out["flash_attn_unavailable"] = f"{type(exc).__name__}: {str(exc)[:80]}"
+
+    def lib_prefill(q, k, v, causal):
+        with sdpa_kernel(SDPBackend.CUDNN_ATTENTION):
+            torch.nn.functional.scaled_dot_product_attention(
+                q, k, v, is_causal=causal, scale=SCALE)
+
+    shapes = [(b, h, n, True) for b, h, n in PUB_PREFILL]
+    shapes += [(C2["B"], C2["H"], C2["N"], True), (C2["B"], C2["H"], C2["N"], False)]
+    for b, h, n, causal in shapes:
+        q, k, v = (randn(b, h, n, HEAD_DIM, seed=200 + i) for i in range(3))
+        f = prefill_flops(b, h, n, causal)
+        t = timer.run(lambda: fa.prefill(q, k, v, causal, SCALE), steps, warmup) / steps
+        row = {"us": round(t * 1e3, 2), "tflops": round(f / (t * 1e-3) / 1e12, 1)}
+        if sdpa_kernel is not None:
+            try:
+                tl = timer.run(lambda: lib_prefill(q, k, v, causal), steps, warmup) / steps
+                row["cudnn_us"] = round(tl * 1e3, 2)
+                row["cudnn_tflops"] = round(f / (tl * 1e-3) / 1e12, 1)
+                row["ours_over_cudnn"] = round(tl / t, 3)
+            except Exception as exc:
+                row["cudnn_unavailable"] = f"{type(exc).__name__}"
+        out[f"prefill_b{b}_h{h}_n{n}_{'causal' if causal else 'full'}"] = row
+        del q, k, v
+    for b, h, s_len in PUB_DECODE:
+        q = randn(b, h, 1, HEAD_DIM, seed=210)
+        k = randn(b, h, s_len, HEAD_DIM, seed=211)
+        v = randn(b, h, s_len, HEAD_DIM, seed=212)
+        lens = torch.full((b,), s_len, dtype=torch.int32, device="cuda")
+        nbytes = b * h * s_len * HEAD_DIM * 2 * 2
+        t = timer.run(lambda: fa.decode(q, k, v, lens, SCALE), steps, warmup) / steps
+        row = {"us": round(t * 1e3, 2), "gbs": round(nbytes / (t * 1e-3) / 1e9, 1)}
+        if flash_attn_with_kvcache is not None:
+            # flash_attn's layout is (batch, seq, heads, dim): converted once,
+            # outside the timed region
+            qf = q.transpose(1, 2).contiguous()
+            kf = k.transpose(1, 2).contiguous()
+            vf = v.transpose(1, 2).contiguous()
+            try:
+                tl = timer.run(lambda: flash_attn_with_kvcache(
+                    qf, kf, vf, cache_seqlens=lens, softmax_scale=SCALE),
+                    steps, warmup) / steps
+                row["flash_attn_us"] = round(tl * 1e3, 2)
+                row["ours_over_flash_attn"] = round(tl / t, 3)
+            except Exception as exc:
+                row["flash_attn_unavailable"] = f"{type(exc).__name__}: {str(exc)[:60]}"
+            del qf, kf, vf
+        out[f"decode_b{b}_h{h}_s{s_len}"] = row
+        del q, k, v
+    out["note"] = ("published sweep shapes of the reference, fp16, L2 flushed "
+                   "before every step; library kernels are context only")
+    return out
+
+
 def cudnn_measure(timer, randn, steps, warmup, ours_tflops):
     """Config 3 through torch SDPA restricted to the cuDNN backend, with the
     same inputs shape, L2 flush and timing as the headline line."""
@@ -725,33 +846,50 @@ def cudnn_measure(timer, randn, steps, warmup, ours_tflops):
         return {"unavailable": f"{type(exc).__name__}: {str(exc)[:120]}"}
 
 
+REF_HEADS_PER_STEP = 4
+
+
+def workload_config(world):
+    """The headline workload's config (both arms print the same one)."""
+    return {"workload": "config3_qwen2.5-0.5b_causal_prefill",
+            "global_batch": C3["B"], "heads": C3["H"], "seq_len": C3["N"],
+            "head_dim": HEAD_DIM, "causal": True,
+            "parallelism": f"batch*head sharded over {world} GPU(s)",
+            "l2": "flushed before every timed step (512 MiB written then read back)"}
+
+
 def run_reference(args, rank, world):
+    """The reference's CPU path on the host cores, rank 0 only. One timed
+    step is REF_HEADS_PER_STEP of config 3's 56 (batch, head) evaluations
+    (the whole config would take minutes per step); ms_per_step is the time
+    of that step as run, and the rate is the workload's own FLOP rate."""
     if rank != 0:
         return
-    budget = max(1.0, args.cpu_budget / max(1, args.steps + args.warmup))
     for _ in range(args.warmup):
-        cpu_sample_heads(budget)
-    heads_total, secs_total = 0, 0.0
+        cpu_sample_heads(0.0, heads=REF_HEADS_PER_STEP)
+    secs = []
     for _ in range(args.steps):
-        h, s = cpu_sample_heads(budget)
-        heads_total += h
-        secs_total += s
+        _, t = cpu_sample_heads(0.0, heads=REF_HEADS_PER_STEP)
+        secs.append(t)
+    secs_total = sum(secs)
+    heads_total = REF_HEADS_PER_STEP * args.steps
     flops = prefill_flops(1, heads_total, C3["N"], True)
     value = flops / secs_total / 1e12
-    ms_per_step = prefill_flops(C3["B"], C3["H"], C3["N"], True) / (value * 1e12) * 1e3
     result = {
         "impl": "reference",
         "metric": "causal prefill TFLOP/s (B=4,H=14,N=4096,d=64 fp16)",
         "value": round(value, 5), "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(ms_per_step, 1), "higher_is_better": True,
+        "ms_per_step": round(secs_total / args.steps * 1e3, 1),
+        "step": f"{REF_HEADS_PER_STEP} of config 3's {C3['B'] * C3['H']} "
+                f"causal N={C3['N']} (batch, head) evaluations",
+        "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None,
         "dtype": "fp32 (numpy, inputs rounded to fp16)",
         "data": "synthetic N(0,1), seeded",
-        "config": {"workload": "config3_qwen2.5-0.5b_causal_prefill",
-                   "global_batch": C3["B"], "heads": C3["H"],
-                   "seq_len": C3["N"], "head_dim": HEAD_DIM, "causal": True,
-                   "parallelism": "host CPU (rank 0 only)"},
+        "config": workload_config(world),
+        "host": "reference CPU path on the host cores of rank 0 (the L2 flush "
+                "and GPU sharding in config describe the GPU arm's timing)",
         "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s",
                          "cores": cpu_threads(), "kind": "port",
                          "sample": f"{heads_total} heads of config 3 over "

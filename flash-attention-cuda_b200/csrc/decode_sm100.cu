@@ -399,10 +399,12 @@ __device__ void produce(const DecodeArgs &a, int nseg, int seg_per_plane,
   const int lane = threadIdx.x & 31;
     // ------------------------------------------------------------ planning
     long long sum_len = 0;
+    int max_len = 0;
     for (int chunk = 0; chunk < a.B; chunk += 32) {
       const int b = chunk + lane;
       const int len = b < a.B ? seq_rows(a, b) : 1;
       if (b < a.B) sum_len += len;
+      if (b < a.B) max_len = max(max_len, len);
       // sequences without rows (other widths: written by the caller)
       unsigned todo = __ballot_sync(
           0xffffffffu, b < a.B && len == 0 &&
@@ -427,6 +429,14 @@ __device__ void produce(const DecodeArgs &a, int nseg, int seg_per_plane,
     if (per <= 0) {
       per = (total + gridDim.x - 1) / gridDim.x;
       if (per < kMinRowsPerCta) per = kMinRowsPerCta;
+      // Short sequences (at most two stages each): one CTA streams a whole
+      // segment rather than splitting it and merging partials across CTAs
+      // (B1 H12 S256: 14.4 -> 12.3 us on the B200).
+#pragma unroll 1
+      for (int o = 16; o > 0; o >>= 1)
+        max_len = max(max_len, __shfl_xor_sync(0xffffffffu, max_len, o));
+      if (max_len <= 2 * kRowsPerStage && per < max_len)
+        per = (max_len + 3) & ~3;
     }
     const long long start = static_cast<long long>(blockIdx.x) * per;
     const long long end = start + per < total ? start + per : total;
