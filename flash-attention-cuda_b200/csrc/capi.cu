@@ -78,15 +78,13 @@ int ensure_device(int *device_out) {
                               prefill_d128_kernel_ptr(dt),
                               decode_gqa_kernel_ptr(64, dt),
                               decode_gqa_kernel_ptr(128, dt),
-                              prefill_head_pairs_kernel_ptr(dt),
-                              prefill_head_pairs_kernel_ptr(dt, true),
-                              prefill_d128_kernel_ptr(dt, true)};
+                              prefill_d128_kernel_ptr(dt, true),
+                              prefill_solo_kernel_ptr(dt)};
     const int bytes[] = {prefill_smem_bytes(), decode_smem_bytes(),
                          decode_d128_smem_bytes(), prefill_d128_smem_bytes(),
                          decode_gqa_smem_bytes(64), decode_gqa_smem_bytes(128),
-                         prefill_smem_bytes(), prefill_smem_bytes(),
-                         prefill_d128_smem_bytes()};
-    for (int i = 0; i < 9; ++i) {
+                         prefill_d128_smem_bytes(), prefill_solo_smem_bytes()};
+    for (int i = 0; i < 8; ++i) {
       if (cudaFuncSetAttribute(big_smem[i],
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                bytes[i]) != cudaSuccess ||
@@ -771,6 +769,8 @@ int fa_occupancy(fa_occupancy_entry *out, int max_entries, int *count) {
   } kernels[] = {
       {"prefill_kernel", prefill_kernel_ptr(), prefill_threads(),
        prefill_smem_bytes()},
+      {"prefill_solo_kernel", prefill_solo_kernel_ptr(),
+       prefill_solo_threads(), prefill_solo_smem_bytes()},
       {"decode_kernel", decode_kernel_ptr(), decode_threads(),
        decode_smem_bytes()},
       {"merge_kernel", merge_kernel_ptr(), merge_threads(), 0},
@@ -844,6 +844,7 @@ int fa_trace_read(unsigned long long *dst, size_t n) {
              : FA_ECUDA;
 }
 #endif
+
 
 int fa_num_sms(void) {
   int dev = 0, sms = 0;

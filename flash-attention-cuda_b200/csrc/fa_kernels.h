@@ -12,9 +12,10 @@ namespace fa {
 
 // ---- prefill (prefill_sm100.cu) -------------------------------------------
 const void *prefill_kernel_ptr(int dtype = FA_DTYPE_F16);
-const void *prefill_head_pairs_kernel_ptr(int dtype = FA_DTYPE_F16,
-                                          bool one_tile = false);
 int prefill_threads();
+const void *prefill_solo_kernel_ptr(int dtype = FA_DTYPE_F16);
+int prefill_solo_smem_bytes();
+int prefill_solo_threads();
 int prefill_smem_bytes();
 cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
                                   const CUtensorMap &tm_k,

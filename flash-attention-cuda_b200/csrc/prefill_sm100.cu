@@ -9,26 +9,28 @@
 // mbarrier ring, and the online softmax runs in registers of dedicated warps
 // that read S straight out of tensor memory and write P back into it.
 //
-// A kernel that allocates tensor memory runs one CTA per SM, so overlap is
-// built inside the CTA: it owns two 128-row query tiles of one (batch, head)
-// (rows [256*i, 256*i + 256)) and ping-pongs them. While one softmax
-// warpgroup exponentiates its S tile, the tensor core computes the other
-// tile's S or PV. Both tiles share every K/V tile loaded.
+// Two CTA forms share one kernel template.
 //
-// CTA = 10 warps (320 threads):
+// Paired form (one CTA per SM): the CTA owns two 128-row query tiles of one
+// (batch, head) and ping-pongs them. While one softmax warpgroup
+// exponentiates its S tile, the tensor core computes the other tile's S or
+// PV; both tiles share every K/V tile loaded. 12 warps (384 threads):
 //   warps 0-3  softmax of query tile 0 (thread = row = TMEM lane)
 //   warps 4-7  softmax of query tile 1
 //   warp 8     TMA producer: Q tiles once, then K_j, V_j per 128-key tile
 //   warp 9     MMA issuer (one thread); owns the TMEM allocation
-//
-// Shared memory (1 KiB aligned, 128-byte-swizzled tiles as written by TMA):
-//   Q0, Q1  [128 rows x 128 B]            32 KiB
-//   K       6 slots x  [128 keys x 128 B] 96 KiB (3 used with one head)
-//   V       6 slots x  [128 keys x 128 B] 96 KiB
-//   mbarriers, TMEM base address, abort flag
+//   warps 10-11 only donate registers
+// Shared memory: Q0, Q1 (32 KiB), K and V rings of 3 x 16 KiB, mbarriers.
 // Tensor memory (512 columns x 128 lanes, fp32 words):
 //   S0 [0,128)  S1 [128,256)  O0 [256,320)  O1 [320,384)
 //   P0 [384,448)  P1 [448,512)   (P = fp16 pairs, the A operand of PV)
+//
+// Solo form (two CTAs per SM): one query tile per CTA, 8 warps (softmax
+// 0-3, producer 4, MMA 5, donors 6-7), Q (16 KiB) and the two 3-slot rings
+// in 112 KiB of shared memory, S [0,128) O [128,192) P [192,256) in 256
+// tensor-memory columns. Two resident CTAs take the place of the two tiles
+// of the paired form, and one CTA's start-up (its first tiles from HBM) and
+// epilogue overlap the other's key steps.
 
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -49,31 +51,18 @@ namespace prefill {
 constexpr int kBlockM = 128;  // query rows per tile
 constexpr int kBlockN = 128;  // keys per KV tile
 constexpr int kTilesPerCta = 2;
-// K/V ring slots in shared memory. One head per CTA cycles through 3 of
-// them (two key tiles ahead of the one in use). Two heads per CTA use all
-// 6: three key steps of both heads, so each head's stream also runs two
-// steps ahead (with 4, one step ahead, a long sequence whose K/V misses L2
-// stalls on every tile).
-constexpr int kRingSlots = 6;
-#ifndef FA_HEAD_PAIR_MAX_TILES
-#define FA_HEAD_PAIR_MAX_TILES 7
-#endif
-// Odd query-tile counts up to this use the two-heads-per-CTA form.
-constexpr int kMaxHeadPairTiles = FA_HEAD_PAIR_MAX_TILES;
+// K/V ring slots in shared memory: two key tiles stream ahead of the one in
+// use.
+constexpr int kRingSlots = 3;
+// Longest sequence, in query tiles, that runs in the solo form (measured:
+// N 4096 solo 743 vs paired 724 TFLOP/s, N 8192 798 vs 809, N 16384 738 vs
+// 746).
+constexpr int kSoloMaxTiles = 48;
 constexpr int kSoftmaxThreads = 128;  // per query tile
-constexpr int kProducerWarp = 8;
-constexpr int kMmaWarp = 9;
-constexpr int kThreads = 384;  // 3 warpgroups; warps 10-11 only donate registers
 constexpr int kCtrlRegs = 24;
-constexpr int kSoftmaxRegs = 240;
-static_assert(128 * kCtrlRegs + 256 * kSoftmaxRegs <= kThreads * 168,
-              "register split exceeds the launch allocation");
 constexpr uint32_t kTileBytes = kBlockN * kRowBytes;  // 16 KiB
 
 constexpr uint32_t kQOff = 0;
-constexpr uint32_t kKOff = kQOff + kTilesPerCta * kTileBytes;
-constexpr uint32_t kVOff = kKOff + kRingSlots * kTileBytes;
-constexpr uint32_t kBarOff = kVOff + kRingSlots * kTileBytes;
 // barrier slots
 constexpr int kBarQFull = 0;
 constexpr int kBarKFull = kBarQFull + 1;          // + stage: K and V tile
@@ -84,15 +73,40 @@ constexpr int kBarPFull = kBarSFree + kTilesPerCta;
 constexpr int kBarODone = kBarPFull + kTilesPerCta;
 constexpr int kBarDrain = kBarODone + kTilesPerCta;
 constexpr int kNumBars = kBarDrain + 1;
-constexpr uint32_t kTmemSlotOff = kBarOff + kNumBars * 8;
-constexpr uint32_t kAbortOff = kTmemSlotOff + 4;
-constexpr uint32_t kSmemBytes = kAbortOff + 4 + 8;
-static_assert(kSmemBytes <= 227 * 1024, "above the sm_100 per-CTA shared memory limit");
-
-constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemS = 0;    // + 128 * tile
-constexpr uint32_t kTmemO = 256;  // + 64 * tile
-constexpr uint32_t kTmemP = 384;  // + 64 * tile
+
+// Two CTA forms share the kernel. The paired form (kSolo false) holds two
+// query tiles in one CTA per SM (384 threads, 512 tensor-memory columns,
+// a 3-slot K/V ring). The solo form holds one query tile per CTA and fits
+// two CTAs on an SM: 256 threads (softmax warps 0-3, producer 4, MMA 5,
+// warps 6-7 donate registers), 256 tensor-memory columns and a 3-slot ring
+// in 112 KiB of shared memory, so one CTA's start-up (first tiles from HBM)
+// and epilogue overlap the other CTA's key steps.
+template <bool kSolo>
+struct Form {
+  static constexpr int kThreads = kSolo ? 256 : 384;
+  static constexpr int kCtasPerSm = kSolo ? 2 : 1;
+  static constexpr int kCtrlWarp0 = kSolo ? 4 : 8;  // first control warp
+  static constexpr int kProducerWarp = kCtrlWarp0;
+  static constexpr int kMmaWarp = kCtrlWarp0 + 1;
+  static constexpr int kSoftmaxRegs = kSolo ? 232 : 240;
+  static constexpr int kQTiles = kSolo ? 1 : 2;
+  static constexpr int kSlots = kRingSlots;
+  static constexpr uint32_t kKOff = kQOff + kQTiles * kTileBytes;
+  static constexpr uint32_t kVOff = kKOff + kSlots * kTileBytes;
+  static constexpr uint32_t kBarOff = kVOff + kSlots * kTileBytes;
+  static constexpr uint32_t kTmemSlotOff = kBarOff + kNumBars * 8;
+  static constexpr uint32_t kAbortOff = kTmemSlotOff + 4;
+  static constexpr uint32_t kSmemBytes = kAbortOff + 4 + 8;
+  static constexpr uint32_t kTmemCols = kSolo ? 256 : 512;
+  static constexpr uint32_t kTmemO = kSolo ? 128 : 256;  // + 64 * tile
+  static constexpr uint32_t kTmemP = kSolo ? 192 : 384;  // + 64 * tile
+  static_assert(128 * kCtrlRegs + 128 * kQTiles * kSoftmaxRegs <=
+                    kThreads * (65536 / (kThreads * kCtasPerSm)),
+                "register split exceeds the launch allocation");
+  static_assert(kCtasPerSm * (kSmemBytes + 1024) <= 228 * 1024,
+                "shared memory of the resident CTAs exceeds the SM's");
+};
 
 template <typename Dt>
 constexpr uint32_t kIdescS = idesc_f16_f32(kBlockM, kBlockN, false, Dt::kFmt);
@@ -206,23 +220,16 @@ __device__ __forceinline__ TileInfo tile_info(int pair, int t, int N,
   return ti;
 }
 
-// kHeadPairs (an odd number of query tiles per head, at most 7): the CTA's
-// two tile slots hold the same query tile of two heads (2 * hp and the
-// next), each streaming its own K/V head, instead of two tiles of one head
-// (which would leave the last tile of every head alone in a half-idle CTA).
-// The two K/V streams interleave in the ring: key tile j of slot t is ring
-// position 2 j + t (position j with one head per CTA). kOneTile: sequences
-// of at most one query tile, where every CTA runs exactly one key step and
-// the compiler drops the loops around it.
-template <typename Dt, bool kHeadPairs = false, bool kOneTile = false>
-__global__ void __launch_bounds__(kThreads, 1)
+template <typename Dt, bool kSolo = false>
+__global__ void __launch_bounds__(Form<kSolo>::kThreads, Form<kSolo>::kCtasPerSm)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
                    const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v,
                    __half *__restrict__ out, int N, int BH, int causal,
                    float scale_log2, int H, int group) {
+  using F = Form<kSolo>;
   extern __shared__ __align__(1024) uint8_t smem[];
-  constexpr int kStages = kHeadPairs ? kRingSlots : 3;
+  constexpr int kStages = kRingSlots;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
@@ -234,57 +241,41 @@ __global__ void __launch_bounds__(kThreads, 1)
     return;
   }
 
-  // Heaviest causal pairs first: blockIdx.x walks query-tile pairs from the
-  // last (most keys) to the first, heads fastest.
+  // Heaviest first: blockIdx.x walks query tiles (solo) or query-tile pairs
+  // from the last (most keys) to the first, heads fastest.
   const int n_qt = (N + kBlockM - 1) / kBlockM;
   const int n_pairs = (n_qt + 1) / 2;
-  const int n_hp = (BH + 1) / 2;  // head pairs (kHeadPairs)
-  // heaviest first: kHeadPairs walks query tiles from the last, head pairs
-  // fastest
-  const int hp_qt = kHeadPairs && !kOneTile
-                        ? n_qt - 1 - static_cast<int>(blockIdx.x) / n_hp
-                        : 0;
-  const int pair =
-      kHeadPairs ? 0 : n_pairs - 1 - static_cast<int>(blockIdx.x / BH);
-  const int bh = kHeadPairs ? 2 * (kOneTile ? static_cast<int>(blockIdx.x)
-                                            : static_cast<int>(blockIdx.x) % n_hp)
-                            : static_cast<int>(blockIdx.x % BH);
-  const int bh1 = kHeadPairs ? bh + 1 : bh;  // query head of tile 1
-  // K/V head of a query head: `group` query heads share one K/V head
+  const int pair = n_pairs - 1 - static_cast<int>(blockIdx.x / BH);
+  const int bh = static_cast<int>(blockIdx.x % BH);
+  // K/V head of the query head: `group` query heads share one K/V head
   // (group == 1 without grouped-query attention).
   const int kv_bh = (bh / H) * (H / group) + (bh % H) / group;
-  const int kv_bh1 = (bh1 / H) * (H / group) + (bh1 % H) / group;
   TileInfo t0, t1;
-  if (kHeadPairs) {
-    t0.qt = t1.qt = hp_qt;
-    t0.n_kv = kOneTile ? 1 : causal ? hp_qt + 1 : n_qt;
-    t1.n_kv = bh1 < BH ? t0.n_kv : 0;
+  if (kSolo) {
+    t0.qt = n_qt - 1 - static_cast<int>(blockIdx.x / BH);
+    t0.n_kv = causal ? t0.qt + 1 : n_qt;
+    t1.qt = t0.qt;
+    t1.n_kv = 0;
   } else {
     t0 = tile_info(pair, 0, N, causal, zigzag);
     t1 = tile_info(pair, 1, N, causal, zigzag);
   }
   const int n_kv = t0.n_kv > t1.n_kv ? t0.n_kv : t1.n_kv;
 
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kBarOff);
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kTmemSlotOff);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + F::kBarOff);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + F::kTmemSlotOff);
   volatile uint32_t *abort_flag =
-      reinterpret_cast<volatile uint32_t *>(smem + kAbortOff);
+      reinterpret_cast<volatile uint32_t *>(smem + F::kAbortOff);
 
-  // Ring positions: key tile j of tile slot t is position 2 j + t with two
-  // heads per CTA (tile 1's positions skipped when it has no head), else
-  // position j; a position's stage is p % kStages.
-  const int n_pos = kHeadPairs ? 2 * n_kv : n_kv;
-  auto pos_used = [&](int p) { return !kHeadPairs || !(p & 1) || t1.n_kv > 0; };
+  // Key tile j goes to ring stage j % kStages.
+  const int n_pos = n_kv;
   auto load_pos = [&](int p) {
-    if (!pos_used(p)) return;
-    const int j = kHeadPairs ? p >> 1 : p;
-    const int kvh = (kHeadPairs && (p & 1)) ? kv_bh1 : kv_bh;
     const int s = p % kStages;
     mbar_arrive_expect_tx(&bars[kBarKFull + s], 2 * kTileBytes);
-    tma_load_3d(smem + kKOff + s * kTileBytes, &tm_k, &bars[kBarKFull + s], 0,
-                j * kBlockN, kvh);
-    tma_load_3d(smem + kVOff + s * kTileBytes, &tm_v, &bars[kBarKFull + s], 0,
-                j * kBlockN, kvh);
+    tma_load_3d(smem + F::kKOff + s * kTileBytes, &tm_k, &bars[kBarKFull + s], 0,
+                p * kBlockN, kv_bh);
+    tma_load_3d(smem + F::kVOff + s * kTileBytes, &tm_v, &bars[kBarKFull + s], 0,
+                p * kBlockN, kv_bh);
   };
 
   // The producer lane sets up the barriers and issues the Q tiles and the
@@ -292,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // overlaps the TMEM allocation; the device error word (a global read) is
   // checked after that and turns into the abort flag.
   int preissued = 0;
-  if (warp == kProducerWarp && lane == 0) {
+  if (warp == F::kProducerWarp && lane == 0) {
     mbar_init(&bars[kBarQFull], 1);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&bars[kBarKFull + s], 1);
@@ -314,13 +305,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_load_3d(smem + kQOff, &tm_q, &bars[kBarQFull], 0, t0.qt * kBlockM, bh);
     if (two)
       tma_load_3d(smem + kQOff + kTileBytes, &tm_q, &bars[kBarQFull], 0,
-                  t1.qt * kBlockM, bh1);
+                  t1.qt * kBlockM, bh);
     for (; preissued < n_pos && preissued < kStages; ++preissued)
       load_pos(preissued);
     *abort_flag = device_failed() ? 1u : 0u;
   }
-  if (warp == kMmaWarp) {
-    tmem_alloc(tmem_slot, kTmemCols);
+  if (warp == F::kMmaWarp) {
+    tmem_alloc(tmem_slot, F::kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -331,12 +322,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // Register split: the control warpgroup (producer, MMA, two idle warps)
   // gives registers to the two softmax warpgroups, which hold a full S row.
-  // 128 * kCtrlRegs + 256 * kSoftmaxRegs <= kThreads * 168 (launch budget).
+  // 128 * kCtrlRegs + 128 * tiles * kSoftmaxRegs fits the launch budget
+  // (checked in Form).
   // Each role's code sits inside the branch that sized its registers, so
   // the compiler allocates each region for its own budget.
-  if (warp >= 8) {
+  if (warp >= F::kCtrlWarp0) {
     setmaxnreg_dec<kCtrlRegs>();
-  if (warp == kProducerWarp) {
+  if (warp == F::kProducerWarp) {
     // ------------------------------------------------------------------ TMA
     if (lane == 0) {
       int issued = preissued;
@@ -344,7 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (*abort_flag) break;
         const int s = p % kStages;
         const int use = p / kStages;
-        if (pos_used(p) && use > 0 &&
+        if (use > 0 &&
             !mbar_wait(&bars[kBarKVEmpty + s], (use - 1) & 1)) {
           *abort_flag = 1;
           break;
@@ -358,12 +350,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(&bars[kBarQFull], 0);
         for (int p = (issued > kStages ? issued - kStages : 0); p < issued;
              ++p) {
-          if (pos_used(p))
-            mbar_wait(&bars[kBarKFull + p % kStages], (p / kStages) & 1);
+          mbar_wait(&bars[kBarKFull + p % kStages], (p / kStages) & 1);
         }
       }
     }
-  } else if (warp == kMmaWarp) {
+  } else if (warp == F::kMmaWarp) {
     // ------------------------------------------------------------------ MMA
     // The whole warp runs the control flow, so every operand below is
     // warp-uniform; one elected lane issues the tcgen05 instructions.
@@ -373,24 +364,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int n0 = t0.n_kv;
     const int n1 = t1.n_kv;
     const uint64_t desc0 = sw128_desc(sbase);
-    // ring position of key tile j of slot t
-    auto kpos = [&](int t, int j) { return kHeadPairs ? 2 * j + t : j; };
     bool ok = mbar_wait(&bars[kBarQFull], 0) &&
-              mbar_wait(&bars[kBarKFull + 0], 0) &&
-              (!kHeadPairs || kOneTile || n1 == 0 ||
-               mbar_wait(&bars[kBarKFull + 1], 0));
+              mbar_wait(&bars[kBarKFull + 0], 0);
     if (ok) {
       tc_fence_after();
       if (leader) {
         if (n0 > 0) {
-          issue_s_tile<Dt>(tmem + kTmemS, desc0 + (kQOff >> 4), desc0 + (kKOff >> 4));
+          issue_s_tile<Dt>(tmem + kTmemS, desc0 + (kQOff >> 4), desc0 + (F::kKOff >> 4));
           mma_commit(&bars[kBarSFull + 0]);
         }
-        // With two heads tile 1's first K/V tile has its own ring position;
-        // one-tile CTAs issue S0 before waiting on it.
-        if (n1 > 0 && (!kOneTile || mbar_wait(&bars[kBarKFull + 1], 0))) {
+        if (n1 > 0) {
           issue_s_tile<Dt>(tmem + kTmemS + 128, desc0 + ((kQOff + kTileBytes) >> 4),
-                       desc0 + ((kKOff + (kpos(1, 0) % kStages) * kTileBytes) >> 4));
+                       desc0 + (F::kKOff >> 4));
           mma_commit(&bars[kBarSFull + 1]);
         }
       }
@@ -405,14 +390,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = 0; t < kTilesPerCta; ++t) {
         const int nt = t ? n1 : n0;
         if (!ok || j >= nt) continue;
-        const int s = kpos(t, j) % kStages;         // K_j, V_j of this slot
-        const int p1 = kpos(t, j + 1);
+        const int s = j % kStages;                  // K_j, V_j
+        const int p1 = j + 1;
         const int s1 = p1 % kStages;                // K_{j+1}
         if (j + 1 < nt) {
           // K/V tile j+1 is waited on once per round (by the first tile
-          // that uses it, or by each slot with two heads); V_j was waited
-          // on with K_j the round before.
-          const bool need_kv = kHeadPairs || (t == 0) || (n0 <= j + 1);
+          // that uses it); V_j was waited on with K_j the round before.
+          const bool need_kv = (t == 0) || (n0 <= j + 1);
           if ((need_kv &&
                !mbar_wait(&bars[kBarKFull + s1], (p1 / kStages) & 1)) ||
               !mbar_wait(&bars[kBarSFree + t], j & 1)) {
@@ -424,7 +408,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (leader) {
             issue_s_tile<Dt>(tmem + kTmemS + 128 * t,
                          desc0 + ((kQOff + t * kTileBytes) >> 4),
-                         desc0 + ((kKOff + s1 * kTileBytes) >> 4));
+                         desc0 + ((F::kKOff + s1 * kTileBytes) >> 4));
             mma_commit(&bars[kBarSFull + t]);
           }
           __syncwarp();
@@ -437,18 +421,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         FA_TRACE_EVENT(2048 + j * 16 + t * 8 + 4);
         tc_fence_after();
         if (leader) {
-          issue_pv_tile<Dt>(tmem + kTmemO + 64 * t, tmem + kTmemP + 64 * t,
-                        desc0 + ((kVOff + s * kTileBytes) >> 4), j > 0);
+          issue_pv_tile<Dt>(tmem + F::kTmemO + 64 * t, tmem + F::kTmemP + 64 * t,
+                        desc0 + ((F::kVOff + s * kTileBytes) >> 4), j > 0);
           mma_commit(&bars[kBarODone + t]);
         }
         __syncwarp();
         FA_TRACE_EVENT(2048 + j * 16 + t * 8 + 2);
       }
       if (!ok) break;
-      // release round j's ring positions (both slots' with two heads)
+      // release round j's ring stage
       if (leader) {
-        mma_commit(&bars[kBarKVEmpty + kpos(0, j) % kStages]);
-        if (kHeadPairs) mma_commit(&bars[kBarKVEmpty + kpos(1, j) % kStages]);
+        mma_commit(&bars[kBarKVEmpty + j % kStages]);
       }
       __syncwarp();
     }
@@ -460,15 +443,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_wait(&bars[kBarDrain], 0);
   }
   } else {
-    setmaxnreg_inc<kSoftmaxRegs>();
+    setmaxnreg_inc<F::kSoftmaxRegs>();
     // -------------------------------------------------------------- softmax
     const int t = warp >> 2;            // query tile of this warpgroup
     const int row = threadIdx.x & 127;  // row in the tile == TMEM lane
     const TileInfo ti = t == 0 ? t0 : t1;
     const uint32_t lane_addr = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t tS = tmem_base + lane_addr + kTmemS + 128 * t;
-    const uint32_t tO = tmem_base + lane_addr + kTmemO + 64 * t;
-    const uint32_t tP = tmem_base + lane_addr + kTmemP + 64 * t;
+    const uint32_t tO = tmem_base + lane_addr + F::kTmemO + 64 * t;
+    const uint32_t tP = tmem_base + lane_addr + F::kTmemP + 64 * t;
     uint64_t *s_full = &bars[kBarSFull + t];
     uint64_t *s_free = &bars[kBarSFree + t];
     uint64_t *p_full = &bars[kBarPFull + t];
@@ -571,7 +554,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (q_row < N) {
           const float inv_l = (l_sum > 0.f) ? 1.f / l_sum : 0.f;
           uint4 *dst = reinterpret_cast<uint4 *>(
-              out + (static_cast<size_t>(t ? bh1 : bh) * N + q_row) * kHeadDim);
+              out + (static_cast<size_t>(bh) * N + q_row) * kHeadDim);
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             uint4 v;
@@ -595,88 +578,34 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == kMmaWarp) {
+  if (warp == F::kMmaWarp) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    tmem_dealloc(tmem_base, F::kTmemCols);
   }
 }
 
 }  // namespace prefill
 
-namespace prefill {
-
-// Estimated run time, in key-step units, of CTAs list-scheduled heaviest
-// first on `sms` SMs (the order both grids launch in): each CTA starts on
-// the SM that frees up first. classes: (cost, count), decreasing cost.
-// SMs are kept as (time free, how many), so a class of c equal CTAs costs
-// one map operation per wave, not per CTA.
-static double list_makespan(const std::pair<double, long long> *classes,
-                            int n, int sms) {
-  std::map<double, long long> free_at{{0.0, sms}};
-  double end = 0.0;
-  for (int i = 0; i < n; ++i) {
-    long long left = classes[i].second;
-    while (left > 0) {
-      auto it = free_at.begin();
-      const double t = it->first + classes[i].first;
-      const long long k = std::min(left, it->second);
-      if ((it->second -= k) == 0) free_at.erase(it);
-      free_at[t] += k;
-      end = std::max(end, t);
-      left -= k;
-    }
-  }
-  return end;
-}
-
-// Whether an odd number of query tiles (n_qt) runs faster as the same tile
-// of two heads per CTA than as tile pairs of one head, whose last CTA per
-// head holds a lone tile with half the softmax warps idle. Cost model, in
-// key steps of a one-head CTA: a CTA costs kCtaFixed plus its key steps (a
-// CTA's step time hardly depends on whether it holds one query tile or
-// two); a two-head step costs kPairStep, since it streams two K/V heads
-// where one head's two tiles share each K/V tile. Both constants are fitted
-// to measured B200 times (B16/B8 x 12 heads, N 384-896, causal and full).
-bool head_pairs_pay(int BH, int n_qt, bool causal, int sms) {
-  constexpr double kCtaFixed = 1.0, kPairStep = 1.25;
-  std::pair<double, long long> one[(kMaxHeadPairTiles + 1) / 2],
-      two[kMaxHeadPairTiles];
-  const int n_pairs = (n_qt + 1) / 2;
-  const bool zigzag = causal && static_cast<long long>(n_pairs) * BH <= sms;
-  for (int p = 0; p < n_pairs; ++p) {
-    // key steps of a CTA: those of its longer tile
-    const int steps = !causal ? n_qt
-                      : zigzag ? n_qt - p
-                               : std::min(2 * p + 1, n_qt - 1) + 1;
-    one[p] = {kCtaFixed + steps, BH};
-  }
-  for (int q = 0; q < n_qt; ++q) {
-    const int steps = causal ? n_qt - q : n_qt;
-    two[q] = {kCtaFixed + kPairStep * steps, (BH + 1) / 2};
-  }
-  std::sort(one, one + n_pairs, std::greater<>());
-  return list_makespan(two, n_qt, sms) < list_makespan(one, n_pairs, sms);
-}
-
-}  // namespace prefill
-
-const void *prefill_head_pairs_kernel_ptr(int dtype, bool one_tile) {
+const void *prefill_solo_kernel_ptr(int dtype) {
   using prefill::prefill_kernel;
-  if (one_tile)
-    return dtype == FA_DTYPE_BF16
-               ? reinterpret_cast<const void *>(prefill_kernel<BF16, true, true>)
-               : reinterpret_cast<const void *>(prefill_kernel<F16, true, true>);
   return dtype == FA_DTYPE_BF16
              ? reinterpret_cast<const void *>(prefill_kernel<BF16, true>)
              : reinterpret_cast<const void *>(prefill_kernel<F16, true>);
 }
+int prefill_solo_smem_bytes() {
+  return static_cast<int>(prefill::Form<true>::kSmemBytes);
+}
+int prefill_solo_threads() { return prefill::Form<true>::kThreads; }
 const void *prefill_kernel_ptr(int dtype) {
   return dtype == FA_DTYPE_BF16
              ? reinterpret_cast<const void *>(prefill::prefill_kernel<BF16>)
              : reinterpret_cast<const void *>(prefill::prefill_kernel<F16>);
 }
-int prefill_threads() { return prefill::kThreads; }
-int prefill_smem_bytes() { return static_cast<int>(prefill::kSmemBytes); }
+int prefill_threads() { return prefill::Form<false>::kThreads; }
+int prefill_smem_bytes() {
+  return static_cast<int>(prefill::Form<false>::kSmemBytes);
+}
+
 
 cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
                                   const CUtensorMap &tm_k,
@@ -695,25 +624,25 @@ cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
   // One wave of CTAs: zig-zag pairs of equal causal work, so the kernel
   // does not wait on the heaviest pair. Several waves: heaviest first.
   const int zigzag = causal && grid <= static_cast<unsigned>(sms) ? 2 : 0;
-  const long long hp_ctas = static_cast<long long>((BH + 1) / 2) * n_qt;
-  const bool head_pairs = (n_qt & 1) && n_qt <= prefill::kMaxHeadPairTiles &&
-                          prefill::head_pairs_pay(BH, n_qt, causal, sms);
-  if (head_pairs) {
+  // Solo form (one query tile per CTA, two CTAs per SM) unless the paired
+  // grid fits one wave, where zig-zag pairs give every SM equal work, or
+  // the sequence is long enough that the pairs' shared K/V loads win.
+  const bool solo = n_qt <= prefill::kSoloMaxTiles &&
+                    (n_qt == 1 || grid > static_cast<unsigned>(sms));
+  if (solo) {
     using prefill::prefill_kernel;
-    auto kernel = n_qt == 1 ? (dtype == FA_DTYPE_BF16
-                                   ? prefill_kernel<BF16, true, true>
-                                   : prefill_kernel<F16, true, true>)
-                            : (dtype == FA_DTYPE_BF16 ? prefill_kernel<BF16, true>
-                                                      : prefill_kernel<F16, true>);
-    kernel<<<static_cast<unsigned>(hp_ctas), prefill::kThreads,
-             prefill::kSmemBytes, stream>>>(
+    auto kernel = dtype == FA_DTYPE_BF16 ? prefill_kernel<BF16, true>
+                                         : prefill_kernel<F16, true>;
+    kernel<<<static_cast<unsigned>(n_qt) * BH, prefill::Form<true>::kThreads,
+             prefill::Form<true>::kSmemBytes, stream>>>(
         tm_q, tm_k, tm_v, out, N, BH, causal ? 1 : 0, scale_log2, H,
         H / H_kv);
     return cudaGetLastError();
   }
   auto kernel = dtype == FA_DTYPE_BF16 ? prefill::prefill_kernel<BF16>
                                        : prefill::prefill_kernel<F16>;
-  kernel<<<grid, prefill::kThreads, prefill::kSmemBytes, stream>>>(
+  kernel<<<grid, prefill::Form<false>::kThreads,
+           prefill::Form<false>::kSmemBytes, stream>>>(
       tm_q, tm_k, tm_v, out, N, BH, (causal ? 1 : 0) | zigzag, scale_log2, H,
       H / H_kv);
   return cudaGetLastError();

@@ -370,8 +370,13 @@ def test_occupancy_report_rows():
                           "theoretical_occupancy"}
         assert r["max_active_blocks_per_sm"] >= 1
     by = {r["kernel"]: r for r in rows}
-    # tensor-memory kernels run one CTA per SM
+    # the paired prefill form fills an SM (all registers, 512 tensor-memory
+    # columns); the solo form is sized for two per SM (half of each), which
+    # the occupancy API reports as 1 for kernels that allocate tensor
+    # memory, although two run side by side (per-CTA SM stamps on a B200)
     assert by["prefill_kernel"]["max_active_blocks_per_sm"] == 1
+    assert by["prefill_solo_kernel"]["registers_per_thread"] <= 128
+    assert by["prefill_solo_kernel"]["shared_bytes_per_block"] * 2 + 2048 <= 228 * 1024
 
 
 def test_prefill_causal_single_key_rows_are_exact():

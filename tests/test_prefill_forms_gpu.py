@@ -1,10 +1,10 @@
-"""Prefill with an odd number of 128-row query tiles (up to 7) over more
-than one wave of SMs: the kernel then gives each CTA the same tile of two
-heads, their K/V tiles interleaved in one ring. Edges: an odd number of
-(batch, head) units (the last CTA holds one head), grouped K/V heads (two
-heads of a pair may read different K/V heads), ragged N, both dtypes,
-causal and full, against fp32 attention. The small shapes stay below one
-wave and take the one-head-per-CTA form; same bar."""
+"""Prefill in both CTA forms against fp32 attention. The solo form (one
+query tile per CTA, two CTAs per SM) runs every sequence of up to 48 query
+tiles whose paired grid exceeds one wave of SMs; the paired form (two tiles
+of one head per CTA) runs the rest: one-wave grids (zig-zag pairs) and long
+sequences. Edges: short and ragged N, odd (batch, head) counts, grouped K/V
+heads, both dtypes, causal and full, and the sequence lengths on either
+side of the solo/paired switch."""
 
 import pytest
 import torch
@@ -61,3 +61,22 @@ def test_short_prefill_d128_matches_fp32(dtype, tol, b, h, h_kv, n, causal):
     err = (got.float() - reference(q, k, v, causal, scale)).abs().max().item()
     assert err <= tol, err
     assert flashattn_cuda.take_device_error() == 0
+
+
+@pytest.mark.parametrize("b,h,n", [
+    (1, 7, 4096),    # paired grid of 112 CTAs fits one wave: zig-zag pairs
+    (2, 7, 4096),    # 224 pairs: solo
+    (1, 2, 6144),    # 48 pairs on 148 SMs: one wave, paired
+    (2, 4, 6144),    # 48 tiles, 192 pairs: solo
+    (2, 4, 6145),    # 49 tiles: paired
+    (1, 4, 16384),   # long: paired
+])
+@pytest.mark.parametrize("causal", [True, False])
+def test_form_switch_lengths_match_fp32(b, h, n, causal):
+    torch.manual_seed(n + h)
+    q = torch.randn(b, h, n, 64, device="cuda").half()
+    k = torch.randn(b, h, n, 64, device="cuda").half()
+    v = torch.randn(b, h, n, 64, device="cuda").half()
+    got = flashattn_cuda.prefill(q, k, v, causal, 0.125)
+    err = (got.float() - reference(q, k, v, causal, 0.125)).abs().max().item()
+    assert err <= 2e-3, err
