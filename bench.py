@@ -15,11 +15,20 @@ Secondary measurements in the same line (`secondary`):
   c5_decode            long decode B=1 H=14 S=131072; KV sequence-sharded over
                        ranks, per-rank log-sum-exp partials all-gathered with
                        NCCL and merged
+  published_shapes     the reference's published sweep shapes (prefill B1/B8
+                       H12 N4096, B4 H12 N2048, config 2; decode B1 H12
+                       S128-4096, B8 H12 S2048) with cuDNN / flash_attn
+                       kernels timed beside ours (library context only)
+  per_rank             each rank's prefill / C4 / C5 times and work share,
+                       so a scaling run shows its limiter at each N
+`e2e.link` times the pinned host copies alone: link_frac = the longer of
+upload and download / the e2e step.
 Decode GB/s counts valid K+V rows only (128 B per row each for K and V).
 
 `--impl reference` times the reference's CPU path (src/attention_cpu.py,
-restated in oracle/oracle.py) on a bounded sample of the same workload on the
-host cores; under torchrun only rank 0 runs it.
+restated in oracle/oracle.py) on the host cores, one step = 4 of config 3's
+56 (batch, head) evaluations, and prints the same workload config as this
+arm; under torchrun only rank 0 runs it.
 """
 
 import argparse

@@ -78,12 +78,12 @@ int ensure_device(int *device_out) {
                               prefill_d128_kernel_ptr(dt),
                               decode_gqa_kernel_ptr(64, dt),
                               decode_gqa_kernel_ptr(128, dt),
-                              prefill_d128_kernel_ptr(dt, true),
-                              prefill_solo_kernel_ptr(dt)};
+                              prefill_solo_kernel_ptr(dt),
+                              prefill_d128_solo_kernel_ptr(dt)};
     const int bytes[] = {prefill_smem_bytes(), decode_smem_bytes(),
                          decode_d128_smem_bytes(), prefill_d128_smem_bytes(),
                          decode_gqa_smem_bytes(64), decode_gqa_smem_bytes(128),
-                         prefill_d128_smem_bytes(), prefill_solo_smem_bytes()};
+                         prefill_solo_smem_bytes(), prefill_d128_solo_smem_bytes()};
     for (int i = 0; i < 8; ++i) {
       if (cudaFuncSetAttribute(big_smem[i],
                                cudaFuncAttributeMaxDynamicSharedMemorySize,

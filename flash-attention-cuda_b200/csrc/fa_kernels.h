@@ -16,6 +16,8 @@ int prefill_threads();
 const void *prefill_solo_kernel_ptr(int dtype = FA_DTYPE_F16);
 int prefill_solo_smem_bytes();
 int prefill_solo_threads();
+const void *prefill_d128_solo_kernel_ptr(int dtype = FA_DTYPE_F16);
+int prefill_d128_solo_smem_bytes();
 int prefill_smem_bytes();
 cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
                                   const CUtensorMap &tm_k,
@@ -25,8 +27,7 @@ cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
                                   cudaStream_t stream);
 
 // ---- prefill, head_dim 128 (prefill_d128_sm100.cu) -------------------------
-const void *prefill_d128_kernel_ptr(int dtype = FA_DTYPE_F16,
-                                   bool head_pairs = false);
+const void *prefill_d128_kernel_ptr(int dtype = FA_DTYPE_F16);
 int prefill_d128_smem_bytes();
 cudaError_t launch_prefill_d128_kernel(const CUtensorMap &tm_q,
                                        const CUtensorMap &tm_k,

@@ -20,8 +20,8 @@
 // 128-byte-swizzled halves (head dims 0-63 and 64-127) in separate blocks,
 // the layout TMA writes with one 64-column box per half:
 //   Q0, Q1  2 x [128 rows x 128 B] each            64 KiB
-//   K       4 slots x 2 x [64 keys x 128 B]         64 KiB (3 used with one head)
-//   V       4 slots x 2 x [64 keys x 128 B]         64 KiB
+//   K       3 slots x 2 x [64 keys x 128 B]         48 KiB
+//   V       3 slots x 2 x [64 keys x 128 B]         48 KiB
 // Tensor memory (512 columns x 128 lanes, fp32 words):
 //   S_t [64t, 64t+64)   O_t [128+128t, 256+128t)   P_t [384+32t, 416+32t)
 
@@ -42,10 +42,9 @@ constexpr int kHalfBytes = 128;  // one swizzled half-row (64 dims)
 constexpr int kBlockM = 128;     // query rows per tile
 constexpr int kBlockN = 64;      // keys per K/V tile
 constexpr int kTilesPerCta = 2;
-// K/V ring slots: one head per CTA cycles through 3 of them; two heads per
-// CTA (sequences of one query tile, at most two 64-key tiles per head) hold
-// all four of their K/V tiles at once.
-constexpr int kRingSlots = 4;
+// K/V ring slots of the paired form: two key tiles stream ahead of the
+// one in use.
+constexpr int kRingSlots = 3;
 constexpr int kSoftmaxThreads = 128;
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
@@ -82,6 +81,38 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemS = 0;    // + 64 * tile
 constexpr uint32_t kTmemO = 128;  // + 128 * tile
 constexpr uint32_t kTmemP = 384;  // + 32 * tile
+
+// Two CTA forms, as in the head_dim-64 kernel. Paired (kSolo false): the
+// layout above, one CTA per SM. Solo: one query tile per CTA and two CTAs
+// per SM: 256 threads (softmax warps 0-3, producer 4, MMA 5, donors 6-7),
+// tensor memory S [0,64) O [64,192) P [192,224) of a 256-column
+// allocation, and Q (32 KiB) plus a 2-slot K/V ring (64 KiB) of shared
+// memory.
+template <bool kSolo>
+struct Form {
+  static constexpr int kThreads = kSolo ? 256 : 384;
+  static constexpr int kCtasPerSm = kSolo ? 2 : 1;
+  static constexpr int kCtrlWarp0 = kSolo ? 4 : 8;
+  static constexpr int kProducerWarp = kCtrlWarp0;
+  static constexpr int kMmaWarp = kCtrlWarp0 + 1;
+  static constexpr int kSoftmaxRegs = kSolo ? 232 : 240;
+  static constexpr int kQTiles = kSolo ? 1 : 2;
+  static constexpr int kSlots = kSolo ? 2 : kRingSlots;
+  static constexpr uint32_t kKOff = kQOff + kQTiles * kQTile;
+  static constexpr uint32_t kVOff = kKOff + kSlots * kKVTile;
+  static constexpr uint32_t kBarOff = kVOff + kSlots * kKVTile;
+  static constexpr uint32_t kTmemSlotOff = kBarOff + kNumBars * 8;
+  static constexpr uint32_t kAbortOff = kTmemSlotOff + 4;
+  static constexpr uint32_t kSmemBytes = kAbortOff + 4 + 8;
+  static constexpr uint32_t kTmemCols = kSolo ? 256 : 512;
+  static constexpr uint32_t kTmemO = kSolo ? 64 : 128;   // + 128 * tile
+  static constexpr uint32_t kTmemP = kSolo ? 192 : 384;  // + 32 * tile
+  static_assert(128 * kCtrlRegs + 128 * kQTiles * kSoftmaxRegs <=
+                    kThreads * (65536 / (kThreads * kCtasPerSm)),
+                "register split exceeds the launch allocation");
+  static_assert(kCtasPerSm * (kSmemBytes + 1024) <= 228 * 1024,
+                "shared memory of the resident CTAs exceeds the SM's");
+};
 
 template <typename Dt>
 constexpr uint32_t kIdescS = idesc_f16_f32(kBlockM, kBlockN, false, Dt::kFmt);
@@ -150,20 +181,16 @@ __device__ __forceinline__ TileInfo tile_info(int pair, int t, int N,
   return ti;
 }
 
-// kHeadPairs (sequences of one 128-row query tile, N <= 128): the CTA's two
-// tile slots hold query tile 0 of two heads (2 * blockIdx.x and the next)
-// instead of two tiles of one head, whose second slot would stay empty. The
-// two heads' K/V streams interleave in the ring: key tile j of slot t is
-// ring position 2 j + t (position j with one head per CTA).
-template <typename Dt, bool kHeadPairs = false>
-__global__ void __launch_bounds__(kThreads, 1)
+template <typename Dt, bool kSolo = false>
+__global__ void __launch_bounds__(Form<kSolo>::kThreads, Form<kSolo>::kCtasPerSm)
     prefill_d128_kernel(const __grid_constant__ CUtensorMap tm_q,
                         const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v,
                         __half *__restrict__ out, int N, int BH, int causal,
                         float scale_log2, int H, int group) {
+  using F = Form<kSolo>;
   extern __shared__ __align__(1024) uint8_t smem[];
-  constexpr int kStages = kHeadPairs ? kRingSlots : 3;
+  constexpr int kStages = F::kSlots;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
@@ -178,40 +205,38 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Heaviest causal pairs first, heads fastest.
   const int n_qt = (N + kBlockM - 1) / kBlockM;
   const int n_pairs = (n_qt + kTilesPerCta - 1) / kTilesPerCta;
-  const int pair =
-      kHeadPairs ? 0 : n_pairs - 1 - static_cast<int>(blockIdx.x / BH);
-  const int bh = kHeadPairs ? 2 * static_cast<int>(blockIdx.x)
-                            : static_cast<int>(blockIdx.x % BH);
-  const int bh1 = kHeadPairs ? bh + 1 : bh;  // query head of tile 1
+  const int pair = n_pairs - 1 - static_cast<int>(blockIdx.x / BH);
+  const int bh = static_cast<int>(blockIdx.x % BH);
   const int kv_bh = (bh / H) * (H / group) + (bh % H) / group;
-  const int kv_bh1 = (bh1 / H) * (H / group) + (bh1 % H) / group;
   TileInfo t0 = tile_info(pair, 0, N, causal, zigzag);
   TileInfo t1 = tile_info(pair, 1, N, causal, zigzag);
-  if (kHeadPairs) {
-    t1.qt = 0;
-    t1.n_kv = bh1 < BH ? t0.n_kv : 0;
+  if (kSolo) {
+    // one query tile per CTA, heaviest first, heads fastest
+    t0.qt = n_qt - 1 - static_cast<int>(blockIdx.x / BH);
+    t0.n_kv = ((causal ? min((t0.qt + 1) * kBlockM, N) : N) + kBlockN - 1) /
+              kBlockN;
+    t1.qt = t0.qt;
+    t1.n_kv = 0;
   }
   const int n_kv = t0.n_kv > t1.n_kv ? t0.n_kv : t1.n_kv;
 
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kBarOff);
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kTmemSlotOff);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + F::kBarOff);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + F::kTmemSlotOff);
   volatile uint32_t *abort_flag =
-      reinterpret_cast<volatile uint32_t *>(smem + kAbortOff);
+      reinterpret_cast<volatile uint32_t *>(smem + F::kAbortOff);
 
   // Ring positions (tile 1's skipped when the CTA has one head); a
   // position's stage is p % kStages.
-  const int n_pos = kHeadPairs ? 2 * n_kv : n_kv;
-  auto pos_used = [&](int p) { return !kHeadPairs || !(p & 1) || t1.n_kv > 0; };
+  const int n_pos = n_kv;
   auto load_pos = [&](int p) {
-    if (!pos_used(p)) return;
-    const int j = kHeadPairs ? p >> 1 : p;
-    const int kvh = (kHeadPairs && (p & 1)) ? kv_bh1 : kv_bh;
+    const int j = p;
+    const int kvh = kv_bh;
     const int s = p % kStages;
     mbar_arrive_expect_tx(&bars[kBarKFull + s], 2 * kKVTile);
     for (int h = 0; h < 2; ++h) {
-      tma_load_3d(smem + kKOff + s * kKVTile + h * kKVHalf, &tm_k,
+      tma_load_3d(smem + F::kKOff + s * kKVTile + h * kKVHalf, &tm_k,
                   &bars[kBarKFull + s], 64 * h, j * kBlockN, kvh);
-      tma_load_3d(smem + kVOff + s * kKVTile + h * kKVHalf, &tm_v,
+      tma_load_3d(smem + F::kVOff + s * kKVTile + h * kKVHalf, &tm_v,
                   &bars[kBarKFull + s], 64 * h, j * kBlockN, kvh);
     }
   };
@@ -221,7 +246,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // overlaps the TMEM allocation), then turns the device error word into
   // the abort flag.
   int preissued = 0;
-  if (warp == kProducerWarp && lane == 0) {
+  if (warp == F::kProducerWarp && lane == 0) {
     mbar_init(&bars[kBarQFull], 1);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&bars[kBarKFull + s], 1);
@@ -244,14 +269,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row0 = (t == 0 ? t0.qt : t1.qt) * kBlockM;
       for (int h = 0; h < 2; ++h)
         tma_load_3d(smem + kQOff + t * kQTile + h * kQHalf, &tm_q,
-                    &bars[kBarQFull], 64 * h, row0, t ? bh1 : bh);
+                    &bars[kBarQFull], 64 * h, row0, bh);
     }
     for (; preissued < n_pos && preissued < kStages; ++preissued)
       load_pos(preissued);
     *abort_flag = device_failed() ? 1u : 0u;
   }
-  if (warp == kMmaWarp) {
-    tmem_alloc(tmem_slot, kTmemCols);
+  if (warp == F::kMmaWarp) {
+    tmem_alloc(tmem_slot, F::kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -260,18 +285,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
   const uint32_t sbase = smem_u32(smem);
 
-  if (warp >= 8) {
+  if (warp >= F::kCtrlWarp0) {
     setmaxnreg_dec<kCtrlRegs>();
-    if (warp == kProducerWarp) {
+    if (warp == F::kProducerWarp) {
       // ---------------------------------------------------------------- TMA
       if (lane == 0) {
         int issued = preissued;
-        // (two heads per CTA: every position was issued above)
-        for (int p = preissued; !kHeadPairs && p < n_pos; ++p) {
+        for (int p = preissued; p < n_pos; ++p) {
           if (*abort_flag) break;
           const int s = p % kStages;
           const int use = p / kStages;
-          if (pos_used(p) && use > 0 &&
+          if (use > 0 &&
               !mbar_wait(&bars[kBarKVEmpty + s], (use - 1) & 1)) {
             *abort_flag = 1;
             break;
@@ -283,24 +307,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_wait(&bars[kBarQFull], 0);
           for (int p = (issued > kStages ? issued - kStages : 0); p < issued;
                ++p)
-            if (pos_used(p))
-              mbar_wait(&bars[kBarKFull + p % kStages], (p / kStages) & 1);
+            mbar_wait(&bars[kBarKFull + p % kStages], (p / kStages) & 1);
         }
       }
-    } else if (warp == kMmaWarp) {
+    } else if (warp == F::kMmaWarp) {
       // ---------------------------------------------------------------- MMA
       const bool leader = elect_one();
       const uint32_t tmem = __shfl_sync(0xffffffffu, tmem_base, 0);
       const int n_t[2] = {t0.n_kv, t1.n_kv};
       const uint64_t desc0 = sw128_desc(sbase);
       const uint64_t vdesc0 = sw128_desc_lbo(sbase, kKVHalf);
-      // ring position of key tile j of slot t
-      auto kpos = [&](int t, int j) { return kHeadPairs ? 2 * j + t : j; };
-      // with two heads, tile 1's first K/V tile has its own ring position
       bool ok = mbar_wait(&bars[kBarQFull], 0) &&
-                mbar_wait(&bars[kBarKFull + 0], 0) &&
-                (!kHeadPairs || n_t[1] == 0 ||
-                 mbar_wait(&bars[kBarKFull + 1], 0));
+                mbar_wait(&bars[kBarKFull + 0], 0);
       if (ok) {
         tc_fence_after();
         if (leader) {
@@ -308,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (n_t[t] == 0) continue;
             issue_s_tile<Dt>(tmem + kTmemS + 64 * t,
                          desc0 + ((kQOff + t * kQTile) >> 4),
-                         desc0 + ((kKOff + kpos(t, 0) * kKVTile) >> 4));
+                         desc0 + (F::kKOff >> 4));
             mma_commit(&bars[kBarSFull + t]);
           }
         }
@@ -323,13 +341,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = 0; t < kTilesPerCta; ++t) {
           const int nt = n_t[t];
           if (!ok || j >= nt) continue;
-          const int s = kpos(t, j) % kStages;  // K_j, V_j of this slot
-          const int p1 = kpos(t, j + 1);
+          const int s = j % kStages;  // K_j, V_j
+          const int p1 = j + 1;
           const int s1 = p1 % kStages;         // K_{j+1}
           if (j + 1 < nt) {
             // K/V tile j+1 is waited on once per round (by the first tile
-            // that uses it, or by each slot with two heads)
-            const bool need_kv = kHeadPairs || (t == 0) || (n_t[0] <= j + 1);
+            // that uses it)
+            const bool need_kv = (t == 0) || (n_t[0] <= j + 1);
             if ((need_kv &&
                  !mbar_wait(&bars[kBarKFull + s1], (p1 / kStages) & 1)) ||
                 !mbar_wait(&bars[kBarSFree + t], j & 1)) {
@@ -340,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (leader) {
               issue_s_tile<Dt>(tmem + kTmemS + 64 * t,
                            desc0 + ((kQOff + t * kQTile) >> 4),
-                           desc0 + ((kKOff + s1 * kKVTile) >> 4));
+                           desc0 + ((F::kKOff + s1 * kKVTile) >> 4));
               mma_commit(&bars[kBarSFull + t]);
             }
             __syncwarp();
@@ -351,17 +369,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           if (leader) {
-            issue_pv_tile<Dt>(tmem + kTmemO + 128 * t, tmem + kTmemP + 32 * t,
-                          vdesc0 + ((kVOff + s * kKVTile) >> 4), j > 0);
+            issue_pv_tile<Dt>(tmem + F::kTmemO + 128 * t, tmem + F::kTmemP + 32 * t,
+                          vdesc0 + ((F::kVOff + s * kKVTile) >> 4), j > 0);
             mma_commit(&bars[kBarODone + t]);
           }
           __syncwarp();
         }
         if (!ok) break;
-        // release round j's ring positions (both slots' with two heads)
+        // release round j's ring stage
         if (leader) {
-          mma_commit(&bars[kBarKVEmpty + kpos(0, j) % kStages]);
-          if (kHeadPairs) mma_commit(&bars[kBarKVEmpty + kpos(1, j) % kStages]);
+          mma_commit(&bars[kBarKVEmpty + j % kStages]);
         }
         __syncwarp();
       }
@@ -371,15 +388,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(&bars[kBarDrain], 0);
     }
   } else {
-    setmaxnreg_inc<kSoftmaxRegs>();
+    setmaxnreg_inc<F::kSoftmaxRegs>();
     // -------------------------------------------------------------- softmax
     const int t = warp >> 2;
     const int row = threadIdx.x & 127;
     const TileInfo ti = t == 0 ? t0 : t1;
     const uint32_t lane_addr = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t tS = tmem_base + lane_addr + kTmemS + 64 * t;
-    const uint32_t tO = tmem_base + lane_addr + kTmemO + 128 * t;
-    const uint32_t tP = tmem_base + lane_addr + kTmemP + 32 * t;
+    const uint32_t tO = tmem_base + lane_addr + F::kTmemO + 128 * t;
+    const uint32_t tP = tmem_base + lane_addr + F::kTmemP + 32 * t;
     uint64_t *s_full = &bars[kBarSFull + t];
     uint64_t *s_free = &bars[kBarSFree + t];
     uint64_t *p_full = &bars[kBarPFull + t];
@@ -497,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const float inv_l = (l_sum > 0.f) ? 1.f / l_sum : 0.f;
         uint4 *dst = reinterpret_cast<uint4 *>(
-            out + (static_cast<size_t>(t ? bh1 : bh) * N + q_row) * kD);
+            out + (static_cast<size_t>(bh) * N + q_row) * kD);
 #pragma unroll
         for (int h = 0; h < kD / 32; ++h) {
           uint32_t o[32];
@@ -528,23 +545,29 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == kMmaWarp) {
+  if (warp == F::kMmaWarp) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    tmem_dealloc(tmem_base, F::kTmemCols);
   }
 }
 
 }  // namespace prefill128
 
-const void *prefill_d128_kernel_ptr(int dtype, bool head_pairs) {
+const void *prefill_d128_kernel_ptr(int dtype) {
   using prefill128::prefill_d128_kernel;
-  if (head_pairs)
-    return dtype == FA_DTYPE_BF16
-               ? reinterpret_cast<const void *>(prefill_d128_kernel<BF16, true>)
-               : reinterpret_cast<const void *>(prefill_d128_kernel<F16, true>);
   return dtype == FA_DTYPE_BF16
              ? reinterpret_cast<const void *>(prefill_d128_kernel<BF16>)
              : reinterpret_cast<const void *>(prefill_d128_kernel<F16>);
+}
+const void *prefill_d128_solo_kernel_ptr(int dtype) {
+  return dtype == FA_DTYPE_BF16
+             ? reinterpret_cast<const void *>(
+                   prefill128::prefill_d128_kernel<BF16, true>)
+             : reinterpret_cast<const void *>(
+                   prefill128::prefill_d128_kernel<F16, true>);
+}
+int prefill_d128_solo_smem_bytes() {
+  return static_cast<int>(prefill128::Form<true>::kSmemBytes);
 }
 int prefill_d128_smem_bytes() {
   return static_cast<int>(prefill128::kSmemBytes);
@@ -566,15 +589,18 @@ cudaError_t launch_prefill_d128_kernel(const CUtensorMap &tm_q,
   // One wave of CTAs: zig-zag pairs of equal causal work, so the kernel
   // does not wait on the heaviest pair. Several waves: heaviest first.
   const int zigzag = causal && grid <= static_cast<unsigned>(sms) ? 2 : 0;
-  // One query tile per head (N <= 128): query tile 0 of two heads per CTA,
-  // once the one-head grid no longer fits one wave of SMs (below that the
-  // heads run side by side on idle SMs instead).
-  if (n_qt == 1 && grid > static_cast<unsigned>(sms)) {
+  // Solo form for short sequences (measured, TFLOP/s, solo vs paired:
+  // B64 H32 N128 causal 145 vs 123, B16 H12 N384 causal 253 vs 208, B8 H32
+  // N640 causal 392 vs 369; from four tiles on its 2-slot K/V ring loses:
+  // B16 H32 N512 causal 343 vs 385, config 3's shape 806 vs 954).
+  const bool solo = (n_qt <= 3 || n_qt == 5) &&
+                    (n_qt == 1 || grid > static_cast<unsigned>(sms));
+  if (solo) {
     auto kernel = dtype == FA_DTYPE_BF16
                       ? prefill128::prefill_d128_kernel<BF16, true>
                       : prefill128::prefill_d128_kernel<F16, true>;
-    kernel<<<static_cast<unsigned>((BH + 1) / 2), prefill128::kThreads,
-             prefill128::kSmemBytes, stream>>>(
+    kernel<<<static_cast<unsigned>(n_qt) * BH, prefill128::Form<true>::kThreads,
+             prefill128::Form<true>::kSmemBytes, stream>>>(
         tm_q, tm_k, tm_v, out, N, BH, causal ? 1 : 0, scale_log2, H,
         H / H_kv);
     return cudaGetLastError();
