@@ -31,6 +31,8 @@
 #include <math.h>
 #include <stdint.h>
 
+#include <algorithm>
+
 #include "fa_kernels.h"
 #include "fa_sm100.cuh"
 
@@ -187,7 +189,8 @@ __global__ void __launch_bounds__(Form<kSolo>::kThreads, Form<kSolo>::kCtasPerSm
                         const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v,
                         __half *__restrict__ out, int N, int BH, int causal,
-                        float scale_log2, int H, int group) {
+                        float scale_log2, int H, int group,
+                        int head_block) {
   using F = Form<kSolo>;
   extern __shared__ __align__(1024) uint8_t smem[];
   constexpr int kStages = F::kSlots;
@@ -202,17 +205,27 @@ __global__ void __launch_bounds__(Form<kSolo>::kThreads, Form<kSolo>::kCtasPerSm
     return;
   }
 
-  // Heaviest causal pairs first, heads fastest.
+  // Heaviest causal pairs first, heads fastest, within blocks of
+  // head_block heads (0: one block of all heads) whose K/V fit in L2, so a
+  // head's tiles run close together and its K/V is read from HBM once.
   const int n_qt = (N + kBlockM - 1) / kBlockM;
   const int n_pairs = (n_qt + kTilesPerCta - 1) / kTilesPerCta;
-  const int pair = n_pairs - 1 - static_cast<int>(blockIdx.x / BH);
-  const int bh = static_cast<int>(blockIdx.x % BH);
+  const int n_units = kSolo ? n_qt : n_pairs;  // per head
+  const int hb = head_block > 0 ? head_block : BH;
+  const int blk = static_cast<int>(blockIdx.x) / (hb * n_units);
+  const int r = static_cast<int>(blockIdx.x) % (hb * n_units);
+  const int h0 = blk * hb;
+  const int h_here = min(hb, BH - h0);
+  const int unit = n_units - 1 - r / h_here;  // heaviest first
+  const int pair = unit;
+  const int bh = h0 + r % h_here;
+  if (h_here <= 0 || bh >= BH) return;  // only if the grid outran the work
   const int kv_bh = (bh / H) * (H / group) + (bh % H) / group;
   TileInfo t0 = tile_info(pair, 0, N, causal, zigzag);
   TileInfo t1 = tile_info(pair, 1, N, causal, zigzag);
   if (kSolo) {
     // one query tile per CTA, heaviest first, heads fastest
-    t0.qt = n_qt - 1 - static_cast<int>(blockIdx.x / BH);
+    t0.qt = unit;
     t0.n_kv = ((causal ? min((t0.qt + 1) * kBlockM, N) : N) + kBlockN - 1) /
               kBlockN;
     t1.qt = t0.qt;
@@ -602,14 +615,31 @@ cudaError_t launch_prefill_d128_kernel(const CUtensorMap &tm_q,
     kernel<<<static_cast<unsigned>(n_qt) * BH, prefill128::Form<true>::kThreads,
              prefill128::Form<true>::kSmemBytes, stream>>>(
         tm_q, tm_k, tm_v, out, N, BH, causal ? 1 : 0, scale_log2, H,
-        H / H_kv);
+        H / H_kv, 0);
     return cudaGetLastError();
   }
   auto kernel = dtype == FA_DTYPE_BF16 ? prefill128::prefill_d128_kernel<BF16>
                                        : prefill128::prefill_d128_kernel<F16>;
+#ifndef FA_D128_L2_MB
+#define FA_D128_L2_MB 32
+#endif
+  // Blocks of heads whose K/V (both tensors, all N rows) fit in about
+  // FA_D128_L2_MB of L2, equal in size, for multi-wave grids.
+  int head_block = 0;
+  if (!zigzag && FA_D128_L2_MB > 0) {
+    // K and V bytes per query head (grouped heads share theirs)
+    const long long per_head = std::max(
+        1LL, static_cast<long long>(N) * 2 * prefill128::kD * 2 * H_kv / H);
+    const long long budget = static_cast<long long>(FA_D128_L2_MB) << 20;
+    const int fit = static_cast<int>(std::max(1LL, budget / per_head));
+    if (fit < BH) {
+      const int blocks = (BH + fit - 1) / fit;
+      head_block = (BH + blocks - 1) / blocks;
+    }
+  }
   kernel<<<grid, prefill128::kThreads, prefill128::kSmemBytes, stream>>>(
       tm_q, tm_k, tm_v, out, N, BH, (causal ? 1 : 0) | zigzag, scale_log2, H,
-      H / H_kv);
+      H / H_kv, head_block);
   return cudaGetLastError();
 }
 

@@ -226,7 +226,7 @@ __global__ void __launch_bounds__(Form<kSolo>::kThreads, Form<kSolo>::kCtasPerSm
                    const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v,
                    __half *__restrict__ out, int N, int BH, int causal,
-                   float scale_log2, int H, int group) {
+                   float scale_log2, int H, int group, int head_block) {
   using F = Form<kSolo>;
   extern __shared__ __align__(1024) uint8_t smem[];
   constexpr int kStages = kRingSlots;
@@ -243,16 +243,26 @@ __global__ void __launch_bounds__(Form<kSolo>::kThreads, Form<kSolo>::kCtasPerSm
 
   // Heaviest first: blockIdx.x walks query tiles (solo) or query-tile pairs
   // from the last (most keys) to the first, heads fastest.
+  // Within blocks of head_block heads (0: all heads) whose K/V fit in L2,
+  // so a head's tiles run close together and its K/V is read once.
   const int n_qt = (N + kBlockM - 1) / kBlockM;
   const int n_pairs = (n_qt + 1) / 2;
-  const int pair = n_pairs - 1 - static_cast<int>(blockIdx.x / BH);
-  const int bh = static_cast<int>(blockIdx.x % BH);
+  const int n_units = kSolo ? n_qt : n_pairs;  // per head
+  const int hb = head_block > 0 ? head_block : BH;
+  const int blk = static_cast<int>(blockIdx.x) / (hb * n_units);
+  const int r = static_cast<int>(blockIdx.x) % (hb * n_units);
+  const int h0 = blk * hb;
+  const int h_here = min(hb, BH - h0);
+  const int unit = n_units - 1 - r / h_here;  // heaviest first
+  const int pair = unit;
+  const int bh = h0 + r % h_here;
+  if (h_here <= 0 || bh >= BH) return;  // only if the grid outran the work
   // K/V head of the query head: `group` query heads share one K/V head
   // (group == 1 without grouped-query attention).
   const int kv_bh = (bh / H) * (H / group) + (bh % H) / group;
   TileInfo t0, t1;
   if (kSolo) {
-    t0.qt = n_qt - 1 - static_cast<int>(blockIdx.x / BH);
+    t0.qt = unit;
     t0.n_kv = causal ? t0.qt + 1 : n_qt;
     t1.qt = t0.qt;
     t1.n_kv = 0;
@@ -629,6 +639,22 @@ cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
   // the sequence is long enough that the pairs' shared K/V loads win.
   const bool solo = n_qt <= prefill::kSoloMaxTiles &&
                     (n_qt == 1 || grid > static_cast<unsigned>(sms));
+#ifndef FA_L2_MB
+#define FA_L2_MB 32
+#endif
+  // Blocks of heads whose K/V (both tensors, all N rows) fit in about
+  // FA_L2_MB of L2, equal in size, for multi-wave grids.
+  int head_block = 0;
+  if (!zigzag && FA_L2_MB > 0) {
+    const long long per_head = std::max(
+        1LL, static_cast<long long>(N) * 2 * kHeadDim * 2 * H_kv / H);
+    const long long budget = static_cast<long long>(FA_L2_MB) << 20;
+    const int fit = static_cast<int>(std::max(1LL, budget / per_head));
+    if (fit < BH) {
+      const int blocks = (BH + fit - 1) / fit;
+      head_block = (BH + blocks - 1) / blocks;
+    }
+  }
   if (solo) {
     using prefill::prefill_kernel;
     auto kernel = dtype == FA_DTYPE_BF16 ? prefill_kernel<BF16, true>
@@ -636,7 +662,7 @@ cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
     kernel<<<static_cast<unsigned>(n_qt) * BH, prefill::Form<true>::kThreads,
              prefill::Form<true>::kSmemBytes, stream>>>(
         tm_q, tm_k, tm_v, out, N, BH, causal ? 1 : 0, scale_log2, H,
-        H / H_kv);
+        H / H_kv, head_block);
     return cudaGetLastError();
   }
   auto kernel = dtype == FA_DTYPE_BF16 ? prefill::prefill_kernel<BF16>
@@ -644,7 +670,7 @@ cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
   kernel<<<grid, prefill::Form<false>::kThreads,
            prefill::Form<false>::kSmemBytes, stream>>>(
       tm_q, tm_k, tm_v, out, N, BH, (causal ? 1 : 0) | zigzag, scale_log2, H,
-      H / H_kv);
+      H / H_kv, head_block);
   return cudaGetLastError();
 }
 
