@@ -357,27 +357,63 @@ __device__ void merger(const DecodeArgs &a, uint8_t *red_base,
     if (!last) continue;
     __threadfence();
     // every partial of the segment is in place: merge them
-    float M2 = kNegBig;
+    // (m, l) of up to 32 partials per lane round; with at most 32 partials
+    // (the usual case) the first round's values are kept for the weights.
+    float M2 = kNegBig, m_keep = kNegBig, l_keep = 0.f;
     for (int c = c0 + lane; c <= c1; c += 32) {
       const float *pp = a.ws_partials + (g + c) * static_cast<size_t>(kPartialFloats);
-      if (__ldcg(pp + 1) > 0.f) M2 = fmaxf(M2, __ldcg(pp));
+      const float lc = __ldcg(pp + 1);
+      const float mc = __ldcg(pp);
+      if (c < c0 + 32) {
+        m_keep = mc;
+        l_keep = lc;
+      }
+      if (lc > 0.f) M2 = fmaxf(M2, mc);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1)
       M2 = fmaxf(M2, __shfl_xor_sync(0xffffffffu, M2, o));
+    // Weights one partial per lane, then the head dims in batches of 16
+    // partials whose loads are all in flight together (the merge is on the
+    // kernel's tail: a load round trip per partial would cost microseconds).
     float L2 = 0.f, B0 = 0.f, B1 = 0.f;
-#pragma unroll 4
-    for (int c = c0; c <= c1; ++c) {
-      const float *pp = a.ws_partials + (g + c) * static_cast<size_t>(kPartialFloats);
-      const float lc = __ldcg(pp + 1);
-      const float mc = __ldcg(pp);
-      const float x0 = __ldcg(pp + 4 + lane);
-      const float x1 = __ldcg(pp + 4 + 32 + lane);
-      const float fc = lc > 0.f ? fast_exp2(mc - M2) : 0.f;
-      L2 = fmaf(lc, fc, L2);
-      B0 = fmaf(x0, fc, B0);
-      B1 = fmaf(x1, fc, B1);
+    for (int cb = c0; cb <= c1; cb += 32) {
+      const int nb = c1 - cb + 1 < 32 ? c1 - cb + 1 : 32;
+      float fc = 0.f;
+      if (lane < nb) {
+        float lc = l_keep, mc = m_keep;
+        if (cb != c0) {
+          const float *pp = a.ws_partials +
+                            (g + cb + lane) * static_cast<size_t>(kPartialFloats);
+          lc = __ldcg(pp + 1);
+          mc = __ldcg(pp);
+        }
+        if (lc > 0.f) fc = fast_exp2(mc - M2);
+        L2 = fmaf(lc, fc, L2);
+      }
+      for (int i0 = 0; i0 < nb; i0 += 16) {
+        float x0[16], x1[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          x0[i] = 0.f;
+          x1[i] = 0.f;
+          if (i0 + i < nb) {
+            const float *pp = a.ws_partials +
+                              (g + cb + i0 + i) * static_cast<size_t>(kPartialFloats);
+            x0[i] = __ldcg(pp + 4 + lane);
+            x1[i] = __ldcg(pp + 4 + 32 + lane);
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float f = __shfl_sync(0xffffffffu, fc, (i0 + i) & 31);
+          B0 = fmaf(x0[i], f, B0);
+          B1 = fmaf(x1[i], f, B1);
+        }
+      }
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) L2 += __shfl_xor_sync(0xffffffffu, L2, o);
     finish_segment(a, g, M2, L2, B0, B1, lane);
   }
 }
