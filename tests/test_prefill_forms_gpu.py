@@ -80,3 +80,27 @@ def test_form_switch_lengths_match_fp32(b, h, n, causal):
     got = flashattn_cuda.prefill(q, k, v, causal, 0.125)
     err = (got.float() - reference(q, k, v, causal, 0.125)).abs().max().item()
     assert err <= 2e-3, err
+
+
+@pytest.mark.parametrize("b,h,h_kv,n,d,causal,dtype", [
+    (4, 14, 14, 4096, 64, True, torch.float16),    # 56 MB of K/V: 2 blocks of 28
+    (3, 13, 13, 4096, 64, False, torch.float16),   # 39 heads: uneven blocks
+    (2, 24, 6, 8192, 64, True, torch.float16),     # grouped K/V heads in blocks
+    (4, 14, 14, 4096, 64, True, torch.bfloat16),
+    (4, 7, 7, 4096, 128, True, torch.float16),     # d128: 2 MB per head
+    (3, 11, 11, 4096, 128, False, torch.bfloat16),
+])
+def test_head_block_launch_order_matches_fp32(b, h, h_kv, n, d, causal, dtype):
+    """Grids whose K/V exceed the L2 budget launch in blocks of heads; every
+    (head, query tile) must still be computed once, for every block size."""
+    torch.manual_seed(b * h + n + d)
+    q = torch.randn(b, h, n, d, device="cuda").to(dtype)
+    k = torch.randn(b, h_kv, n, d, device="cuda").to(dtype)
+    v = torch.randn(b, h_kv, n, d, device="cuda").to(dtype)
+    scale = d ** -0.5
+    got = flashattn_cuda.prefill(q, k, v, causal, scale)
+    tol = 2e-3 if dtype == torch.float16 else 1.5e-2
+    for bi in range(b):  # per batch entry keeps the fp32 reference small
+        ref = reference(q[bi:bi + 1], k[bi:bi + 1], v[bi:bi + 1], causal, scale)
+        err = (got[bi:bi + 1].float() - ref).abs().max().item()
+        assert err <= tol, (bi, err)
