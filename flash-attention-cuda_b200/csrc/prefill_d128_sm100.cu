@@ -121,13 +121,13 @@ constexpr uint32_t kIdescS = idesc_f16_f32(kBlockM, kBlockN, false, Dt::kFmt);
 template <typename Dt>
 constexpr uint32_t kIdescPV = idesc_f16_f32(kBlockM, kD, true, Dt::kFmt);
 constexpr float kRescaleThreshold = 8.0f;
-#ifndef FA_D128_MASK8
-#define FA_D128_MASK8 0x3B
-#endif
+// K/V bytes of one block of heads in the launch order (measured on C3-shape
+// and N 2048-8192 grids: 32 MiB best or tied; 56 MiB lost 20 % on C3).
+constexpr long long kHeadBlockL2Bytes = 32ll << 20;
 // Bit i set: column pair i of every 8 takes its exponentials from the MUFU
 // unit, the others from the polynomial on the FMA pipe (the same balance as
 // the head_dim-64 kernel).
-constexpr unsigned kMufuMask8 = FA_D128_MASK8;
+constexpr unsigned kMufuMask8 = 0x3B;
 
 // S = Q K^T for one 128x64 tile: 8 MMAs of K=16; steps 0-3 read the first
 // 64-dim half of Q and K, steps 4-7 the second half (a separate block).
@@ -620,17 +620,14 @@ cudaError_t launch_prefill_d128_kernel(const CUtensorMap &tm_q,
   }
   auto kernel = dtype == FA_DTYPE_BF16 ? prefill128::prefill_d128_kernel<BF16>
                                        : prefill128::prefill_d128_kernel<F16>;
-#ifndef FA_D128_L2_MB
-#define FA_D128_L2_MB 32
-#endif
   // Blocks of heads whose K/V (both tensors, all N rows) fit in about
-  // FA_D128_L2_MB of L2, equal in size, for multi-wave grids.
+  // kHeadBlockL2Bytes of L2, equal in size, for multi-wave grids.
   int head_block = 0;
-  if (!zigzag && FA_D128_L2_MB > 0) {
+  if (!zigzag) {
     // K and V bytes per query head (grouped heads share theirs)
     const long long per_head = std::max(
         1LL, static_cast<long long>(N) * 2 * prefill128::kD * 2 * H_kv / H);
-    const long long budget = static_cast<long long>(FA_D128_L2_MB) << 20;
+    const long long budget = prefill128::kHeadBlockL2Bytes;
     const int fit = static_cast<int>(std::max(1LL, budget / per_head));
     if (fit < BH) {
       const int blocks = (BH + fit - 1) / fit;

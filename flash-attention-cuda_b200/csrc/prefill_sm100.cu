@@ -58,6 +58,9 @@ constexpr int kRingSlots = 3;
 // N 4096 solo 743 vs paired 724 TFLOP/s, N 8192 798 vs 809, N 16384 738 vs
 // 746).
 constexpr int kSoloMaxTiles = 48;
+// K/V bytes of one block of heads in the launch order (the same budget as
+// the head_dim-128 kernel; B8 H12 N4096 full +5 %, C3 unchanged).
+constexpr long long kHeadBlockL2Bytes = 32ll << 20;
 constexpr int kSoftmaxThreads = 128;  // per query tile
 constexpr int kCtrlRegs = 24;
 constexpr uint32_t kTileBytes = kBlockN * kRowBytes;  // 16 KiB
@@ -639,16 +642,13 @@ cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
   // the sequence is long enough that the pairs' shared K/V loads win.
   const bool solo = n_qt <= prefill::kSoloMaxTiles &&
                     (n_qt == 1 || grid > static_cast<unsigned>(sms));
-#ifndef FA_L2_MB
-#define FA_L2_MB 32
-#endif
   // Blocks of heads whose K/V (both tensors, all N rows) fit in about
-  // FA_L2_MB of L2, equal in size, for multi-wave grids.
+  // kHeadBlockL2Bytes of L2, equal in size, for multi-wave grids.
   int head_block = 0;
-  if (!zigzag && FA_L2_MB > 0) {
+  if (!zigzag) {
     const long long per_head = std::max(
         1LL, static_cast<long long>(N) * 2 * kHeadDim * 2 * H_kv / H);
-    const long long budget = static_cast<long long>(FA_L2_MB) << 20;
+    const long long budget = prefill::kHeadBlockL2Bytes;
     const int fit = static_cast<int>(std::max(1LL, budget / per_head));
     if (fit < BH) {
       const int blocks = (BH + fit - 1) / fit;
