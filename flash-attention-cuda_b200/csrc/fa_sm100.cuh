@@ -285,17 +285,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 
-// Waits for this thread's outstanding tensor-memory loads, naming the
-// registers of the last one as read-write operands: the compiler then
-// cannot read (or move) them before the load has landed, which lets a load
-// stay in flight while other registers are worked on.
-__device__ __forceinline__ void tmem_wait_ld_into(uint32_t (&r)[32]) {
-  asm volatile("tcgen05.wait::ld.sync.aligned;"
-               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
-               :
-               : "memory");
-}
-
 __device__ __forceinline__ void tmem_st32(uint32_t taddr,
                                           const uint32_t (&r)[32]) {
   asm volatile(
@@ -414,43 +403,10 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
   return __fadd2_rn(a, b);
 }
 
-__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
-  return __fmul2_rn(a, b);
-}
-
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
-}
-
-// 2^x for two values on the FMA/ALU pipes instead of the MUFU unit.
-// Cody-Waite style range reduction: x = j + f with j = round(x) and
-// |f| <= 1/2, where j comes from the "add 1.5 * 2^23" rounding trick (the
-// integer lands in the low mantissa bits of t). 2^f is a degree-3 polynomial
-// whose coefficients were fit for this project by iteratively reweighted
-// least squares toward the minimax relative error on [-1/2, 1/2]
-// (max relative error 7.5e-5, below half an fp16 ulp, which is all the
-// result needs: it becomes an fp16 P entry). Finally j is added to the
-// exponent field. Inputs below -125 are clamped (the result is then ~0).
-__device__ __forceinline__ float2 exp2_poly2(float2 x) {
-  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
-  constexpr float kC0 = 0.99992806f;
-  constexpr float kC1 = 0.69326097f;
-  constexpr float kC2 = 0.24261113f;
-  constexpr float kC3 = 0.05517166f;
-  x.x = fmaxf(x.x, -125.f);
-  x.y = fmaxf(x.y, -125.f);
-  const float2 t = fadd2(x, make_float2(kRound, kRound));
-  const float2 r = fadd2(t, make_float2(-kRound, -kRound));
-  const float2 f = ffma2(r, make_float2(-1.f, -1.f), x);
-  float2 p = ffma2(make_float2(kC3, kC3), f, make_float2(kC2, kC2));
-  p = ffma2(p, f, make_float2(kC1, kC1));
-  p = ffma2(p, f, make_float2(kC0, kC0));
-  float2 out;
-  out.x = __uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23));
-  out.y = __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23));
-  return out;
 }
 
 // fma with the result clamped to [0, 1] (the .sat modifier; there is no
@@ -461,13 +417,19 @@ __device__ __forceinline__ float fma_sat(float a, float b, float c) {
   return d;
 }
 
-// 2^x for two values on the FMA pipe, the exponent given in clamped affine
-// form: xs in [0, 1] stands for x = kExp2Lo + kExp2Span * xs, so the caller
-// forms xs = saturate(s * a + b) with one scalar FMA per value and the clamp
-// of x to [-126, 127] comes free with it (the range keeps the biased
-// exponent written below inside 0..254). Same range reduction and
-// polynomial as exp2_poly2: t = j + 1.5 * 2^23 rounds x to the integer j,
-// f = x - j, 2^f from the degree-3 fit, j added to the exponent field.
+// 2^x for two values on the FMA pipe instead of the MUFU unit, the exponent
+// given in clamped affine form: xs in [0, 1] stands for
+// x = kExp2Lo + kExp2Span * xs, so the caller forms xs = saturate(s * a + b)
+// with one scalar FMA per value and the clamp of x to [-126, 127] comes
+// free with it (the range keeps the biased exponent written below inside
+// 0..254). Cody-Waite style range reduction: x = j + f with j = round(x)
+// and |f| <= 1/2, where j comes from the "add 1.5 * 2^23" rounding trick
+// (the integer lands in the low mantissa bits of t). 2^f is a degree-3
+// polynomial whose coefficients were fit for this project by iteratively
+// reweighted least squares toward the minimax relative error on
+// [-1/2, 1/2] (max relative error 7.5e-5, below half an fp16 ulp, which is
+// all the result needs: it becomes a 16-bit P entry). Finally j is added
+// to the exponent field.
 constexpr float kExp2Lo = -126.f;
 constexpr float kExp2Span = 253.f;
 __device__ __forceinline__ float2 exp2_poly2_affine(float2 xs) {
@@ -511,11 +473,6 @@ struct F16 {
   __device__ static __forceinline__ float2 unpack2(uint32_t w) {
     return __half22float2(*reinterpret_cast<const __half2 *>(&w));
   }
-  // w * c in the packed type (two lanes)
-  __device__ static __forceinline__ uint32_t scale2(uint32_t w, float c) {
-    __half2 h = __hmul2(*reinterpret_cast<const __half2 *>(&w), __float2half2_rn(c));
-    return *reinterpret_cast<uint32_t *>(&h);
-  }
   __device__ static __forceinline__ void mma16816(float (&d)[4],
                                                   const uint32_t (&a)[4],
                                                   uint32_t b0, uint32_t b1) {
@@ -532,11 +489,6 @@ struct BF16 {
   }
   __device__ static __forceinline__ float2 unpack2(uint32_t w) {
     return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w));
-  }
-  __device__ static __forceinline__ uint32_t scale2(uint32_t w, float c) {
-    __nv_bfloat162 h = __hmul2(*reinterpret_cast<const __nv_bfloat162 *>(&w),
-                               __float2bfloat162_rn(c));
-    return *reinterpret_cast<uint32_t *>(&h);
   }
   __device__ static __forceinline__ void mma16816(float (&d)[4],
                                                   const uint32_t (&a)[4],
