@@ -75,8 +75,7 @@ __device__ __forceinline__ void finish_segment(const DecodeArgs &a, size_t g,
                                                float M, float L,
                                                const float (&A)[4], int lane) {
   if (a.x_peers) {  // sequence-sharded: send to every rank, merge all
-    decode::x_send<kD>(a, g, M, L, A, lane);
-    decode::x_finish<kD>(a, g, lane);
+    decode::x_send_deferred<kD>(a, g, M, L, A, lane);
     return;
   }
   if (a.partial_out) {
@@ -100,13 +99,18 @@ __device__ __forceinline__ void finish_segment(const DecodeArgs &a, size_t g,
 __device__ void merger(const DecodeArgs &a, uint8_t *red_base,
                        uint64_t *red_full, uint64_t *red_empty) {
   const int lane = threadIdx.x & 31;
+  if (lane == 0) decode::x_deferred().n = 0;
+  __syncwarp();
   for (int piece = 0;; ++piece) {
     const int buf = piece & 1;
     if (!mbar_wait(&red_full[buf], (piece >> 1) & 1)) return;
     const float *red = reinterpret_cast<const float *>(red_base + buf * kRedBufBytes);
     const int *hdr_in = reinterpret_cast<const int *>(red + kConsumerWarps * kPF);
     const int flags = hdr_in[1];
-    if (flags & kDone) return;
+    if (flags & kDone) {
+      if (a.x_peers) decode::x_finish_deferred<kD>(a, lane);
+      return;
+    }
     const size_t g = static_cast<size_t>(hdr_in[0]);
     const int c0 = hdr_in[2];
     const int c1 = hdr_in[3];

@@ -274,6 +274,51 @@ __device__ void x_finish(const DecodeArgs &a, size_t g, int lane) {
     a.out[g * D + 32 * i + lane] = store_elem(acc[i] * inv, a.dtype);
 }
 
+// Segments this CTA has sent to every rank and still has to merge: the
+// merger warp sends a finished segment at once but waits for the other
+// ranks' partials of it only after the CTA's last piece, so a slower peer
+// does not hold up this CTA's own stream (the hand-off buffers stay free).
+constexpr int kMaxDeferred = 64;
+struct XDeferred {
+  int n;
+  int g[kMaxDeferred];
+};
+__device__ __forceinline__ XDeferred &x_deferred() {
+  __shared__ XDeferred d;
+  return d;
+}
+
+// Whole warp: x_send, then either defer the merge (room in the list) or
+// do it now.
+template <int D>
+__device__ __forceinline__ void x_send_deferred(const DecodeArgs &a, size_t g,
+                                                float M, float L,
+                                                const float (&A)[D / 32],
+                                                int lane) {
+  x_send<D>(a, g, M, L, A, lane);
+  XDeferred &d = x_deferred();
+  const int n = d.n;
+  if (n < kMaxDeferred) {
+    __syncwarp();
+    if (lane == 0) {
+      d.g[n] = static_cast<int>(g);
+      d.n = n + 1;
+    }
+    __syncwarp();
+  } else {
+    x_finish<D>(a, g, lane);
+  }
+}
+
+// Whole warp: the deferred merges, in the order the segments were sent.
+template <int D>
+__device__ __forceinline__ void x_finish_deferred(const DecodeArgs &a,
+                                                  int lane) {
+  XDeferred &d = x_deferred();
+  __syncwarp();
+  for (int i = 0; i < d.n; ++i) x_finish<D>(a, static_cast<size_t>(d.g[i]), lane);
+}
+
 // Writes a finished (m, l, acc) for segment g: the fp16 output, or the
 // partial in partial mode, or (sharded) sends it to every rank and writes
 // the merge of all ranks. Lane l holds dims l and l + 32.
@@ -282,8 +327,7 @@ __device__ __forceinline__ void finish_segment(const DecodeArgs &a, size_t g,
                                                float A1, int lane) {
   if (a.x_peers) {
     const float A[2] = {A0, A1};
-    x_send<kHeadDim>(a, g, M, L, A, lane);
-    x_finish<kHeadDim>(a, g, lane);
+    x_send_deferred<kHeadDim>(a, g, M, L, A, lane);
     return;
   }
   if (a.partial_out) {
@@ -311,13 +355,18 @@ __device__ __forceinline__ void finish_segment(const DecodeArgs &a, size_t g,
 __device__ void merger(const DecodeArgs &a, uint8_t *red_base,
                        uint64_t *red_full, uint64_t *red_empty) {
   const int lane = threadIdx.x & 31;
+  if (lane == 0) x_deferred().n = 0;
+  __syncwarp();
   for (int piece = 0;; ++piece) {
     const int buf = piece & 1;
     if (!mbar_wait(&red_full[buf], (piece >> 1) & 1)) return;
     const float *red = reinterpret_cast<const float *>(red_base + buf * kRedBufBytes);
     const int *hdr_in = reinterpret_cast<const int *>(red + kConsumerWarps * kPartialFloats);
     const int flags = hdr_in[1];
-    if (flags & kDone) return;
+    if (flags & kDone) {
+      if (a.x_peers) x_finish_deferred<kHeadDim>(a, lane);
+      return;
+    }
     const size_t g = static_cast<size_t>(hdr_in[0]);
     const int c0 = hdr_in[2];
     const int c1 = hdr_in[3];
