@@ -200,6 +200,25 @@ def test_decode_ragged_batch(seq_lens):
     assert max_abs_diff(out, ref) <= TOL
 
 
+@pytest.mark.parametrize("seq_lens,heads", [
+    ([1, 128, 129, 255, 256], 12),   # every segment fits two stages: one CTA each
+    ([256] * 40, 16),                # more whole segments than the grid has CTAs
+    ([0, 256, 3, 200], 2),           # an empty sequence among short ones
+    ([256, 257, 100], 12),           # one sequence just past the whole-segment limit
+])
+def test_decode_short_sequences_whole_segments(seq_lens, heads):
+    """Sequences of at most two 128-row stages are streamed whole by one
+    CTA (no cross-CTA merge); mixed with longer ones the usual split runs."""
+    batch, cache = len(seq_lens), 257
+    q = rand(batch, heads, 1, HEAD_DIM, seed=11)
+    k_cache = rand(batch, heads, cache, HEAD_DIM)
+    v_cache = rand(batch, heads, cache, HEAD_DIM)
+    lens = torch.tensor(seq_lens, dtype=torch.int32, device="cuda")
+    out = flashattn_cuda.decode(q, k_cache, v_cache, lens, SCALE)
+    ref = decode_reference(q, k_cache, v_cache, lens)
+    assert max_abs_diff(out, ref) <= TOL
+
+
 @pytest.mark.parametrize("cache", [1, 63, 512, 513, 2048])
 def test_decode_cache_lengths(cache):
     batch, heads = 3, 12
