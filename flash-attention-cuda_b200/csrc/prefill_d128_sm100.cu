@@ -216,9 +216,10 @@ __global__ void __launch_bounds__(Form<kSolo>::kThreads, Form<kSolo>::kCtasPerSm
   const int r = static_cast<int>(blockIdx.x) % (hb * n_units);
   const int h0 = blk * hb;
   const int h_here = min(hb, BH - h0);
-  const int unit = n_units - 1 - r / h_here;  // heaviest first
+  const int h_div = h_here > 0 ? h_here : 1;
+  const int unit = n_units - 1 - r / h_div;  // heaviest first
   const int pair = unit;
-  const int bh = h0 + r % h_here;
+  const int bh = h0 + r % h_div;
   if (h_here <= 0 || bh >= BH) return;  // only if the grid outran the work
   const int kv_bh = (bh / H) * (H / group) + (bh % H) / group;
   TileInfo t0 = tile_info(pair, 0, N, causal, zigzag);

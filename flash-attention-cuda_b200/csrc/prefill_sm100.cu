@@ -78,13 +78,8 @@ constexpr int kBarDrain = kBarODone + kTilesPerCta;
 constexpr int kNumBars = kBarDrain + 1;
 constexpr uint32_t kTmemS = 0;    // + 128 * tile
 
-// Two CTA forms share the kernel. The paired form (kSolo false) holds two
-// query tiles in one CTA per SM (384 threads, 512 tensor-memory columns,
-// a 3-slot K/V ring). The solo form holds one query tile per CTA and fits
-// two CTAs on an SM: 256 threads (softmax warps 0-3, producer 4, MMA 5,
-// warps 6-7 donate registers), 256 tensor-memory columns and a 3-slot ring
-// in 112 KiB of shared memory, so one CTA's start-up (first tiles from HBM)
-// and epilogue overlap the other CTA's key steps.
+// Threads, roles, shared-memory offsets and tensor-memory columns of the
+// paired (kSolo false) and solo forms described at the top of this file.
 template <bool kSolo>
 struct Form {
   static constexpr int kThreads = kSolo ? 256 : 384;
@@ -256,9 +251,10 @@ __global__ void __launch_bounds__(Form<kSolo>::kThreads, Form<kSolo>::kCtasPerSm
   const int r = static_cast<int>(blockIdx.x) % (hb * n_units);
   const int h0 = blk * hb;
   const int h_here = min(hb, BH - h0);
-  const int unit = n_units - 1 - r / h_here;  // heaviest first
+  const int h_div = h_here > 0 ? h_here : 1;
+  const int unit = n_units - 1 - r / h_div;  // heaviest first
   const int pair = unit;
-  const int bh = h0 + r % h_here;
+  const int bh = h0 + r % h_div;
   if (h_here <= 0 || bh >= BH) return;  // only if the grid outran the work
   // K/V head of the query head: `group` query heads share one K/V head
   // (group == 1 without grouped-query attention).
