@@ -86,6 +86,21 @@ def read_profile_traffic(name):
     return None
 
 
+def read_profile_clock(name):
+    """SM clock (GHz) inside the kernel's ncu capture, from a committed
+    summary line `sm_clock_ghz_in_kernel: <float>` (None if absent): the
+    clock the power-capped kernel actually ran at, which the NVML samples
+    between launches do not show."""
+    path = os.path.join(PROFILES, name + ".md")
+    try:
+        for line in open(path):
+            if line.strip().startswith("sm_clock_ghz_in_kernel:"):
+                return float(line.split(":", 1)[1].strip())
+    except Exception:
+        pass
+    return None
+
+
 def shard_range(total, world, rank):
     sys.path.insert(0, PKG_DIR)
     from flashattn_cuda.dist import shard_units
@@ -621,7 +636,9 @@ def run_ours(args, rank, world, local_rank):
                      "frac": round(achieved / peak, 4),
                      "peak_source": f"{peaks_src} bf16 cuBLAS burst",
                      "frac_of_nominal_2250": round(achieved / 2250.0, 4),
-                     "traffic": read_profile_traffic("prefill_kernel_c3")},
+                     "traffic": read_profile_traffic("prefill_kernel_c3"),
+                     "sm_clock_ghz_in_kernel_ncu": read_profile_clock(
+                         "prefill_kernel_c3")},
         "gpu_launches": launches,
         "clocks": clocks,
         "secondary": secondary,
