@@ -79,12 +79,17 @@ int ensure_device(int *device_out) {
                               decode_gqa_kernel_ptr(64, dt),
                               decode_gqa_kernel_ptr(128, dt),
                               prefill_solo_kernel_ptr(dt),
-                              prefill_d128_solo_kernel_ptr(dt)};
+                              prefill_d128_solo_kernel_ptr(dt),
+                              prefill_split_kernel_ptr(dt)};
     const int bytes[] = {prefill_smem_bytes(), decode_smem_bytes(),
                          decode_d128_smem_bytes(), prefill_d128_smem_bytes(),
                          decode_gqa_smem_bytes(64), decode_gqa_smem_bytes(128),
-                         prefill_solo_smem_bytes(), prefill_d128_solo_smem_bytes()};
-    for (int i = 0; i < 8; ++i) {
+                         prefill_solo_smem_bytes(), prefill_d128_solo_smem_bytes(),
+                         prefill_split_smem_bytes()};
+    static_assert(sizeof(big_smem) / sizeof(big_smem[0]) ==
+                      sizeof(bytes) / sizeof(bytes[0]),
+                  "one shared-memory size per kernel");
+    for (size_t i = 0; i < sizeof(bytes) / sizeof(bytes[0]); ++i) {
       if (cudaFuncSetAttribute(big_smem[i],
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                bytes[i]) != cudaSuccess ||
@@ -310,7 +315,7 @@ int run_decode(const void *q, const void *k_cache, const void *v_cache,
 // maps and the launch.
 int run_prefill(const void *q, const void *k, const void *v, void *o, int B,
                 int H, int H_kv, int N, int head_dim, int dtype, int causal,
-                float scale, void *stream) {
+                float scale, void *stream, long long plan_bh = 0) {
   if (head_dim != FA_HEAD_DIM && head_dim != 128) return FA_EINVAL;
   if (B <= 0 || H <= 0 || N <= 0 || !isfinite(scale)) return FA_EINVAL;
   if (H_kv <= 0 || H % H_kv != 0) return FA_EINVAL;
@@ -334,7 +339,7 @@ int run_prefill(const void *q, const void *k, const void *v, void *o, int B,
           ? launch_prefill_kernel(tq, tk, tv, static_cast<__half *>(o), B, H,
                                   N, causal != 0, scale, H_kv,
                                   g_devices[dev].sms, dtype,
-                                  static_cast<cudaStream_t>(stream))
+                                  static_cast<cudaStream_t>(stream), plan_bh)
           : launch_prefill_d128_kernel(tq, tk, tv, static_cast<__half *>(o), B,
                                        H, N, causal != 0, scale, H_kv,
                                        g_devices[dev].sms, dtype,
@@ -343,6 +348,15 @@ int run_prefill(const void *q, const void *k, const void *v, void *o, int B,
 }
 
 }  // namespace
+
+int prefill_chunk_ex(const void *q, const void *k, const void *v, void *o,
+                     int B, int H, int H_kv, int N, int head_dim, int dtype,
+                     int causal, float scale, void *stream, long long plan_bh) {
+  if (dtype != FA_DTYPE_F16 && dtype != FA_DTYPE_BF16) return FA_EINVAL;
+  return run_prefill(q, k, v, o, B, H, H_kv, N, head_dim, dtype, causal,
+                     scale, stream, plan_bh);
+}
+
 }  // namespace fa
 
 using namespace fa;
@@ -771,6 +785,8 @@ int fa_occupancy(fa_occupancy_entry *out, int max_entries, int *count) {
        prefill_smem_bytes()},
       {"prefill_solo_kernel", prefill_solo_kernel_ptr(),
        prefill_solo_threads(), prefill_solo_smem_bytes()},
+      {"prefill_split_kernel", prefill_split_kernel_ptr(), prefill_threads(),
+       prefill_split_smem_bytes()},
       {"decode_kernel", decode_kernel_ptr(), decode_threads(),
        decode_smem_bytes()},
       {"merge_kernel", merge_kernel_ptr(), merge_threads(), 0},

@@ -16,6 +16,8 @@ int prefill_threads();
 const void *prefill_solo_kernel_ptr(int dtype = FA_DTYPE_F16);
 int prefill_solo_smem_bytes();
 int prefill_solo_threads();
+const void *prefill_split_kernel_ptr(int dtype = FA_DTYPE_F16);
+int prefill_split_smem_bytes();
 const void *prefill_d128_solo_kernel_ptr(int dtype = FA_DTYPE_F16);
 int prefill_d128_solo_smem_bytes();
 int prefill_smem_bytes();
@@ -24,7 +26,13 @@ cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
                                   const CUtensorMap &tm_v, __half *out, int B,
                                   int H, int N, bool causal, float scale,
                                   int H_kv, int sms, int dtype,
-                                  cudaStream_t stream);
+                                  cudaStream_t stream, long long plan_bh = 0);
+// fa_prefill_ex for one chunk of a larger problem of plan_bh (batch x head)
+// pairs: the CTA form is chosen for the whole problem, so a head's output
+// does not depend on how the problem was cut into launches (capi.cu).
+int prefill_chunk_ex(const void *q, const void *k, const void *v, void *o,
+                     int B, int H, int H_kv, int N, int head_dim, int dtype,
+                     int causal, float scale, void *stream, long long plan_bh);
 
 // ---- prefill, head_dim 128 (prefill_d128_sm100.cu) -------------------------
 const void *prefill_d128_kernel_ptr(int dtype = FA_DTYPE_F16);

@@ -23,6 +23,7 @@
 #include <mutex>
 
 #include "fa_b200.h"
+#include "fa_kernels.h"
 
 namespace fa {
 namespace {
@@ -226,8 +227,9 @@ int fa_prefill_host_ex(const void *q, const void *k, const void *v, void *o,
       rc = FA_ECUDA;
       break;
     }
-    rc = fa_prefill_ex(sq, sk, sv, so, nu, p.unit_heads, 1, N, head_dim,
-                       dtype, causal, scale, stream);
+    rc = prefill_chunk_ex(sq, sk, sv, so, nu, p.unit_heads, 1, N, head_dim,
+                          dtype, causal, scale, stream,
+                          static_cast<long long>(B) * H);
     if (rc != FA_OK) break;
     if (cudaEventRecord(st->computed[r], cs) != cudaSuccess ||
         cudaStreamWaitEvent(st->copy_out, st->computed[r], 0) != cudaSuccess ||

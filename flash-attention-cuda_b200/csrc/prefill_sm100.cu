@@ -38,6 +38,9 @@
 #include <math.h>
 #include <stdint.h>
 
+#include <stdlib.h>
+#include <string.h>
+
 #include <algorithm>
 #include <functional>
 #include <map>
@@ -54,6 +57,9 @@ constexpr int kTilesPerCta = 2;
 // K/V ring slots in shared memory: two key tiles stream ahead of the one in
 // use.
 constexpr int kRingSlots = 3;
+// Ring slots of the key-split form, which consumes two key tiles per round.
+constexpr int kSplitRingSlots = 5;
+constexpr int kMaxRingSlots = kSplitRingSlots;
 // Longest sequence, in query tiles, that runs in the solo form (measured:
 // N 4096 solo 743 vs paired 724 TFLOP/s, N 8192 798 vs 809, N 16384 738 vs
 // 746).
@@ -69,8 +75,8 @@ constexpr uint32_t kQOff = 0;
 // barrier slots
 constexpr int kBarQFull = 0;
 constexpr int kBarKFull = kBarQFull + 1;          // + stage: K and V tile
-constexpr int kBarKVEmpty = kBarKFull + kRingSlots;  // + stage
-constexpr int kBarSFull = kBarKVEmpty + kRingSlots;  // + tile
+constexpr int kBarKVEmpty = kBarKFull + kMaxRingSlots;  // + stage
+constexpr int kBarSFull = kBarKVEmpty + kMaxRingSlots;  // + tile
 constexpr int kBarSFree = kBarSFull + kTilesPerCta;
 constexpr int kBarPFull = kBarSFree + kTilesPerCta;
 constexpr int kBarODone = kBarPFull + kTilesPerCta;
@@ -79,27 +85,34 @@ constexpr int kNumBars = kBarDrain + 1;
 constexpr uint32_t kTmemS = 0;    // + 128 * tile
 
 // Threads, roles, shared-memory offsets and tensor-memory columns of the
-// paired (kSolo false) and solo forms described at the top of this file.
-template <bool kSolo>
+// paired (kSolo false), solo and key-split forms described at the top of
+// this file. The key-split form has the paired form's warps and tensor
+// memory but one Q tile, a deeper ring and the merge rows (m, l of the
+// second warpgroup) in shared memory.
+template <bool kSolo, bool kSplit = false>
 struct Form {
+  static_assert(!(kSolo && kSplit), "one form at a time");
   static constexpr int kThreads = kSolo ? 256 : 384;
   static constexpr int kCtasPerSm = kSolo ? 2 : 1;
   static constexpr int kCtrlWarp0 = kSolo ? 4 : 8;  // first control warp
   static constexpr int kProducerWarp = kCtrlWarp0;
   static constexpr int kMmaWarp = kCtrlWarp0 + 1;
   static constexpr int kSoftmaxRegs = kSolo ? 232 : 240;
-  static constexpr int kQTiles = kSolo ? 1 : 2;
-  static constexpr int kSlots = kRingSlots;
+  static constexpr int kQTiles = (kSolo || kSplit) ? 1 : 2;
+  static constexpr int kSlots = kSplit ? kSplitRingSlots : kRingSlots;
   static constexpr uint32_t kKOff = kQOff + kQTiles * kTileBytes;
   static constexpr uint32_t kVOff = kKOff + kSlots * kTileBytes;
   static constexpr uint32_t kBarOff = kVOff + kSlots * kTileBytes;
   static constexpr uint32_t kTmemSlotOff = kBarOff + kNumBars * 8;
   static constexpr uint32_t kAbortOff = kTmemSlotOff + 4;
-  static constexpr uint32_t kSmemBytes = kAbortOff + 4 + 8;
+  static constexpr uint32_t kMergeOff = kAbortOff + 12;  // 16-byte aligned
+  static constexpr uint32_t kSmemBytes = kMergeOff + (kSplit ? 2 * 128 * 4 : 0);
   static constexpr uint32_t kTmemCols = kSolo ? 256 : 512;
   static constexpr uint32_t kTmemO = kSolo ? 128 : 256;  // + 64 * tile
   static constexpr uint32_t kTmemP = kSolo ? 192 : 384;  // + 64 * tile
-  static_assert(128 * kCtrlRegs + 128 * kQTiles * kSoftmaxRegs <=
+  static_assert(kMergeOff % 16 == 0, "merge rows misaligned");
+  static constexpr int kSoftmaxGroups = kSolo ? 1 : 2;
+  static_assert(128 * kCtrlRegs + 128 * kSoftmaxGroups * kSoftmaxRegs <=
                     kThreads * (65536 / (kThreads * kCtasPerSm)),
                 "register split exceeds the launch allocation");
   static_assert(kCtasPerSm * (kSmemBytes + 1024) <= 228 * 1024,
@@ -218,16 +231,17 @@ __device__ __forceinline__ TileInfo tile_info(int pair, int t, int N,
   return ti;
 }
 
-template <typename Dt, bool kSolo = false>
-__global__ void __launch_bounds__(Form<kSolo>::kThreads, Form<kSolo>::kCtasPerSm)
+template <typename Dt, bool kSolo = false, bool kSplit = false>
+__global__ void __launch_bounds__(Form<kSolo, kSplit>::kThreads,
+                                  Form<kSolo, kSplit>::kCtasPerSm)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
                    const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v,
                    __half *__restrict__ out, int N, int BH, int causal,
                    float scale_log2, int H, int group, int head_block) {
-  using F = Form<kSolo>;
+  using F = Form<kSolo, kSplit>;
   extern __shared__ __align__(1024) uint8_t smem[];
-  constexpr int kStages = kRingSlots;
+  constexpr int kStages = F::kSlots;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
@@ -245,7 +259,7 @@ __global__ void __launch_bounds__(Form<kSolo>::kThreads, Form<kSolo>::kCtasPerSm
   // so a head's tiles run close together and its K/V is read once.
   const int n_qt = (N + kBlockM - 1) / kBlockM;
   const int n_pairs = (n_qt + 1) / 2;
-  const int n_units = kSolo ? n_qt : n_pairs;  // per head
+  const int n_units = (kSolo || kSplit) ? n_qt : n_pairs;  // per head
   const int hb = head_block > 0 ? head_block : BH;
   const int blk = static_cast<int>(blockIdx.x) / (hb * n_units);
   const int r = static_cast<int>(blockIdx.x) % (hb * n_units);
@@ -260,7 +274,17 @@ __global__ void __launch_bounds__(Form<kSolo>::kThreads, Form<kSolo>::kCtasPerSm
   // (group == 1 without grouped-query attention).
   const int kv_bh = (bh / H) * (H / group) + (bh % H) / group;
   TileInfo t0, t1;
-  if (kSolo) {
+  // Key-split form: one query tile whose key tiles alternate between the two
+  // softmax warpgroups (even key tiles to t0, odd to t1); TileInfo.n_kv then
+  // counts rounds of that warpgroup.
+  int n_keys = 0;
+  if (kSplit) {
+    t0.qt = unit;
+    t1.qt = unit;
+    n_keys = causal ? unit + 1 : n_qt;
+    t0.n_kv = (n_keys + 1) / 2;
+    t1.n_kv = n_keys / 2;
+  } else if (kSolo) {
     t0.qt = unit;
     t0.n_kv = causal ? t0.qt + 1 : n_qt;
     t1.qt = t0.qt;
@@ -277,7 +301,7 @@ __global__ void __launch_bounds__(Form<kSolo>::kThreads, Form<kSolo>::kCtasPerSm
       reinterpret_cast<volatile uint32_t *>(smem + F::kAbortOff);
 
   // Key tile j goes to ring stage j % kStages.
-  const int n_pos = n_kv;
+  const int n_pos = kSplit ? n_keys : n_kv;
   auto load_pos = [&](int p) {
     const int s = p % kStages;
     mbar_arrive_expect_tx(&bars[kBarKFull + s], 2 * kTileBytes);
@@ -309,7 +333,7 @@ __global__ void __launch_bounds__(Form<kSolo>::kThreads, Form<kSolo>::kCtasPerSm
     prefetch_tensormap(&tm_q);
     prefetch_tensormap(&tm_k);
     prefetch_tensormap(&tm_v);
-    const bool two = t1.n_kv > 0;
+    const bool two = !kSplit && t1.n_kv > 0;
     mbar_arrive_expect_tx(&bars[kBarQFull], (two ? 2 : 1) * kTileBytes);
     tma_load_3d(smem + kQOff, &tm_q, &bars[kBarQFull], 0, t0.qt * kBlockM, bh);
     if (two)
@@ -373,18 +397,25 @@ __global__ void __launch_bounds__(Form<kSolo>::kThreads, Form<kSolo>::kCtasPerSm
     const int n0 = t0.n_kv;
     const int n1 = t1.n_kv;
     const uint64_t desc0 = sw128_desc(sbase);
+    // Q tile of warpgroup t and the key position (ring order) of its round j.
+    auto q_off = [](int t) -> uint32_t {
+      return kSplit ? kQOff : kQOff + t * kTileBytes;
+    };
+    auto kpos = [](int j, int t) { return kSplit ? 2 * j + t : j; };
     bool ok = mbar_wait(&bars[kBarQFull], 0) &&
-              mbar_wait(&bars[kBarKFull + 0], 0);
+              mbar_wait(&bars[kBarKFull + 0], 0) &&
+              (!kSplit || n1 == 0 || mbar_wait(&bars[kBarKFull + 1], 0));
     if (ok) {
       tc_fence_after();
       if (leader) {
         if (n0 > 0) {
-          issue_s_tile<Dt>(tmem + kTmemS, desc0 + (kQOff >> 4), desc0 + (F::kKOff >> 4));
+          issue_s_tile<Dt>(tmem + kTmemS, desc0 + (q_off(0) >> 4),
+                           desc0 + (F::kKOff >> 4));
           mma_commit(&bars[kBarSFull + 0]);
         }
         if (n1 > 0) {
-          issue_s_tile<Dt>(tmem + kTmemS + 128, desc0 + ((kQOff + kTileBytes) >> 4),
-                       desc0 + (F::kKOff >> 4));
+          issue_s_tile<Dt>(tmem + kTmemS + 128, desc0 + (q_off(1) >> 4),
+                           desc0 + ((F::kKOff + kpos(0, 1) * kTileBytes) >> 4));
           mma_commit(&bars[kBarSFull + 1]);
         }
       }
@@ -399,13 +430,14 @@ __global__ void __launch_bounds__(Form<kSolo>::kThreads, Form<kSolo>::kCtasPerSm
       for (int t = 0; t < kTilesPerCta; ++t) {
         const int nt = t ? n1 : n0;
         if (!ok || j >= nt) continue;
-        const int s = j % kStages;                  // K_j, V_j
-        const int p1 = j + 1;
+        const int s = kpos(j, t) % kStages;         // K_j, V_j
+        const int p1 = kpos(j + 1, t);
         const int s1 = p1 % kStages;                // K_{j+1}
         if (j + 1 < nt) {
           // K/V tile j+1 is waited on once per round (by the first tile
           // that uses it); V_j was waited on with K_j the round before.
-          const bool need_kv = (t == 0) || (n0 <= j + 1);
+          // In the key-split form each key tile has one user.
+          const bool need_kv = kSplit || (t == 0) || (n0 <= j + 1);
           if ((need_kv &&
                !mbar_wait(&bars[kBarKFull + s1], (p1 / kStages) & 1)) ||
               !mbar_wait(&bars[kBarSFree + t], j & 1)) {
@@ -415,9 +447,8 @@ __global__ void __launch_bounds__(Form<kSolo>::kThreads, Form<kSolo>::kCtasPerSm
           FA_TRACE_EVENT(2048 + j * 16 + t * 8 + 3);
           tc_fence_after();
           if (leader) {
-            issue_s_tile<Dt>(tmem + kTmemS + 128 * t,
-                         desc0 + ((kQOff + t * kTileBytes) >> 4),
-                         desc0 + ((F::kKOff + s1 * kTileBytes) >> 4));
+            issue_s_tile<Dt>(tmem + kTmemS + 128 * t, desc0 + (q_off(t) >> 4),
+                             desc0 + ((F::kKOff + s1 * kTileBytes) >> 4));
             mma_commit(&bars[kBarSFull + t]);
           }
           __syncwarp();
@@ -433,13 +464,16 @@ __global__ void __launch_bounds__(Form<kSolo>::kThreads, Form<kSolo>::kCtasPerSm
           issue_pv_tile<Dt>(tmem + F::kTmemO + 64 * t, tmem + F::kTmemP + 64 * t,
                         desc0 + ((F::kVOff + s * kTileBytes) >> 4), j > 0);
           mma_commit(&bars[kBarODone + t]);
+          // key-split form: this key tile's ring stage is free once its PV
+          // retires
+          if (kSplit) mma_commit(&bars[kBarKVEmpty + s]);
         }
         __syncwarp();
         FA_TRACE_EVENT(2048 + j * 16 + t * 8 + 2);
       }
       if (!ok) break;
       // release round j's ring stage
-      if (leader) {
+      if (!kSplit && leader) {
         mma_commit(&bars[kBarKVEmpty + j % kStages]);
       }
       __syncwarp();
@@ -500,8 +534,9 @@ __global__ void __launch_bounds__(Form<kSolo>::kThreads, Form<kSolo>::kCtasPerSm
         sl = 1.f;
       }
       uint32_t pk[2][32];  // P row as fp16 pairs, TMEM columns [0,32), [32,64)
-      const int kbase = j * kBlockN;
-      const bool diag = causal && (j == ti.qt);
+      const int kt = kSplit ? 2 * j + t : j;  // key tile of this round
+      const int kbase = kt * kBlockN;
+      const bool diag = causal && (kt == ti.qt);
       if (diag || kbase + kBlockN > N) {
         int lim = N - kbase;
         if (diag) lim = min(lim, row + 1);
@@ -552,33 +587,84 @@ __global__ void __launch_bounds__(Form<kSolo>::kThreads, Form<kSolo>::kCtasPerSm
       if (row == 0) FA_TRACE_EVENT(t * 1024 + j * 8 + 4);
     }
 
-    if (ti.n_kv > 0) {
+    // Row q_row of the output: O (fp32 words, 64 columns) times w.
+    auto store_row = [&](const uint32_t (&o)[2][32], float w) {
+      const int q_row = ti.qt * kBlockM + row;
+      if (q_row >= N) return;
+      uint4 *dst = reinterpret_cast<uint4 *>(
+          out + (static_cast<size_t>(bh) * N + q_row) * kHeadDim);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint4 v;
+        const uint32_t *src = &o[c >> 2][(c & 3) * 8];
+        v.x = Dt::pack2(__uint_as_float(src[0]) * w, __uint_as_float(src[1]) * w);
+        v.y = Dt::pack2(__uint_as_float(src[2]) * w, __uint_as_float(src[3]) * w);
+        v.z = Dt::pack2(__uint_as_float(src[4]) * w, __uint_as_float(src[5]) * w);
+        v.w = Dt::pack2(__uint_as_float(src[6]) * w, __uint_as_float(src[7]) * w);
+        dst[c] = v;
+      }
+    };
+
+    if (kSplit) {
+      // Merge of the two warpgroups' partial rows (same query row, disjoint
+      // key tiles). Warpgroup 1 leaves its (m, l) in shared memory and
+      // arrives; warpgroup 0 waits, reads them and warpgroup 1's O from
+      // tensor memory (warps w and w + 4 reach the same lanes), rescales
+      // both to the larger max and writes the row. Both warpgroups always
+      // reach the barrier, also after giving up.
+      float *merge_m = reinterpret_cast<float *>(smem + F::kMergeOff);
+      float *merge_l = merge_m + 128;
+      const bool done =
+          ok && (ti.n_kv == 0 || mbar_wait(o_done, (ti.n_kv - 1) & 1));
+      if (!done) *abort_flag = 1;
+      if (t == 1) {
+        merge_m[row] = ti.n_kv > 0 ? m_use : -INFINITY;
+        merge_l[row] = ti.n_kv > 0 ? l_sum : 0.f;
+        tc_fence_before();
+        named_bar_arrive(1, 2 * kSoftmaxThreads);
+      } else {
+        named_bar_sync(1, 2 * kSoftmaxThreads);
+        tc_fence_after();
+        if (!*abort_flag) {
+          const float m1 = merge_m[row];
+          const float l1 = merge_l[row];
+          const float m = fmaxf(m_use, m1);
+          const float c0 = fast_exp2(m_use - m);
+          const float c1 = l1 > 0.f ? fast_exp2(m1 - m) : 0.f;
+          const float l = l_sum * c0 + l1 * c1;
+          const float inv_l = l > 0.f ? 1.f / l : 0.f;
+          uint32_t o[2][32];
+          tmem_ld32(tO, o[0]);
+          tmem_ld32(tO + 32, o[1]);
+          tmem_wait_ld();
+          if (t1.n_kv > 0) {  // CTA-uniform: warpgroup 1 had key tiles
+            const uint32_t tO1 = tO + 64;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              uint32_t o1[32];
+              tmem_ld32(tO1 + 32 * h, o1);
+              tmem_wait_ld();
+#pragma unroll
+              for (int c = 0; c < 32; ++c) {
+                const float a = __uint_as_float(o[h][c]) * c0;
+                const float b = l1 > 0.f ? __uint_as_float(o1[c]) * c1 : 0.f;
+                o[h][c] = __float_as_uint(a + b);
+              }
+            }
+            store_row(o, inv_l);
+          } else {
+            store_row(o, c0 * inv_l);
+          }
+        }
+      }
+    } else if (ti.n_kv > 0) {
       if (ok && mbar_wait(o_done, (ti.n_kv - 1) & 1)) {
         tc_fence_after();
         uint32_t o[2][32];
         tmem_ld32(tO, o[0]);
         tmem_ld32(tO + 32, o[1]);
         tmem_wait_ld();
-        const int q_row = ti.qt * kBlockM + row;
-        if (q_row < N) {
-          const float inv_l = (l_sum > 0.f) ? 1.f / l_sum : 0.f;
-          uint4 *dst = reinterpret_cast<uint4 *>(
-              out + (static_cast<size_t>(bh) * N + q_row) * kHeadDim);
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            uint4 v;
-            const uint32_t *src = &o[c >> 2][(c & 3) * 8];
-            v.x = Dt::pack2(__uint_as_float(src[0]) * inv_l,
-                             __uint_as_float(src[1]) * inv_l);
-            v.y = Dt::pack2(__uint_as_float(src[2]) * inv_l,
-                             __uint_as_float(src[3]) * inv_l);
-            v.z = Dt::pack2(__uint_as_float(src[4]) * inv_l,
-                             __uint_as_float(src[5]) * inv_l);
-            v.w = Dt::pack2(__uint_as_float(src[6]) * inv_l,
-                             __uint_as_float(src[7]) * inv_l);
-            dst[c] = v;
-          }
-        }
+        store_row(o, (l_sum > 0.f) ? 1.f / l_sum : 0.f);
       } else {
         *abort_flag = 1;
       }
@@ -605,6 +691,15 @@ int prefill_solo_smem_bytes() {
   return static_cast<int>(prefill::Form<true>::kSmemBytes);
 }
 int prefill_solo_threads() { return prefill::Form<true>::kThreads; }
+const void *prefill_split_kernel_ptr(int dtype) {
+  using prefill::prefill_kernel;
+  return dtype == FA_DTYPE_BF16
+             ? reinterpret_cast<const void *>(prefill_kernel<BF16, false, true>)
+             : reinterpret_cast<const void *>(prefill_kernel<F16, false, true>);
+}
+int prefill_split_smem_bytes() {
+  return static_cast<int>(prefill::Form<false, true>::kSmemBytes);
+}
 const void *prefill_kernel_ptr(int dtype) {
   return dtype == FA_DTYPE_BF16
              ? reinterpret_cast<const void *>(prefill::prefill_kernel<BF16>)
@@ -621,7 +716,7 @@ cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
                                   const CUtensorMap &tm_v, __half *out, int B,
                                   int H, int N, bool causal, float scale,
                                   int H_kv, int sms, int dtype,
-                                  cudaStream_t stream) {
+                                  cudaStream_t stream, long long plan_bh) {
   static_assert(prefill::kBlockM == prefill::kBlockN,
                 "causal tile skipping assumes square tiles");
   const int BH = B * H;
@@ -636,8 +731,34 @@ cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
   // Solo form (one query tile per CTA, two CTAs per SM) unless the paired
   // grid fits one wave, where zig-zag pairs give every SM equal work, or
   // the sequence is long enough that the pairs' shared K/V loads win.
-  const bool solo = n_qt <= prefill::kSoloMaxTiles &&
-                    (n_qt == 1 || grid > static_cast<unsigned>(sms));
+  bool solo = n_qt <= prefill::kSoloMaxTiles &&
+              (n_qt == 1 || grid > static_cast<unsigned>(sms));
+  // Key-split form (one query tile per CTA, its key tiles alternating
+  // between two softmax warpgroups) for causal grids of at most two query
+  // tiles per SM: there the longest query tile's chain of key steps, not
+  // the total work, sets the kernel time, and the split halves that chain.
+  // Its rounding differs from the other forms' (key tiles summed in another
+  // order), so the rule is evaluated on the whole problem (plan_bh) when a
+  // caller launches it in chunks.
+  const long long form_bh = plan_bh > 0 ? plan_bh : BH;
+  bool split = causal && n_qt > 1 && n_qt * form_bh <= 2LL * sms;
+  // FA_PREFILL_FORM=paired|solo|split forces a form (measurement only).
+  static const char *force = getenv("FA_PREFILL_FORM");
+  if (force && *force) {
+    split = !strcmp(force, "split");
+    solo = !strcmp(force, "solo");
+  }
+  if (split) {
+    using prefill::prefill_kernel;
+    auto kernel = dtype == FA_DTYPE_BF16 ? prefill_kernel<BF16, false, true>
+                                         : prefill_kernel<F16, false, true>;
+    kernel<<<static_cast<unsigned>(n_qt) * BH,
+             prefill::Form<false, true>::kThreads,
+             prefill::Form<false, true>::kSmemBytes, stream>>>(
+        tm_q, tm_k, tm_v, out, N, BH, causal ? 1 : 0, scale_log2, H,
+        H / H_kv, 0);
+    return cudaGetLastError();
+  }
   // Blocks of heads whose K/V (both tensors, all N rows) fit in about
   // kHeadBlockL2Bytes of L2, equal in size, for multi-wave grids.
   int head_block = 0;

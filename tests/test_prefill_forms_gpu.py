@@ -1,7 +1,10 @@
-"""Prefill in both CTA forms against fp32 attention. The solo form (one
-query tile per CTA, two CTAs per SM) runs every sequence of up to 48 query
-tiles whose paired grid exceeds one wave of SMs; the paired form (two tiles
-of one head per CTA) runs the rest: one-wave grids (zig-zag pairs) and long
+"""Prefill in all three CTA forms against fp32 attention. The key-split
+form (one query tile per CTA, its key tiles alternating between two
+softmax warpgroups whose partial rows merge at the end) runs causal grids
+of at most two query tiles per SM; the solo form (one query tile per CTA,
+two CTAs per SM) runs every other sequence of up to 48 query tiles whose
+paired grid exceeds one wave of SMs; the paired form (two tiles of one head
+per CTA) runs the rest: one-wave full grids (zig-zag pairs) and long
 sequences. Edges: short and ragged N, odd (batch, head) counts, grouped K/V
 heads, both dtypes, causal and full, and the sequence lengths on either
 side of the solo/paired switch."""
@@ -64,7 +67,11 @@ def test_short_prefill_d128_matches_fp32(dtype, tol, b, h, h_kv, n, causal):
 
 
 @pytest.mark.parametrize("b,h,n", [
-    (1, 7, 4096),    # paired grid of 112 CTAs fits one wave: zig-zag pairs
+    (1, 7, 4096),    # causal: 224 tiles, key-split; full: zig-zag pairs
+    (1, 1, 129),     # causal key-split: warpgroup 1 holds only the diagonal
+    (1, 3, 257),     # three key tiles: two on warpgroup 0, one on 1
+    (1, 9, 4096),    # causal: 288 tiles, key-split at the 2-per-SM limit
+    (1, 10, 4096),   # causal: 320 tiles, solo
     (2, 7, 4096),    # 224 pairs: solo
     (1, 2, 6144),    # 48 pairs on 148 SMs: one wave, paired
     (2, 4, 6144),    # 48 tiles, 192 pairs: solo
