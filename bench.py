@@ -284,8 +284,8 @@ def run_ours(args, rank, world, local_rank):
             "prefill_ms": [round(x / args.steps, 5) for x in timer.last_all],
             "prefill_heads": [shard_range(bh, world, r)[1] - shard_range(bh, world, r)[0]
                               for r in range(world)],
-            # one CTA per (head, query-tile pair), one CTA per SM at a time
-            "prefill_ctas_rank0": units * ((n + 255) // 256), "sms": sms}
+            "prefill_form_rank0": fa._C._prefill_form(units, n, True, sms),
+            "sms": sms}
         flops_total = prefill_flops(C3["B"], C3["H"], n, True)
         value = flops_total / (ms * 1e-3) / 1e12
         flops_rank = prefill_flops(1, units, n, True)

@@ -509,6 +509,21 @@ int64_t choose_decode_split(int64_t max_seq, int64_t batch, int64_t heads,
                                 static_cast<int>(min_blocks));
 }
 
+// CTA form of the head_dim-64 prefill for bh (batch x head) pairs of n
+// tokens on a device of `sms` SMs (host-only, no GPU needed).
+py::dict prefill_form(int64_t bh, int64_t n, bool causal, int64_t sms) {
+  int ctas = 0;
+  const int form = fa_prefill_form(bh, static_cast<int>(n), causal ? 1 : 0,
+                                   static_cast<int>(sms), &ctas);
+  TORCH_CHECK(form >= 0, "prefill_form: bh, n and sms must be positive");
+  static const char *names[] = {"paired", "solo", "key-split"};
+  py::dict d;
+  d["form"] = std::string(names[form]);
+  d["ctas"] = ctas;
+  d["ctas_per_sm"] = form == FA_PREFILL_FORM_SOLO ? 2 : 1;
+  return d;
+}
+
 // occupancy_report(): reference csrc/bindings.cpp:80-97, same row keys.
 py::list occupancy_report() {
   fa_occupancy_entry rows[8];
@@ -575,6 +590,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("scale"), py::arg("out") = py::none(),
         py::arg("non_blocking") = false);
   m.def("_prefill_host_launches", &prefill_host_launches);
+  m.def("_prefill_form", &prefill_form, py::arg("bh"), py::arg("n"),
+        py::arg("causal"), py::arg("sms"));
   m.def("decode", &decode, "Single-query attention against a KV cache",
         py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
         py::arg("seq_lens"), py::arg("scale"));

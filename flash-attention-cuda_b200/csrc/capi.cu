@@ -390,6 +390,11 @@ int fa_prefill_ex(const void *q, const void *k, const void *v, void *o, int B,
                      scale, stream);
 }
 
+int fa_prefill_form(long long bh, int n, int causal, int sms, int *ctas) {
+  if (bh <= 0 || n <= 0 || sms <= 0) return -1;
+  return prefill_form_of(bh, n, causal != 0, sms, 0, ctas);
+}
+
 size_t fa_decode_workspace_bytes(int B, int H, int S_max, int split_size,
                                  int device) {
   if (B <= 0 || H <= 0 || S_max <= 0) return 0;

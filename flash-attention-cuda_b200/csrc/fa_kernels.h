@@ -27,6 +27,11 @@ cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
                                   int H, int N, bool causal, float scale,
                                   int H_kv, int sms, int dtype,
                                   cudaStream_t stream, long long plan_bh = 0);
+// CTA form of the head_dim-64 prefill for BH (batch x head) pairs of N
+// tokens (FA_PREFILL_FORM_*); *ctas (if given) receives the grid size.
+// plan_bh > 0: the form of a chunk of a larger problem of plan_bh pairs.
+int prefill_form_of(long long BH, int N, bool causal, int sms,
+                    long long plan_bh, int *ctas);
 // fa_prefill_ex for one chunk of a larger problem of plan_bh (batch x head)
 // pairs: the CTA form is chosen for the whole problem, so a head's output
 // does not depend on how the problem was cut into launches (capi.cu).

@@ -44,6 +44,8 @@
 #include <algorithm>
 #include <functional>
 #include <map>
+#include <queue>
+#include <vector>
 
 #include "fa_kernels.h"
 #include "fa_sm100.cuh"
@@ -681,6 +683,123 @@ __global__ void __launch_bounds__(Form<kSolo, kSplit>::kThreads,
 
 }  // namespace prefill
 
+namespace prefill {
+
+// Kernel-time estimates of the causal forms, in microseconds, from list
+// scheduling of the grid in launch order (each CTA to the slot that frees
+// first) with per-CTA costs fitted to B200 measurements of the three forms
+// (20 causal shapes, N 512-32768, 2-96 heads; the estimate picks the faster
+// form on 19 of them, and the one miss costs 1.5 %):
+//   paired / key-split CTA: 4.0 + 1.35 per round in which both warpgroups
+//     compute + 1.0 per round in which one does; one CTA per SM;
+//   solo CTA: 3.0 + 1.2 per key step, two CTAs per SM, and no shorter than
+//     3.0 + 0.8 per step of the longest tile (a CTA alone on an SM).
+double list_schedule(const std::vector<double> &costs, int slots) {
+  std::priority_queue<double, std::vector<double>, std::greater<double>> free_at;
+  for (int i = 0; i < slots; ++i) free_at.push(0.0);
+  double end = 0.0;
+  for (double c : costs) {
+    const double t = free_at.top() + c;
+    free_at.pop();
+    free_at.push(t);
+    end = std::max(end, t);
+  }
+  return end;
+}
+
+bool key_split_pays(int n_qt, long long bh, int sms) {
+  // Beyond about four tiles per SM the forms differ only by per-CTA costs,
+  // which the key split doubles; 1 tile cannot be split.
+  if (n_qt < 2 || n_qt * bh > 4LL * sms || sms <= 0) return false;
+  struct Memo {
+    int n_qt;
+    long long bh;
+    int sms;
+    bool pays;
+  };
+  static thread_local Memo memo[8] = {};
+  static thread_local int memo_next = 0;
+  for (const Memo &m : memo)
+    if (m.n_qt == n_qt && m.bh == bh && m.sms == sms) return m.pays;
+
+  constexpr double kCta = 4.0, kDouble = 1.35, kSingle = 1.0;
+  constexpr double kSoloCta = 3.0, kSoloStep = 1.2, kSoloAlone = 0.8;
+  std::vector<double> costs;
+  costs.reserve(static_cast<size_t>(n_qt * bh));
+  for (int n = n_qt; n >= 1; --n)  // heaviest query tile first
+    for (long long h = 0; h < bh; ++h)
+      costs.push_back(kCta + kDouble * ((n + 1) / 2));
+  const double t_split = list_schedule(costs, sms);
+
+  const int n_pairs = (n_qt + 1) / 2;
+  const bool solo = n_qt <= kSoloMaxTiles && n_pairs * bh > sms;
+  double t_default;
+  costs.clear();
+  if (solo) {
+    for (int n = n_qt; n >= 1; --n)
+      for (long long h = 0; h < bh; ++h) costs.push_back(kSoloCta + kSoloStep * n);
+    t_default = std::max(kSoloCta + kSoloAlone * n_qt,
+                         list_schedule(costs, 2 * sms));
+  } else {
+    // paired: zig-zag pairs (p, n_qt - 1 - p) in one wave, else (2p, 2p+1)
+    // heaviest first; a pair's rounds are those of its longer tile
+    const bool zigzag = n_pairs * bh <= sms;
+    for (int p = n_pairs - 1; p >= 0; --p) {
+      int hi, lo;
+      if (zigzag) {
+        hi = n_qt - p;
+        lo = (p == n_qt - 1 - p) ? 0 : p + 1;
+      } else {
+        hi = std::min(2 * p + 2, n_qt);
+        lo = 2 * p + 1 < n_qt ? 2 * p + 1 : 0;
+      }
+      if (lo > hi) std::swap(lo, hi);
+      for (long long h = 0; h < bh; ++h)
+        costs.push_back(kCta + kDouble * lo + kSingle * (hi - lo));
+    }
+    std::sort(costs.begin(), costs.end(), std::greater<double>());
+    t_default = list_schedule(costs, sms);
+  }
+  const bool pays = t_split < t_default;
+  memo[memo_next] = {n_qt, bh, sms, pays};
+  memo_next = (memo_next + 1) % 8;
+  return pays;
+}
+
+}  // namespace prefill
+
+int prefill_form_of(long long BH, int N, bool causal, int sms,
+                    long long plan_bh, int *ctas) {
+  const int n_qt = (N + prefill::kBlockM - 1) / prefill::kBlockM;
+  const long long n_pairs = (n_qt + 1) / 2;
+  // Solo form (one query tile per CTA, two CTAs per SM) unless the paired
+  // grid fits one wave, where zig-zag pairs give every SM equal work, or
+  // the sequence is long enough that the pairs' shared K/V loads win.
+  int form = n_qt <= prefill::kSoloMaxTiles && (n_qt == 1 || n_pairs * BH > sms)
+                 ? FA_PREFILL_FORM_SOLO
+                 : FA_PREFILL_FORM_PAIRED;
+  // Key-split form (one query tile per CTA, its key tiles alternating
+  // between two softmax warpgroups) where the list-scheduling estimate
+  // (key_split_pays) says it finishes first: causal grids of about two
+  // query tiles per SM or fewer, where the longest query tile's chain of key
+  // steps, not the total work, sets the kernel time, and the split halves
+  // that chain. Its rounding differs from the other forms' (key tiles summed
+  // in another order), so the choice is made on the whole problem (plan_bh)
+  // when a caller launches it in chunks.
+  if (causal && prefill::key_split_pays(n_qt, plan_bh > 0 ? plan_bh : BH, sms))
+    form = FA_PREFILL_FORM_KEY_SPLIT;
+  // FA_PREFILL_FORM=paired|solo|split forces a form (measurement only).
+  static const char *force = getenv("FA_PREFILL_FORM");
+  if (force && *force) {
+    form = !strcmp(force, "split")  ? FA_PREFILL_FORM_KEY_SPLIT
+           : !strcmp(force, "solo") ? FA_PREFILL_FORM_SOLO
+                                    : FA_PREFILL_FORM_PAIRED;
+  }
+  if (ctas) *ctas = static_cast<int>(form == FA_PREFILL_FORM_PAIRED ? n_pairs * BH
+                                                                    : n_qt * BH);
+  return form;
+}
+
 const void *prefill_solo_kernel_ptr(int dtype) {
   using prefill::prefill_kernel;
   return dtype == FA_DTYPE_BF16
@@ -728,26 +847,9 @@ cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
   // One wave of CTAs: zig-zag pairs of equal causal work, so the kernel
   // does not wait on the heaviest pair. Several waves: heaviest first.
   const int zigzag = causal && grid <= static_cast<unsigned>(sms) ? 2 : 0;
-  // Solo form (one query tile per CTA, two CTAs per SM) unless the paired
-  // grid fits one wave, where zig-zag pairs give every SM equal work, or
-  // the sequence is long enough that the pairs' shared K/V loads win.
-  bool solo = n_qt <= prefill::kSoloMaxTiles &&
-              (n_qt == 1 || grid > static_cast<unsigned>(sms));
-  // Key-split form (one query tile per CTA, its key tiles alternating
-  // between two softmax warpgroups) for causal grids of at most two query
-  // tiles per SM: there the longest query tile's chain of key steps, not
-  // the total work, sets the kernel time, and the split halves that chain.
-  // Its rounding differs from the other forms' (key tiles summed in another
-  // order), so the rule is evaluated on the whole problem (plan_bh) when a
-  // caller launches it in chunks.
-  const long long form_bh = plan_bh > 0 ? plan_bh : BH;
-  bool split = causal && n_qt > 1 && n_qt * form_bh <= 2LL * sms;
-  // FA_PREFILL_FORM=paired|solo|split forces a form (measurement only).
-  static const char *force = getenv("FA_PREFILL_FORM");
-  if (force && *force) {
-    split = !strcmp(force, "split");
-    solo = !strcmp(force, "solo");
-  }
+  const int form = prefill_form_of(BH, N, causal, sms, plan_bh, nullptr);
+  const bool split = form == FA_PREFILL_FORM_KEY_SPLIT;
+  const bool solo = form == FA_PREFILL_FORM_SOLO;
   if (split) {
     using prefill::prefill_kernel;
     auto kernel = dtype == FA_DTYPE_BF16 ? prefill_kernel<BF16, false, true>

@@ -384,6 +384,19 @@ int fa_merge_partials(const float *partials, int G, void *o, int B, int H,
  */
 int fa_choose_decode_split(int max_seq, int batch, int heads, int min_blocks);
 
+/*
+ * CTA form the head_dim-64 prefill launches for bh (batch x head) pairs of
+ * n tokens on a device with `sms` SMs: one of FA_PREFILL_FORM_*; *ctas (if
+ * not NULL) receives the grid size; -1 for a non-positive argument. Pure
+ * host function. The reference's
+ * launch_prefill (csrc/prefill.cu:347-373) has a single form with grid
+ * (ceil(N/64), H, B); this reports which of the three B200 forms runs.
+ */
+#define FA_PREFILL_FORM_PAIRED 0    /* two query tiles of one head per CTA */
+#define FA_PREFILL_FORM_SOLO 1      /* one query tile per CTA, 2 CTAs/SM */
+#define FA_PREFILL_FORM_KEY_SPLIT 2 /* one query tile, key tiles split */
+int fa_prefill_form(long long bh, int n, int causal, int sms, int *ctas);
+
 /* One row of the occupancy report (reference csrc/flash_common.h:31-38). */
 typedef struct fa_occupancy_entry {
   char name[64];

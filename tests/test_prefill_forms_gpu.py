@@ -1,13 +1,14 @@
 """Prefill in all three CTA forms against fp32 attention. The key-split
 form (one query tile per CTA, its key tiles alternating between two
 softmax warpgroups whose partial rows merge at the end) runs causal grids
-of at most two query tiles per SM; the solo form (one query tile per CTA,
-two CTAs per SM) runs every other sequence of up to 48 query tiles whose
-paired grid exceeds one wave of SMs; the paired form (two tiles of one head
-per CTA) runs the rest: one-wave full grids (zig-zag pairs) and long
-sequences. Edges: short and ragged N, odd (batch, head) counts, grouped K/V
-heads, both dtypes, causal and full, and the sequence lengths on either
-side of the solo/paired switch."""
+of about two query tiles per SM or fewer; the solo form (one query tile
+per CTA, two CTAs per SM) runs every other sequence of up to 48 query tiles
+whose paired grid exceeds one wave of SMs; the paired form (two tiles of
+one head per CTA) runs the rest: one-wave grids (zig-zag pairs) and long
+sequences. flashattn_cuda._C._prefill_form reports the choice. Edges:
+short and ragged N, odd (batch, head) counts, grouped K/V heads, both
+dtypes, causal and full, and the sequence lengths on either side of each
+switch."""
 
 import pytest
 import torch
@@ -70,13 +71,14 @@ def test_short_prefill_d128_matches_fp32(dtype, tol, b, h, h_kv, n, causal):
     (1, 7, 4096),    # causal: 224 tiles, key-split; full: zig-zag pairs
     (1, 1, 129),     # causal key-split: warpgroup 1 holds only the diagonal
     (1, 3, 257),     # three key tiles: two on warpgroup 0, one on 1
-    (1, 9, 4096),    # causal: 288 tiles, key-split at the 2-per-SM limit
-    (1, 10, 4096),   # causal: 320 tiles, solo
+    (1, 10, 4096),   # causal: 320 tiles, still key-split; full: solo
+    (1, 14, 4096),   # causal: 448 tiles, solo
+    (1, 64, 512),    # causal: zig-zag pairs (a key split does not pay)
     (2, 7, 4096),    # 224 pairs: solo
-    (1, 2, 6144),    # 48 pairs on 148 SMs: one wave, paired
+    (1, 2, 6144),    # causal key-split; full: 48 pairs in one wave, paired
     (2, 4, 6144),    # 48 tiles, 192 pairs: solo
-    (2, 4, 6145),    # 49 tiles: paired
-    (1, 4, 16384),   # long: paired
+    (2, 4, 6145),    # 49 tiles: causal key-split, full paired
+    (1, 4, 16384),   # long: causal key-split, full paired
 ])
 @pytest.mark.parametrize("causal", [True, False])
 def test_form_switch_lengths_match_fp32(b, h, n, causal):
