@@ -27,6 +27,8 @@ CASES = {
     "prefill_c2_causal": ("prefill", (8, 12, 1024), True, None),
     "prefill_c2_full": ("prefill", (8, 12, 1024), False, None),
     "prefill_small": ("prefill", (1, 8, 2048), True, None),
+    # one GPU's share of config 3 on eight GPUs: key-split form
+    "prefill_c3_shard8": ("prefill", (1, 7, 4096), True, None),
     # two heads per CTA: one query tile each (N <= 128), and three tiles
     "prefill_pairs_n128": ("prefill", (64, 32, 128), True, None),
     "prefill_pairs_n384": ("prefill", (64, 32, 384), True, None),
