@@ -471,6 +471,29 @@ def run_ours(args, rank, world, local_rank):
             "scaling": scaling}
         del qd, kc, vc
 
+        # ------- one GPU's share of config 3 at 2 / 4 / 8 GPUs, timed alone:
+        # the per-rank kernel time a strong-scaling run is bounded by, with
+        # the CTA form each share runs in
+        if world == 1:
+            shares = {}
+            for w in (2, 4, 8):
+                hs = C3["B"] * C3["H"] // w
+                qs = randn(1, hs, C3["N"], HEAD_DIM, seed=95)
+                ks = randn(1, hs, C3["N"], HEAD_DIM, seed=96)
+                vs = randn(1, hs, C3["N"], HEAD_DIM, seed=97)
+                t = timer.run(lambda: fa.prefill(qs, ks, vs, True, SCALE),
+                              args.steps, args.warmup) / args.steps
+                launches += args.steps
+                fl = prefill_flops(1, hs, C3["N"], True)
+                shares[f"gpus{w}_b1_h{hs}"] = {
+                    "ms": round(t, 5),
+                    "tflops": round(fl / (t * 1e-3) / 1e12, 1),
+                    "form": fa._C._prefill_form(hs, C3["N"], True, sms)["form"]}
+                del qs, ks, vs
+            shares["note"] = ("causal N=4096 prefill of config 3's per-GPU head "
+                              "share on one GPU; the scaling run's per-rank time")
+            secondary["c3_prefill_per_gpu_share"] = shares
+
         # ------- grouped-query variants (Qwen2.5-0.5B really has 2 K/V heads):
         # same outputs as the pre-expanded configs without repeating K/V
         if world == 1:
