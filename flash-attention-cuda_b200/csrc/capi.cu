@@ -80,12 +80,14 @@ int ensure_device(int *device_out) {
                               decode_gqa_kernel_ptr(128, dt),
                               prefill_solo_kernel_ptr(dt),
                               prefill_d128_solo_kernel_ptr(dt),
-                              prefill_split_kernel_ptr(dt)};
+                              prefill_split_kernel_ptr(dt),
+                              prefill_d128_wide_kernel_ptr(dt)};
     const int bytes[] = {prefill_smem_bytes(), decode_smem_bytes(),
                          decode_d128_smem_bytes(), prefill_d128_smem_bytes(),
                          decode_gqa_smem_bytes(64), decode_gqa_smem_bytes(128),
                          prefill_solo_smem_bytes(), prefill_d128_solo_smem_bytes(),
-                         prefill_split_smem_bytes()};
+                         prefill_split_smem_bytes(),
+                         prefill_d128_wide_smem_bytes()};
     static_assert(sizeof(big_smem) / sizeof(big_smem[0]) ==
                       sizeof(bytes) / sizeof(bytes[0]),
                   "one shared-memory size per kernel");

@@ -20,6 +20,8 @@ const void *prefill_split_kernel_ptr(int dtype = FA_DTYPE_F16);
 int prefill_split_smem_bytes();
 const void *prefill_d128_solo_kernel_ptr(int dtype = FA_DTYPE_F16);
 int prefill_d128_solo_smem_bytes();
+const void *prefill_d128_wide_kernel_ptr(int dtype = FA_DTYPE_F16);
+int prefill_d128_wide_smem_bytes();
 int prefill_smem_bytes();
 cudaError_t launch_prefill_kernel(const CUtensorMap &tm_q,
                                   const CUtensorMap &tm_k,

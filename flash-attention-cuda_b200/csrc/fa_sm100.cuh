@@ -552,4 +552,67 @@ __device__ __forceinline__ void named_bar_arrive(uint32_t id, uint32_t nthreads)
   asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// ---------------------------------------------------------------------------
+// Softmax row helpers of the prefill kernels (one thread per 128-key S row).
+// ---------------------------------------------------------------------------
+// Bit i set: column pair i of every 8 takes its exponentials from the MUFU
+// unit, the others from the polynomial on the FMA pipe. Five of eight
+// balances the two pipes on the B200 (measured per-instruction costs: a warp
+// ex2 holds the MUFU pipe 8 cycles, a packed FMA 2, and a polynomial pair
+// costs about 18 FMA-pipe cycles against 16 MUFU cycles for a MUFU pair
+// plus 4 on the FMA pipe); the fp16 pack and the row max run on a third
+// pipe.
+constexpr unsigned kMufuMask8 = 0x3B;
+
+// Max of a 128-column S row: three-input max over 8 independent chains (one
+// 127-long dependent chain would leave the two softmax warps of an SM
+// sub-partition stalled on max latency).
+__device__ __forceinline__ float row_max_128(const float (&s)[128]) {
+  float mxp[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) mxp[i] = s[i];
+#pragma unroll
+  for (int c = 8; c + 16 <= 128; c += 16) {  // columns 8..119
+#pragma unroll
+    for (int i = 0; i < 8; ++i) mxp[i] = fmax3(mxp[i], s[c + i], s[c + 8 + i]);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) mxp[i] = fmaxf(mxp[i], s[120 + i]);
+  return fmax3(fmax3(mxp[0], mxp[1], mxp[2]), fmax3(mxp[3], mxp[4], mxp[5]),
+               fmaxf(mxp[6], mxp[7]));
+}
+
+// P = 2^(s * sl - m) for a 128-column row, packed to 16-bit pairs in pk;
+// returns the row sum of the fp32 P values. The exponentials alternate
+// between the MUFU unit (argument: one packed FMA per two columns) and the
+// polynomial on the FMA pipe (argument: one saturating FMA per column, which
+// also clamps it), so neither pipe bounds the step alone. The row sum uses
+// four packed accumulators.
+template <typename Dt>
+__device__ __forceinline__ float exp_row(const float (&s)[128], float sl,
+                                         float m, uint32_t (&pk)[2][32]) {
+  const float2 sl2 = make_float2(sl, sl);
+  const float2 nm2 = make_float2(-m, -m);
+  const float a = sl * (1.f / kExp2Span);
+  const float b = (-m - kExp2Lo) * (1.f / kExp2Span);
+  float2 rs[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) rs[i] = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int c = 0; c < 128; c += 2) {
+    float2 p;
+    if (!((kMufuMask8 >> ((c >> 1) & 7)) & 1)) {
+      p = exp2_poly2_affine(
+          make_float2(fma_sat(s[c], a, b), fma_sat(s[c + 1], a, b)));
+    } else {
+      const float2 x = ffma2(make_float2(s[c], s[c + 1]), sl2, nm2);
+      p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+    }
+    rs[(c >> 1) & 3] = fadd2(rs[(c >> 1) & 3], p);
+    pk[c >> 6][(c >> 1) & 31] = Dt::pack2(p.x, p.y);
+  }
+  const float2 r = fadd2(fadd2(rs[0], rs[1]), fadd2(rs[2], rs[3]));
+  return r.x + r.y;
+}
+
 }  // namespace fa

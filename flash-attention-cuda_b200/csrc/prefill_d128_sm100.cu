@@ -31,6 +31,9 @@
 #include <math.h>
 #include <stdint.h>
 
+#include <stdlib.h>
+#include <string.h>
+
 #include <algorithm>
 
 #include "fa_kernels.h"
@@ -565,6 +568,409 @@ __global__ void __launch_bounds__(Form<kSolo>::kThreads, Form<kSolo>::kCtasPerSm
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Wide form: 128-key tiles, P written over S.
+//
+// The form above keeps P in its own tensor-memory columns, which at head
+// dim 128 leaves room only for 64-key S tiles: each QK^T is an N=64 MMA
+// (shared-memory bound on the B200) and every 128 keys cost two rounds of
+// barriers, loads and waits. Here S_t takes 128 columns, O_t 128, and P_t
+// is stored as fp16 pairs over the first 64 columns of S_t once the softmax
+// warps hold S_t in registers:
+//   S0 / P0 [0,128)  S1 / P1 [128,256)  O0 [256,384)  O1 [384,512)
+// Since S_t(j+1) overwrites P_t(j), the MMA warp issues it only once
+// PV_t(j) has completed (its commit barrier); the other query tile's
+// softmax runs meanwhile, so the two tiles alternate between the softmax
+// warps and the tensor core. Shared memory: Q0, Q1 (2 x 32 KiB) and a
+// 2-slot ring of 128-key K and V tiles (4 x 32 KiB), each row as two
+// 128-byte-swizzled 64-dim halves (16 KiB blocks); the K/V boxes are the
+// 64-row boxes of the form above, two per half.
+// ---------------------------------------------------------------------------
+namespace wide {
+constexpr int kBlockN = 128;
+constexpr int kSlots = 2;
+constexpr uint32_t kKVHalf = kBlockN * kHalfBytes;  // 16 KiB
+constexpr uint32_t kKVTile = 2 * kKVHalf;           // 32 KiB
+constexpr uint32_t kQOff = 0;
+constexpr uint32_t kKOff = kQOff + kTilesPerCta * kQTile;
+constexpr uint32_t kVOff = kKOff + kSlots * kKVTile;
+constexpr uint32_t kBarOff = kVOff + kSlots * kKVTile;
+constexpr int kBarQFull = 0;
+constexpr int kBarKFull = kBarQFull + 1;          // + stage: K and V tile
+constexpr int kBarKVEmpty = kBarKFull + kSlots;   // + stage
+constexpr int kBarSFull = kBarKVEmpty + kSlots;   // + tile
+constexpr int kBarPFull = kBarSFull + kTilesPerCta;
+constexpr int kBarODone = kBarPFull + kTilesPerCta;
+constexpr int kBarDrain = kBarODone + kTilesPerCta;
+constexpr int kNumBars = kBarDrain + 1;
+constexpr uint32_t kTmemSlotOff = kBarOff + kNumBars * 8;
+constexpr uint32_t kAbortOff = kTmemSlotOff + 4;
+constexpr uint32_t kSmemBytes = kAbortOff + 4 + 8;
+static_assert(kSmemBytes + 1024 <= 228 * 1024,
+              "above the sm_100 per-CTA shared memory limit");
+constexpr uint32_t kTmemS = 0;    // + 128 * tile (P_t over its first 64)
+constexpr uint32_t kTmemO = 256;  // + 128 * tile
+
+template <typename Dt>
+constexpr uint32_t kIdescS = idesc_f16_f32(kBlockM, kBlockN, false, Dt::kFmt);
+
+// S = Q K^T for one 128x128 tile: 8 MMAs of K=16, steps 0-3 on the first
+// 64-dim half of Q and K, steps 4-7 on the second.
+template <typename Dt>
+__device__ __forceinline__ void issue_s_tile(uint32_t d, uint64_t q_desc,
+                                             uint64_t k_desc) {
+#pragma unroll
+  for (int kk = 0; kk < kD / 16; ++kk) {
+    const uint64_t off_q = (kk >> 2) * (kQHalf >> 4) + 2 * (kk & 3);
+    const uint64_t off_k = (kk >> 2) * (kKVHalf >> 4) + 2 * (kk & 3);
+    mma_f16_ss(d, q_desc + off_q, k_desc + off_k, kIdescS<Dt>, kk > 0 ? 1u : 0u);
+  }
+}
+
+// O (+)= P V for one tile: 8 MMAs of K=16 keys, N=128 head dims; V's two
+// 64-dim halves are kKVHalf bytes apart (the descriptor's leading byte
+// offset) and each step advances 16 rows (2048 bytes).
+template <typename Dt>
+__device__ __forceinline__ void issue_pv_tile(uint32_t d, uint32_t p_tmem,
+                                              uint64_t v_desc, bool accumulate) {
+#pragma unroll
+  for (int kk = 0; kk < kBlockN / 16; ++kk)
+    mma_f16_ts(d, p_tmem + 8 * kk, v_desc + 128 * kk, kIdescPV<Dt>,
+               (accumulate || kk > 0) ? 1u : 0u);
+}
+
+__device__ __forceinline__ TileInfo tile_info(int pair, int t, int N,
+                                              int causal, int zigzag) {
+  TileInfo ti;
+  const int n_qt = (N + kBlockM - 1) / kBlockM;
+  ti.qt = zigzag ? (t == 0 ? pair : n_qt - 1 - pair) : kTilesPerCta * pair + t;
+  if (ti.qt >= n_qt || (t == 1 && zigzag && ti.qt == pair)) {
+    ti.n_kv = 0;
+  } else {
+    ti.n_kv = causal ? ti.qt + 1 : (N + kBlockN - 1) / kBlockN;
+  }
+  return ti;
+}
+}  // namespace wide
+
+template <typename Dt>
+__global__ void __launch_bounds__(kThreads, 1)
+    prefill_d128_wide_kernel(const __grid_constant__ CUtensorMap tm_q,
+                             const __grid_constant__ CUtensorMap tm_k,
+                             const __grid_constant__ CUtensorMap tm_v,
+                             __half *__restrict__ out, int N, int BH,
+                             int causal, float scale_log2, int H, int group,
+                             int head_block) {
+  static_assert(kBlockM == wide::kBlockN, "causal tile skipping assumes square tiles");
+  extern __shared__ __align__(1024) uint8_t smem[];
+  constexpr int kStages = wide::kSlots;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // bit 0: causal; bit 1: zig-zag query-tile pairing
+  const int zigzag = causal >> 1;
+  causal &= 1;
+  if (smem_u32(smem) & 1023u) {
+    if (threadIdx.x == 0) record_error(FA_ERR_SMEM_ALIGN);
+    return;
+  }
+
+  // Heaviest pairs first, heads fastest, within blocks of head_block heads
+  // (0: all heads) whose K/V fit in L2.
+  const int n_qt = (N + kBlockM - 1) / kBlockM;
+  const int n_pairs = (n_qt + kTilesPerCta - 1) / kTilesPerCta;
+  const int hb = head_block > 0 ? head_block : BH;
+  const int blk = static_cast<int>(blockIdx.x) / (hb * n_pairs);
+  const int r = static_cast<int>(blockIdx.x) % (hb * n_pairs);
+  const int h0 = blk * hb;
+  const int h_here = min(hb, BH - h0);
+  const int h_div = h_here > 0 ? h_here : 1;
+  const int pair = n_pairs - 1 - r / h_div;
+  const int bh = h0 + r % h_div;
+  if (h_here <= 0 || bh >= BH) return;
+  const int kv_bh = (bh / H) * (H / group) + (bh % H) / group;
+  const TileInfo t0 = wide::tile_info(pair, 0, N, causal, zigzag);
+  const TileInfo t1 = wide::tile_info(pair, 1, N, causal, zigzag);
+  const int n_kv = t0.n_kv > t1.n_kv ? t0.n_kv : t1.n_kv;
+
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + wide::kBarOff);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + wide::kTmemSlotOff);
+  volatile uint32_t *abort_flag =
+      reinterpret_cast<volatile uint32_t *>(smem + wide::kAbortOff);
+
+  // Key tile p goes to ring stage p % kStages: per 64-dim half, two boxes
+  // of 64 rows for K and two for V.
+  auto load_pos = [&](int p) {
+    const int s = p % kStages;
+    mbar_arrive_expect_tx(&bars[wide::kBarKFull + s], 2 * wide::kKVTile);
+    for (int h = 0; h < 2; ++h) {
+      for (int rb = 0; rb < 2; ++rb) {
+        const uint32_t off = s * wide::kKVTile + h * wide::kKVHalf + rb * (wide::kKVHalf / 2);
+        tma_load_3d(smem + wide::kKOff + off, &tm_k, &bars[wide::kBarKFull + s], 64 * h,
+                    p * wide::kBlockN + 64 * rb, kv_bh);
+        tma_load_3d(smem + wide::kVOff + off, &tm_v, &bars[wide::kBarKFull + s], 64 * h,
+                    p * wide::kBlockN + 64 * rb, kv_bh);
+      }
+    }
+  };
+
+  int preissued = 0;
+  if (warp == kProducerWarp && lane == 0) {
+    mbar_init(&bars[wide::kBarQFull], 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars[wide::kBarKFull + s], 1);
+      mbar_init(&bars[wide::kBarKVEmpty + s], 1);
+    }
+    for (int t = 0; t < kTilesPerCta; ++t) {
+      mbar_init(&bars[wide::kBarSFull + t], 1);
+      mbar_init(&bars[wide::kBarPFull + t], kSoftmaxThreads);
+      mbar_init(&bars[wide::kBarODone + t], 1);
+    }
+    mbar_init(&bars[wide::kBarDrain], 1);
+    fence_barrier_init();
+    prefetch_tensormap(&tm_q);
+    prefetch_tensormap(&tm_k);
+    prefetch_tensormap(&tm_v);
+    const bool two = t1.n_kv > 0;
+    mbar_arrive_expect_tx(&bars[wide::kBarQFull], (two ? 2 : 1) * kQTile);
+    for (int t = 0; t < (two ? 2 : 1); ++t) {
+      const int row0 = (t == 0 ? t0.qt : t1.qt) * kBlockM;
+      for (int h = 0; h < 2; ++h)
+        tma_load_3d(smem + wide::kQOff + t * kQTile + h * kQHalf, &tm_q,
+                    &bars[wide::kBarQFull], 64 * h, row0, bh);
+    }
+    for (; preissued < n_kv && preissued < kStages; ++preissued)
+      load_pos(preissued);
+    *abort_flag = device_failed() ? 1u : 0u;
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t sbase = smem_u32(smem);
+
+  if (warp >= 8) {
+    setmaxnreg_dec<kCtrlRegs>();
+    if (warp == kProducerWarp) {
+      // ---------------------------------------------------------------- TMA
+      if (lane == 0) {
+        int issued = preissued;
+        for (int p = preissued; p < n_kv; ++p) {
+          if (*abort_flag) break;
+          const int s = p % kStages;
+          const int use = p / kStages;
+          if (use > 0 && !mbar_wait(&bars[wide::kBarKVEmpty + s], (use - 1) & 1)) {
+            *abort_flag = 1;
+            break;
+          }
+          load_pos(p);
+          issued = p + 1;
+        }
+        // no copy of ours may still be landing when the CTA exits
+        if (*abort_flag) {
+          mbar_wait(&bars[wide::kBarQFull], 0);
+          for (int p = (issued > kStages ? issued - kStages : 0); p < issued; ++p)
+            mbar_wait(&bars[wide::kBarKFull + p % kStages], (p / kStages) & 1);
+        }
+      }
+    } else if (warp == kMmaWarp) {
+      // ---------------------------------------------------------------- MMA
+      const bool leader = elect_one();
+      const uint32_t tmem = __shfl_sync(0xffffffffu, tmem_base, 0);
+      const int n_t[2] = {t0.n_kv, t1.n_kv};
+      const uint64_t desc0 = sw128_desc(sbase);
+      const uint64_t vdesc0 = sw128_desc_lbo(sbase, wide::kKVHalf);
+      bool ok = mbar_wait(&bars[wide::kBarQFull], 0) &&
+                mbar_wait(&bars[wide::kBarKFull + 0], 0);
+      if (ok) {
+        tc_fence_after();
+        if (leader) {
+          for (int t = 0; t < kTilesPerCta; ++t) {
+            if (n_t[t] == 0) continue;
+            wide::issue_s_tile<Dt>(tmem + wide::kTmemS + 128 * t,
+                                   desc0 + ((wide::kQOff + t * kQTile) >> 4),
+                                   desc0 + (wide::kKOff >> 4));
+            mma_commit(&bars[wide::kBarSFull + t]);
+          }
+        }
+        __syncwarp();
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        if (*abort_flag) {
+          ok = false;
+          break;
+        }
+        const int s = j % kStages;  // K_j, V_j
+#pragma unroll
+        for (int t = 0; t < kTilesPerCta; ++t) {
+          const int nt = n_t[t];
+          if (!ok || j >= nt) continue;
+          if (!mbar_wait(&bars[wide::kBarPFull + t], j & 1)) {
+            ok = false;
+            continue;
+          }
+          tc_fence_after();
+          if (leader) {
+            wide::issue_pv_tile<Dt>(tmem + wide::kTmemO + 128 * t,
+                                    tmem + wide::kTmemS + 128 * t,
+                                    vdesc0 + ((wide::kVOff + s * wide::kKVTile) >> 4), j > 0);
+            mma_commit(&bars[wide::kBarODone + t]);
+            // the round's last PV releases its ring stage
+            if (t == 1 || n_t[1] <= j) mma_commit(&bars[wide::kBarKVEmpty + s]);
+          }
+          __syncwarp();
+          if (j + 1 < nt) {
+            // S_t(j+1) overwrites P_t(j): wait for PV_t(j) to complete.
+            // K/V tile j+1 is waited on by its first user.
+            const int p1 = j + 1;
+            const bool need_kv = (t == 0) || (n_t[0] <= j + 1);
+            if ((need_kv &&
+                 !mbar_wait(&bars[wide::kBarKFull + p1 % kStages], (p1 / kStages) & 1)) ||
+                !mbar_wait(&bars[wide::kBarODone + t], j & 1)) {
+              ok = false;
+              continue;
+            }
+            tc_fence_after();
+            if (leader) {
+              wide::issue_s_tile<Dt>(tmem + wide::kTmemS + 128 * t,
+                                     desc0 + ((wide::kQOff + t * kQTile) >> 4),
+                                     desc0 + ((wide::kKOff + (p1 % kStages) * wide::kKVTile) >> 4));
+              mma_commit(&bars[wide::kBarSFull + t]);
+            }
+            __syncwarp();
+          }
+        }
+      }
+      if (!ok && leader) *abort_flag = 1;
+      if (leader) mma_commit(&bars[wide::kBarDrain]);
+      __syncwarp();
+      mbar_wait(&bars[wide::kBarDrain], 0);
+    }
+  } else {
+    setmaxnreg_inc<kSoftmaxRegs>();
+    // -------------------------------------------------------------- softmax
+    const int t = warp >> 2;
+    const int row = threadIdx.x & 127;
+    const TileInfo ti = t == 0 ? t0 : t1;
+    const uint32_t lane_addr = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem_base + lane_addr + wide::kTmemS + 128 * t;
+    const uint32_t tO = tmem_base + lane_addr + wide::kTmemO + 128 * t;
+    uint64_t *s_full = &bars[wide::kBarSFull + t];
+    uint64_t *p_full = &bars[wide::kBarPFull + t];
+    uint64_t *o_done = &bars[wide::kBarODone + t];
+    const int q_row = ti.qt * kBlockM + row;
+    float m_use = -INFINITY;
+    float l_sum = 0.f;
+    bool ok = true;
+
+    for (int j = 0; j < ti.n_kv; ++j) {
+      if (*abort_flag || !mbar_wait(s_full, j & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sr[4][32];
+      tmem_ld32(tS + 0, sr[0]);
+      tmem_ld32(tS + 32, sr[1]);
+      tmem_ld32(tS + 64, sr[2]);
+      tmem_ld32(tS + 96, sr[3]);
+      tmem_wait_ld();
+
+      float s[128];
+#pragma unroll
+      for (int c = 0; c < 128; ++c) s[c] = __uint_as_float(sr[c >> 5][c & 31]);
+      float sl = scale_log2;
+      if (scale_log2 <= 0.f) {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) s[c] *= scale_log2;
+        sl = 1.f;
+      }
+      const int kbase = j * wide::kBlockN;
+      const bool diag = causal && (j == ti.qt);
+      if (diag || kbase + wide::kBlockN > N) {
+        int lim = N - kbase;
+        if (diag) lim = min(lim, row + 1);
+#pragma unroll
+        for (int c = 0; c < 128; ++c) s[c] = (c < lim) ? s[c] : -INFINITY;
+      }
+      float corr = 1.f;
+      bool rescale = false;
+      const float m_tile = row_max_128(s) * sl;
+      if (m_tile > m_use + prefill128::kRescaleThreshold) {
+        corr = fast_exp2(m_use - m_tile);  // 0 on the first tile
+        m_use = m_tile;
+        rescale = true;
+      }
+      uint32_t pk[2][32];
+      const float rowsum = exp_row<Dt>(s, sl, m_use, pk);
+      l_sum = fmaf(l_sum, corr, rowsum);
+      // PV_t(j-1) has completed: S_t(j) was issued after it.
+      if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+        for (int h = 0; h < kD / 32; ++h) {
+          uint32_t o[32];
+          tmem_ld32(tO + 32 * h, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; ++c)
+            o[c] = __float_as_uint(__uint_as_float(o[c]) * corr);
+          tmem_st32(tO + 32 * h, o);
+        }
+      }
+      tmem_st32(tS, pk[0]);  // P_t over the first 64 columns of S_t
+      tmem_st32(tS + 32, pk[1]);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+
+    if (ti.n_kv > 0) {
+      if (ok && mbar_wait(o_done, (ti.n_kv - 1) & 1)) {
+        tc_fence_after();
+        const float inv_l = (l_sum > 0.f) ? 1.f / l_sum : 0.f;
+        uint4 *dst = reinterpret_cast<uint4 *>(
+            out + (static_cast<size_t>(bh) * N + q_row) * kD);
+#pragma unroll
+        for (int h = 0; h < kD / 32; ++h) {
+          uint32_t o[32];
+          tmem_ld32(tO + 32 * h, o);
+          tmem_wait_ld();
+          if (q_row < N) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const uint32_t *src = &o[c * 8];
+              uint4 v;
+              v.x = Dt::pack2(__uint_as_float(src[0]) * inv_l,
+                               __uint_as_float(src[1]) * inv_l);
+              v.y = Dt::pack2(__uint_as_float(src[2]) * inv_l,
+                               __uint_as_float(src[3]) * inv_l);
+              v.z = Dt::pack2(__uint_as_float(src[4]) * inv_l,
+                               __uint_as_float(src[5]) * inv_l);
+              v.w = Dt::pack2(__uint_as_float(src[6]) * inv_l,
+                               __uint_as_float(src[7]) * inv_l);
+              dst[4 * h + c] = v;
+            }
+          }
+        }
+      } else {
+        *abort_flag = 1;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
 }  // namespace prefill128
 
 const void *prefill_d128_kernel_ptr(int dtype) {
@@ -585,6 +991,15 @@ int prefill_d128_solo_smem_bytes() {
 }
 int prefill_d128_smem_bytes() {
   return static_cast<int>(prefill128::kSmemBytes);
+}
+const void *prefill_d128_wide_kernel_ptr(int dtype) {
+  using prefill128::prefill_d128_wide_kernel;
+  return dtype == FA_DTYPE_BF16
+             ? reinterpret_cast<const void *>(prefill_d128_wide_kernel<BF16>)
+             : reinterpret_cast<const void *>(prefill_d128_wide_kernel<F16>);
+}
+int prefill_d128_wide_smem_bytes() {
+  return static_cast<int>(prefill128::wide::kSmemBytes);
 }
 
 cudaError_t launch_prefill_d128_kernel(const CUtensorMap &tm_q,
@@ -619,6 +1034,13 @@ cudaError_t launch_prefill_d128_kernel(const CUtensorMap &tm_q,
         H / H_kv, 0);
     return cudaGetLastError();
   }
+  // Wide form (128-key tiles, P over S) for every multi-tile grid:
+  // measured against the 64-key paired form (µs, L2 flushed): config 3's
+  // shape causal 216 vs 238, full 434 vs 484, B1 H8 N8192 causal 118 vs
+  // 135, B8 H12 N2048 causal 119 vs 127, B1 H14 N4096 causal 66 vs 74.
+  // FA_PREFILL_D128_FORM=paired selects the 64-key form (measurement only).
+  static const char *force = getenv("FA_PREFILL_D128_FORM");
+  const bool wide = !(force && !strcmp(force, "paired"));
   auto kernel = dtype == FA_DTYPE_BF16 ? prefill128::prefill_d128_kernel<BF16>
                                        : prefill128::prefill_d128_kernel<F16>;
   // Blocks of heads whose K/V (both tensors, all N rows) fit in about
@@ -634,6 +1056,16 @@ cudaError_t launch_prefill_d128_kernel(const CUtensorMap &tm_q,
       const int blocks = (BH + fit - 1) / fit;
       head_block = (BH + blocks - 1) / blocks;
     }
+  }
+  if (wide) {
+    auto wkernel = dtype == FA_DTYPE_BF16
+                       ? prefill128::prefill_d128_wide_kernel<BF16>
+                       : prefill128::prefill_d128_wide_kernel<F16>;
+    wkernel<<<grid, prefill128::kThreads, prefill128::wide::kSmemBytes,
+              stream>>>(tm_q, tm_k, tm_v, out, N, BH,
+                        (causal ? 1 : 0) | zigzag, scale_log2, H, H / H_kv,
+                        head_block);
+    return cudaGetLastError();
   }
   kernel<<<grid, prefill128::kThreads, prefill128::kSmemBytes, stream>>>(
       tm_q, tm_k, tm_v, out, N, BH, (causal ? 1 : 0) | zigzag, scale_log2, H,
