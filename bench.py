@@ -604,6 +604,10 @@ def run_ours(args, rank, world, local_rank):
         if world == 1 and not args.no_library:
             secondary["cudnn_sdpa_c3"] = cudnn_measure(
                 timer, randn, args.steps, args.warmup, value)
+            d128 = secondary.get("c3_prefill_d128", {}).get("tflops")
+            if d128:
+                secondary["cudnn_sdpa_c3_d128"] = cudnn_measure(
+                    timer, randn, args.steps, args.warmup, d128, d=128)
 
         # ------- the reference's published sweep shapes, libraries beside ---
         if world == 1 and not args.no_library:
@@ -870,27 +874,30 @@ def published_shapes(fa, timer, randn, steps, warmup):
     return out
 
 
-def cudnn_measure(timer, randn, steps, warmup, ours_tflops):
-    """Config 3 through torch SDPA restricted to the cuDNN backend, with the
-    same inputs shape, L2 flush and timing as the headline line."""
+def cudnn_measure(timer, randn, steps, warmup, ours_tflops, d=HEAD_DIM):
+    """Config 3 (at head_dim d) through torch SDPA restricted to the cuDNN
+    backend, with the same inputs shape, L2 flush and timing as ours."""
     import torch
     try:
         from torch.nn.attention import SDPBackend, sdpa_kernel
-        q = randn(C3["B"], C3["H"], C3["N"], HEAD_DIM, seed=1000)
-        k = randn(C3["B"], C3["H"], C3["N"], HEAD_DIM, seed=2000)
-        v = randn(C3["B"], C3["H"], C3["N"], HEAD_DIM, seed=3000)
+        q = randn(C3["B"], C3["H"], C3["N"], d, seed=1000)
+        k = randn(C3["B"], C3["H"], C3["N"], d, seed=2000)
+        v = randn(C3["B"], C3["H"], C3["N"], d, seed=3000)
+        scale = d ** -0.5
 
         def step():
             with sdpa_kernel(SDPBackend.CUDNN_ATTENTION):
                 torch.nn.functional.scaled_dot_product_attention(
-                    q, k, v, is_causal=True, scale=SCALE)
+                    q, k, v, is_causal=True, scale=scale)
 
         ms = timer.run(step, steps, warmup) / steps
-        tf = prefill_flops(C3["B"], C3["H"], C3["N"], True) / (ms * 1e-3) / 1e12
+        tf = (prefill_flops(C3["B"], C3["H"], C3["N"], True) * d / HEAD_DIM
+              / (ms * 1e-3) / 1e12)
         return {"ms": round(ms, 5), "tflops": round(tf, 2),
                 "ours_over_cudnn": round(ours_tflops / tf, 3),
                 "note": "cuDNN fused attention (torch SDPA, CUDNN_ATTENTION "
-                        "backend) on config 3: library kernel, context only"}
+                        f"backend) on config 3 at head_dim {d}: library "
+                        "kernel, context only"}
     except Exception as exc:  # library missing or backend refused the shape
         return {"unavailable": f"{type(exc).__name__}: {str(exc)[:120]}"}
 
