@@ -187,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   StageHeader *hdr = reinterpret_cast<StageHeader *>(smem + kHdrOff);
   uint64_t *red_full = empty + kStages;
   uint64_t *red_empty = red_full + kRedBufs;
-  if (device_failed()) return;
+  // (the device error word is read by the producer: decode::produce())
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {

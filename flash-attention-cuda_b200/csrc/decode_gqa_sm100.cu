@@ -582,7 +582,7 @@ __global__ void __launch_bounds__(GqaCfg<D>::kThreads, 1)
   uint64_t *red_full = empty + C::kStages;
   uint64_t *red_empty = red_full + kRedBufs;
   StageHeader *hdr = reinterpret_cast<StageHeader *>(smem + C::kHdrOff);
-  if (device_failed()) return;
+  // (the device error word is read by the producer: produce())
   if (smem_u32(smem) & 1023u) {  // the swizzled stages need 1 KiB alignment
     if (threadIdx.x == 0) record_error(FA_ERR_SMEM_ALIGN);
     return;

@@ -404,6 +404,7 @@ __device__ void merger(const DecodeArgs &a, uint8_t *red_base,
     }
     last = __shfl_sync(0xffffffffu, last, 0);
     if (!last) continue;
+    if (lane == 0) FA_TRACE_CTA(5);
     __threadfence();
     // every partial of the segment is in place: merge them
     // (m, l) of up to 32 partials per lane round; with at most 32 partials
@@ -482,6 +483,12 @@ __device__ void produce(const DecodeArgs &a, int nseg, int seg_per_plane,
                         uint64_t *full, uint64_t *empty, StageHeader *hdr,
                         const CUtensorMap *tm_k, const CUtensorMap *tm_v) {
   const int lane = threadIdx.x & 31;
+  // A kernel that gave up on a bounded wait earlier (device error word)
+  // leaves this CTA with nothing to stream: the end marker goes out at once
+  // and every role exits through its normal path. The word is read here,
+  // beside the first sequence lengths, so the two global round trips
+  // overlap instead of one gating the CTA's start.
+  const bool failed = device_failed();
     // ------------------------------------------------------------ planning
     long long sum_len = 0;
     int max_len = 0;
@@ -495,7 +502,7 @@ __device__ void produce(const DecodeArgs &a, int nseg, int seg_per_plane,
           0xffffffffu, b < a.B && len == 0 &&
                            (b % static_cast<int>(gridDim.x)) ==
                                static_cast<int>(blockIdx.x));
-      while (todo && (kD == kHeadDim || a.x_peers)) {
+      while (todo && !failed && (kD == kHeadDim || a.x_peers)) {
         const int i = __ffs(todo) - 1;
         todo &= todo - 1;
         if (a.x_peers) {
@@ -559,12 +566,13 @@ __device__ void produce(const DecodeArgs &a, int nseg, int seg_per_plane,
 
     // ------------------------------------------------------------ streaming
     if (lane == 0) {
+      if (kNumStages == kStages) FA_TRACE_CTA(2);
       const uint64_t policy = l2_policy_evict_first();
       int it = 0;
       bool ok = true;
       long long cur = start;
       int b = b_start;
-      while (ok && cur < end && b < a.B) {
+      while (ok && !failed && cur < end && b < a.B) {
         const int len = seq_rows(a, b);
         if (len == 0) {
           ++b;
@@ -643,7 +651,7 @@ __device__ void produce(const DecodeArgs &a, int nseg, int seg_per_plane,
     }
     // Sharded: the rows of this CTA's empty sequences come from other
     // ranks; merge them now that this CTA's own stream is issued.
-    if (a.x_peers) {
+    if (a.x_peers && !failed) {
       __syncwarp();
       for (int chunk = 0; chunk < a.B; chunk += 32) {
         const int b = chunk + lane;
@@ -672,7 +680,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   StageHeader *hdr = reinterpret_cast<StageHeader *>(smem + kHdrOff);
   uint64_t *red_full = empty + kStages;
   uint64_t *red_empty = red_full + kRedBufs;
-  if (device_failed()) return;
+  if (threadIdx.x == 0) FA_TRACE_CTA(0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -686,6 +694,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     fence_barrier_init();
   }
   __syncthreads();
+  if (threadIdx.x == 0) FA_TRACE_CTA(1);
 
   if (warp == kProducerWarp) {
     produce<false, kStages>(a, a.H, a.H / a.H_kv, smem, kKOff, kVOff, full,
@@ -695,6 +704,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 
   if (warp == kMergerWarp) {
     merger(a, smem + kRedOff, red_full, red_empty);
+    if (lane == 0) FA_TRACE_CTA(7);
     return;
   }
 
@@ -714,8 +724,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   for (int it = 0;; ++it) {
     const int slot = it % kStages;
     if (!mbar_wait(&full[slot], (it / kStages) & 1)) break;
+    if (it == 0 && threadIdx.x == 0) FA_TRACE_CTA(3);
     const StageHeader hd = hdr[slot];
     if (hd.flags & kDone) {
+      if (threadIdx.x == 0) FA_TRACE_CTA(4);
       // tell the merger warp there is nothing more (same hand-off protocol)
       const int buf = piece & 1;
       if (piece >= kRedBufs &&

@@ -60,9 +60,17 @@ __device__ unsigned long long g_fa_trace[4 * 4096];
   do {                                                                 \
     if (blockIdx.x < 4) g_fa_trace[blockIdx.x * 4096 + (slot)] = clock64(); \
   } while (0)
+// Per-CTA global-timer stamps (8 slots per CTA, up to 2048 CTAs).
+#define FA_TRACE_CTA(slot)                                               \
+  do {                                                                   \
+    if (blockIdx.x < 2048) g_fa_trace[blockIdx.x * 8 + (slot)] = global_timer_ns(); \
+  } while (0)
 #else
 #define FA_TRACE_EVENT(slot) \
   do {                       \
+  } while (0)
+#define FA_TRACE_CTA(slot) \
+  do {                     \
   } while (0)
 #endif
 
